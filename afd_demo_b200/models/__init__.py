@@ -1,0 +1,13 @@
+from .attention import AttentionWorker
+from .disaggregated import DisaggregatedQwenModel
+from .ffn import FFNWorker
+from .kv_cache import KVCache
+from .weights import (AttentionWeights, FFNWeights, load_attention_weights, load_ffn_weights,
+                      random_attention_weights, random_ffn_weights, save_checkpoint,
+                      write_random_checkpoint)
+
+__all__ = [
+    "AttentionWorker", "DisaggregatedQwenModel", "FFNWorker", "KVCache", "AttentionWeights",
+    "FFNWeights", "load_attention_weights", "load_ffn_weights", "random_attention_weights",
+    "random_ffn_weights", "save_checkpoint", "write_random_checkpoint",
+]

@@ -1,0 +1,91 @@
+"""Attention role: embedding, per-layer attention block, KV cache, final norm,
+LM head.
+
+Reference: ``AttentionLayer`` / ``AttentionWorker``
+(src/model/attention_worker.py:24-313), which wrap HF ``Qwen3MoeAttention`` and
+shard layers over the role's visible GPUs. Here one B200 holds every layer
+(≈3.6 GB of attention weights in bf16), and a layer is five ops:
+
+1. ``sum_rmsnorm``   x = sum of the F2A partials (one per FFN rank), RMSNorm
+2. ``linear``        qkv = x_n @ W_qkv^T (tcgen05 GEMM)
+3. ``qk_norm_rope_cache``  per-head q/k RMSNorm, RoPE, K/V append in place
+4. ``attention``     flash decode (q_len 1) or causal flash prefill
+5. ``linear``        h = o @ W_o^T + x  -- the A2F hand-off: with a fused
+   transport the epilogue stores h straight into the FFN GPUs' receive
+   buffers and raises their flags.
+
+``forward_attention_layer`` returns h = attn_out + residual, the
+"pre-combined" tensor the reference ships to the FFN
+(src/model/disaggregated.py:184).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from .kv_cache import KVCache
+from .weights import AttentionWeights
+
+
+class AttentionWorker:
+    def __init__(self, cfg: ModelConfig, weights: AttentionWeights, device, dtype=torch.bfloat16,
+                 max_batch: int = 4, max_seq: int = 2048):
+        self.cfg = cfg
+        self.w = weights
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.num_layers = cfg.num_hidden_layers
+        self.rope = ops.rope_table(max_seq, cfg.head_dim, cfg.rope_theta, self.device)
+        self.cache = KVCache(cfg.num_hidden_layers, max_batch, cfg.num_key_value_heads, max_seq,
+                             cfg.head_dim, self.device, dtype)
+        self.tracker = None  # optional TimingTracker for sub-stage events
+
+    # ------------------------------------------------------------------
+    def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """[B, S] ids -> [B*S, H] hidden states."""
+        return torch.nn.functional.embedding(input_ids.reshape(-1), self.w.embed)
+
+    def get_position_embeddings(self, position_ids: torch.Tensor):
+        """(cos, sin) [B, S, D] for code written against the HF signature."""
+        D = self.cfg.head_dim
+        cs = self.rope[position_ids.long()]
+        cos = torch.cat([cs[..., : D // 2]] * 2, -1).to(self.dtype)
+        sin = torch.cat([cs[..., D // 2:]] * 2, -1).to(self.dtype)
+        return cos, sin
+
+    def forward_attention_layer(self, layer_idx: int, x_parts: Sequence[torch.Tensor],
+                                batch_offset: int, q_len: int, start_pos: Optional[int] = None,
+                                sink=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One attention block for the micro-batch whose sequences occupy cache
+        rows [batch_offset, batch_offset + T // q_len). `x_parts` are the
+        layer inputs (the F2A partials); returns h = x + o_proj(attn)."""
+        cfg = self.cfg
+        lw = self.w.layers[layer_idx]
+        start = self.cache.seq_len if start_pos is None else start_pos
+        x, xn = ops.sum_rmsnorm(list(x_parts), lw.in_norm, cfg.rms_norm_eps)
+        qkv = ops.linear(xn, lw.w_qkv)
+        k_l, v_l = self.cache.layer(layer_idx)
+        q = ops.qk_norm_rope_cache(qkv, lw.q_norm, lw.k_norm, self.rope, k_l, v_l, start,
+                                   self.cache.pos_dev, q_len, batch_offset,
+                                   cfg.num_attention_heads, cfg.num_key_value_heads,
+                                   cfg.rms_norm_eps)
+        o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev)
+        if sink is not None:
+            return ops.linear(o, lw.w_o, residual=x, out=out, **sink.gemm_kwargs())
+        return ops.linear(o, lw.w_o, residual=x, out=out)
+
+    def forward_lm_head(self, x_parts: Sequence[torch.Tensor], q_len: int = 1,
+                        last_only: bool = True) -> torch.Tensor:
+        """Final RMSNorm + LM head. With `last_only`, only the last position of
+        each sequence is projected (that is all sampling needs); returns
+        [B, V] (or [T, V])."""
+        H = self.cfg.hidden_size
+        parts = [p.reshape(-1, H) for p in x_parts]
+        if last_only and q_len > 1:
+            parts = [p.view(-1, q_len, H)[:, -1].contiguous() for p in parts]
+        _, xn = ops.sum_rmsnorm(parts, self.w.final_norm, self.cfg.rms_norm_eps)
+        return ops.linear(xn, self.w.lm_head)

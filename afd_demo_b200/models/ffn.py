@@ -1,0 +1,77 @@
+"""FFN role: post-attention RMSNorm, router, and the (expert-parallel slice
+of the) MoE experts.
+
+Reference: ``FFNLayer`` / ``FFNWorker`` (src/model/ffn_worker.py:31-225), which
+run HF ``Qwen3MoeSparseMoeBlock`` -- a Python loop over the experts hit. Here
+one layer is a fixed sequence of kernels independent of routing:
+
+1. RMSNorm + router GEMM + fp32 softmax/top-k/renormalise
+2. routing: per-expert row counts, expert-sorted rows, row blocks
+3. gather of the normalised tokens into expert order
+4. grouped tcgen05 GEMM  gate_up, SwiGLU epilogue
+5. grouped tcgen05 GEMM  down, routing-weight epilogue
+6. combine: per-token sum of its expert rows (+ residual), stored locally or
+   -- with a fused transport -- straight into the attention GPUs' buffers
+   with a release flag (the F2A return).
+
+Under expert parallelism every FFN rank sees all tokens of the micro-batch and
+contributes the partial sum of its local experts; FFN rank 0 also adds the
+residual, so the attention side's sum over FFN ranks is the layer output.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..utils.timing import EventType
+from .weights import FFNWeights
+
+
+class FFNWorker:
+    def __init__(self, cfg: ModelConfig, weights: FFNWeights, device, dtype=torch.bfloat16):
+        self.cfg = cfg
+        self.w = weights
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.num_layers = cfg.num_hidden_layers
+        self.expert_range = weights.expert_range
+        self.supports_moe_timing = cfg.is_moe
+        self.tracker = None  # optional TimingTracker for router / experts spans
+
+    def _mark(self, start: bool, et: EventType, l: int, mb: int):
+        if self.tracker is not None:
+            (self.tracker.mark_start if start else self.tracker.mark_end)(et, l, mb)
+
+    def forward_ffn_layer(self, layer_idx: int, hidden_states: torch.Tensor,
+                          add_residual: bool = True, sink=None, out: Optional[torch.Tensor] = None,
+                          mb_idx: int = 0) -> torch.Tensor:
+        """h [T, H] (= attn_out + residual) -> h + moe(norm(h)) [T, H], or only
+        the local experts' partial sum when `add_residual` is False."""
+        cfg = self.cfg
+        lw = self.w.layers[layer_idx]
+        H = cfg.hidden_size
+        h = hidden_states.reshape(-1, H)
+        residual = h if add_residual else None
+        kw = sink.combine_kwargs() if sink is not None else {}
+        if lw.w_router is None:  # dense MLP layer (mlp_only_layers)
+            if sink is not None:
+                raise NotImplementedError("the fused F2A store covers MoE layers only; "
+                                          "use --comm-impl nccl for models with dense layers")
+            self._mark(True, EventType.MOE_SHARED_OR_DENSE, layer_idx, mb_idx)
+            xn = ops.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps)
+            y = ops.dense_mlp(xn, lw.w_dense_gate_up, lw.w_dense_down, residual=residual)
+            self._mark(False, EventType.MOE_SHARED_OR_DENSE, layer_idx, mb_idx)
+            return y
+        self._mark(True, EventType.MOE_ROUTER, layer_idx, mb_idx)
+        xn, ids, w = ops.router_topk(h, lw.post_norm, lw.w_router, cfg.num_experts_per_tok,
+                                     cfg.rms_norm_eps, cfg.norm_topk_prob)
+        self._mark(False, EventType.MOE_ROUTER, layer_idx, mb_idx)
+        self._mark(True, EventType.MOE_EXPERTS, layer_idx, mb_idx)
+        y = ops.moe_experts(xn, ids, w, lw.w_gate_up, lw.w_down, lw.expert_start,
+                            residual=residual, out=out, **kw)
+        self._mark(False, EventType.MOE_EXPERTS, layer_idx, mb_idx)
+        return y

@@ -1,0 +1,166 @@
+"""One forward pass (a prefill or one decode step) of the disaggregated model
+for the roles this process holds, over micro-batches, through a transport.
+
+The host loop only *enqueues* work: per (layer, micro-batch) the attention
+block runs on the attention stream, the FFN block on the FFN stream, and every
+receive makes the consuming stream wait. The schedule decides the order and
+the waits:
+
+* ``serial``   -- per layer and micro-batch a full A->F->A round trip before
+  the next micro-batch starts (reference ``SimplePipelineScheduler`` /
+  ``forward_layer_sync``, src/pipeline/scheduler.py:221-236).
+* ``dbo``      -- dual-batch overlap: the attention block of micro-batch m+1
+  runs while the FFN works on micro-batch m. Layer-synchronous by default:
+  layer l+1 starts only after every micro-batch's layer-l result is back
+  (reference decode DBO without ``--crosslayer``).
+* ``dbo`` + ``crosslayer`` -- micro-batch m enters layer l+1 as soon as its
+  own layer-l result is back (reference ``--crosslayer``,
+  src/pipeline/decode_scheduler.py:304-332).
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Dict, List, Optional
+
+import torch
+
+from ..utils.timing import EventType, TimingTracker
+from .micro_batch import ForwardPlan
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def _on(stream):
+    return torch.cuda.stream(stream) if stream is not None else _Null()
+
+
+class PipelineEngine:
+    def __init__(self, model):
+        self.model = model
+
+    def forward(self, plan: ForwardPlan, input_ids: Optional[torch.Tensor], mode: str = "dbo",
+                crosslayer: bool = False, trackers: Optional[Dict[str, TimingTracker]] = None,
+                last_only: bool = True, advance_cache: bool = True) -> Optional[torch.Tensor]:
+        """Runs all layers. `input_ids` are this attention rank's sequences
+        [B_local, q_len] (ignored on an FFN-only rank). Returns logits on
+        attention ranks ([B_local, V] with `last_only`, else [B_local*q_len, V])."""
+        if mode not in ("serial", "dbo"):
+            raise ValueError(f"unknown schedule {mode!r}")
+        m_ = self.model
+        colocated = m_.ctx.is_attention_node and m_.ctx.is_ffn_node
+        serial = mode == "serial"
+        s_main = m_.attn_stream
+        s_ffn = m_.ffn_stream if (colocated and not serial) else s_main
+        caller = torch.cuda.current_stream() if s_main is not None else None
+        for s in {s_main, s_ffn} - {None}:
+            s.wait_stream(caller)
+        try:
+            return self._forward(plan, input_ids, serial, crosslayer, trackers or {}, last_only,
+                                 advance_cache, s_main, s_ffn)
+        finally:
+            for s in {s_main, s_ffn} - {None}:
+                caller.wait_stream(s)
+
+    def _forward(self, plan, input_ids, serial, crosslayer, trackers, last_only, advance_cache,
+                 s_attn, s_ffn):
+        m_ = self.model
+        ctx = m_.ctx
+        tr = m_.transport
+        L = m_.num_layers
+        ta = trackers.get("attention")
+        tf = trackers.get("ffn")
+        has_attn, has_ffn = ctx.is_attention_node, ctx.is_ffn_node
+        colocated = has_attn and has_ffn
+        with _on(s_attn):
+            tr.begin(plan)
+        if has_ffn:
+            m_.ffn_worker.tracker = tf
+
+        def ffn_block(l: int, m: int):
+            with _on(s_ffn):
+                if tf:
+                    tf.mark_start(EventType.RECV_WAIT, l, m)
+                h = tr.a2f_recv(l, m)
+                if tf:
+                    tf.mark_end(EventType.RECV_WAIT, l, m)
+                    tf.mark_start(EventType.FFN_COMPUTE, l, m)
+                out = m_.ffn_worker.forward_ffn_layer(
+                    l, h, add_residual=(ctx.ffn_index == 0), sink=tr.f2a_sink(l, m), mb_idx=m)
+                if tf:
+                    tf.mark_end(EventType.FFN_COMPUTE, l, m)
+                t0 = time.perf_counter()
+                tr.f2a_send(l, m, out)
+                if tf and not tr.fused:
+                    tf.record_send(None, l, m, t0, out)
+
+        if not has_attn:
+            for l in range(L):
+                for m in range(plan.num_mb):
+                    ffn_block(l, m)
+            with _on(s_ffn):
+                tr.end()
+            return None
+
+        attn = m_.attention_worker
+        slots = plan.slots_of(ctx.attn_index)
+        cache = attn.cache
+        start = cache.seq_len
+        xs: Dict[int, List[torch.Tensor]] = {}
+        with _on(s_attn):
+            x0 = attn.embed(input_ids)
+            for s in slots:
+                r0 = s.batch_offset * s.q_len
+                xs[s.idx] = [x0[r0:r0 + s.tokens]]
+        have = {(s.idx, -1) for s in slots}  # (m, l): layer-l output of m received
+
+        def recv(l: int, m: int):
+            if (m, l) in have:
+                return
+            if ta:
+                ta.mark_start(EventType.RECV_WAIT, l, m)
+            xs[m] = tr.f2a_recv(l, m)
+            if ta:
+                ta.mark_end(EventType.RECV_WAIT, l, m)
+            have.add((m, l))
+
+        for l in range(L):
+            if not serial and not crosslayer and l > 0:
+                with _on(s_attn):
+                    for s in slots:
+                        recv(l - 1, s.idx)
+            for s in slots:
+                m = s.idx
+                with _on(s_attn):
+                    recv(l - 1, m)
+                    if ta:
+                        ta.mark_start(EventType.ATTN_COMPUTE, l, m)
+                    h = attn.forward_attention_layer(l, xs[m], s.batch_offset, s.q_len,
+                                                     start_pos=start, sink=tr.a2f_sink(l, m))
+                    if ta:
+                        ta.mark_end(EventType.ATTN_COMPUTE, l, m)
+                    t0 = time.perf_counter()
+                    tr.a2f_send(l, m, h)
+                    if ta and not tr.fused:
+                        ta.record_send(None, l, m, t0, h)
+                if colocated:
+                    ffn_block(l, m)
+                if serial:
+                    with _on(s_attn):
+                        recv(l, m)
+        logits = []
+        with _on(s_attn):
+            for s in slots:
+                recv(L - 1, s.idx)
+                logits.append(attn.forward_lm_head(xs[s.idx], s.q_len, last_only=last_only))
+            out = torch.cat(logits, 0) if len(logits) > 1 else logits[0]
+            if advance_cache:
+                cache.advance(plan.q_len)
+            tr.end()
+        return out

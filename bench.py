@@ -1,0 +1,278 @@
+#!/usr/bin/env python
+"""Headline benchmark: Qwen3-30B-A3B bf16 decode throughput with
+cross-layer decode DBO (plus serial decode TPOT and prefill TTFT, DBO vs
+serial), random-init weights, synthetic token ids.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+N = 1 co-locates the attention and FFN roles on one GPU (two streams);
+N > 1 runs one rank per GPU under torchrun: N/2 attention ranks (data parallel
+over the batch) and N/2 FFN ranks (expert parallel, 128/(N/2) experts each),
+with the fused peer-memory A2F/F2A path. Weak scaling: 32 sequences per GPU
+(global batch 32 * N; 256 at 8 GPUs), prompt 256 tokens.
+
+Timing: W untimed decode steps, then exactly K decode steps between a barrier
+and a device synchronize, measured with CUDA events on the launching stream,
+max over ranks. Each step reads the 61 GB of weights (far above the 126 MB
+L2), so no L2 flush is needed. nvidia-smi clocks are sampled during the timed
+region. The e2e number runs the public ``generate`` API with per-step
+host->device token input and device->host token output from pinned memory.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = ("Qwen3-30B-A3B decode TPOT ms & prefill TTFT ms, DBO vs serial, at 1/2/4/8 B200")
+# published cross-layer decode TPOT (ms) of the reference at seq 256, by batch
+# (4xV100; BASELINE.md decode table): value / (1000 * b / TPOT)
+REF_XL_TPOT_S256 = {2: 243.7, 4: 417.1, 8: 502.9, 16: 739.4, 32: 884.2, 64: 1274.1,
+                    96: 1596.4, 128: 1757.4, 192: 1873.6}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="qwen3-30b-a3b")
+    p.add_argument("--batch-per-gpu", type=int, default=32)
+    p.add_argument("--batch", type=int, default=None, help="global batch (default 32 * gpus)")
+    p.add_argument("--seq", type=int, default=256)
+    p.add_argument("--tokens", type=int, default=20)
+    p.add_argument("--comm-impl", default="auto", choices=["auto", "fused", "nccl"])
+    p.add_argument("--no-serial", action="store_true", help="skip the serial comparison")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--prefill-batch", type=int, default=None,
+                   help="prefill TTFT batch (default: the decode batch)")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.strip().split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args, rank):
+    from afd_demo_b200.scripts.reference_arm import run_reference
+
+    line = run_reference(args)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if world != args.gpus:
+        if args.gpus > 1 and world == 1:
+            raise SystemExit("run N > 1 under torchrun (one rank per GPU)")
+    if args.impl == "reference":
+        return reference_arm(args, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    from afd_demo_b200 import ops
+    from afd_demo_b200.models import DisaggregatedQwenModel
+    from afd_demo_b200.parallel.dist import DistributedConfig, get_distributed_context
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cuda")
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    ctx = get_distributed_context()
+    ctx.initialize(DistributedConfig(world_size=world, rank=rank, local_rank=local,
+                                     backend="nccl", timeout_s=300))
+    B = args.batch or args.batch_per_gpu * args.gpus
+    S, T = args.seq, args.tokens
+    max_seq = S + max(T, args.warmup + args.steps + 2) + 8
+    model = DisaggregatedQwenModel.from_pretrained(
+        args.model, device=f"cuda:{local}", dtype=torch.bfloat16, max_seq_len=max_seq,
+        max_batch_size=B, comm_impl=args.comm_impl, random_init=True, seed=0,
+        num_micro_batches=2)
+    V = model.config.vocab_size
+    g = torch.Generator().manual_seed(1234)
+    ids_host = torch.randint(0, V, (B, S), generator=g).pin_memory()
+    ids = ids_host.to(f"cuda:{local}", non_blocking=True)
+    torch.cuda.synchronize()
+
+    def bar():
+        torch.cuda.synchronize()
+        ctx.barrier()
+
+    def timed(fn, n):
+        bar()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ctx.barrier()
+        ms = s.elapsed_time(e)
+        if world > 1:
+            t = torch.tensor([ms], device=f"cuda:{local}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # ---------------- prefill TTFT: serial vs DBO (2 micro-batches)
+    def prefill(mode, nmb):
+        return model.run_forward(ids, mode, nmb, crosslayer=True, reset_cache=True)
+
+    for _ in range(2):
+        prefill("dbo", 2)
+        prefill("serial", 1)
+    ttft_dbo = timed(lambda: prefill("dbo", 2), 1)
+    ttft_serial = timed(lambda: prefill("serial", 1), 1)
+
+    # ---------------- decode: device-timed graph replays
+    def decode_run(mode, nmb, crosslayer, warm, steps):
+        logits = prefill("dbo", 2)
+        tok = torch.zeros(B, 1, dtype=torch.long, device=f"cuda:{local}")
+        r = model.local_batch(B)
+        holder = {}
+
+        def step():
+            if model.ctx.is_attention_node:
+                tok[r.start:r.stop, 0] = ops.argmax(holder.get("logits", logits))
+            holder["logits"] = model.decode_step(tok, mode, nmb, crosslayer, True)
+
+        for _ in range(warm):
+            step()
+        ops.LAUNCHES.reset()
+        clocks = ClockSampler(local)
+        clocks.start()
+        ms = timed(step, steps)
+        clk = clocks.stop()
+        # kernels of this package in the timed region: graph contents per
+        # replay plus the argmax launched outside the graph each step
+        per_graph = sum(gr.launches for gr in model._graphs.values())
+        launches = steps * per_graph + ops.LAUNCHES.reset()
+        model.release_graphs()
+        return ms / steps, clk, launches
+
+    tpot_xl, clk, launches = decode_run("dbo", 2, True, args.warmup, args.steps)
+    tpot_serial = None
+    if not args.no_serial:
+        tpot_serial, _, _ = decode_run("serial", 1, False, 2, max(3, min(args.steps, 10)))
+
+    # ---------------- e2e through the public generate API (host I/O per step)
+    e2e = None
+    if not args.no_e2e:
+        def gen():
+            ids_dev = ids_host.to(f"cuda:{local}", non_blocking=True)
+            model.generate(ids_dev, max_new_tokens=T, do_sample=False, use_decode_dbo=True,
+                           num_decode_micro_batches=2, decode_use_crosslayer=True,
+                           prefill_mode="dbo", num_prefill_micro_batches=2,
+                           use_cuda_graph=True, host_io=True)
+            return model._last_generation_metrics
+
+        gen()  # warm (graphs for this batch)
+        met = gen()
+        tp = torch.tensor([met["decode_tpot_ms"], met["prefill_ms"]], device=f"cuda:{local}")
+        if world > 1:
+            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+        e2e_tpot = float(tp[0])
+        e2e = {"value": 1000.0 * B / e2e_tpot, "unit": "tok/s", "decode_tpot_ms": e2e_tpot,
+               "prefill_ms": float(tp[1]),
+               "h2d_bytes_per_step": int(len(model.local_batch(B)) * 8)
+               if model.ctx.is_attention_node else 0,
+               "d2h_bytes_per_step": int(len(model.local_batch(B)) * 8)
+               if model.ctx.is_attention_node else 0,
+               "api": "DisaggregatedQwenModel.generate(host_io=True, use_cuda_graph=True)"}
+
+    value = 1000.0 * B / tpot_xl
+    ref = REF_XL_TPOT_S256.get(B) if S == 256 else None
+    topo = model.topology
+    par = ("colocated attention+FFN on 1 GPU" if topo.colocated else
+           f"{topo.n_attn}A{topo.n_ffn}F: attention dp{topo.n_attn}, FFN ep{topo.n_ffn}")
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s (decode, 1000*batch/TPOT)",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tpot_xl,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": (value / (1000.0 * B / ref)) if ref else None,
+        "dtype": "bf16",
+        "data": "synthetic token ids uniform in [0, vocab), random-init weights",
+        "config": {"model": "Qwen3-30B-A3B", "global_batch": B, "seq_len": S,
+                   "decode_tokens": T, "parallelism": par,
+                   "mode": "decode DBO, cross-layer, 2 micro-batches, CUDA graph per step",
+                   "comm_impl": model.comm_impl,
+                   "l2": "inputs larger than L2 (all expert weights read every step)"},
+        "decode_tpot_ms": {"dbo_crosslayer": tpot_xl, "serial": tpot_serial},
+        "dbo_speedup_decode": (tpot_serial / tpot_xl) if tpot_serial else None,
+        "prefill_ttft_ms": {"dbo": ttft_dbo, "serial": ttft_serial,
+                            "speedup": ttft_serial / ttft_dbo},
+        "clocks": clk,
+        "e2e": e2e,
+        "gpu_launches": launches,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.release_graphs()
+    ctx.barrier()
+    ctx.cleanup()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,380 @@
+// PyTorch bindings of the sm_100a kernels and of the peer-memory runtime
+// (CUDA IPC handles, flag signal / bounded wait). Every op launches on the
+// current PyTorch CUDA stream and raises on a bad argument or launch error.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+#include "gemm_tcgen05.h"
+#include "kernels.h"
+
+namespace {
+
+using afd::GemmLaunch;
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define CHECK_ROWMAJOR(x) TORCH_CHECK((x).stride(-1) == 1, #x " must have unit inner stride")
+
+inline void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, " failed with code ", rc,
+              rc > 4000 ? std::string(" (") + cudaGetErrorString((cudaError_t)(rc - 4000)) + ")"
+                        : std::string());
+}
+
+inline __nv_bfloat16* bf(const at::Tensor& t) {
+  return reinterpret_cast<__nv_bfloat16*>(t.data_ptr());
+}
+inline const __nv_bfloat16* cbf(const at::Tensor& t) {
+  return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
+}
+template <typename T>
+inline T* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+int g_num_sms = 0;
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
+}
+
+// out[rows, N] = x[rows, K] @ w^T (+ epilogue); see gemm_tcgen05.cu.
+void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_tiles,
+          int64_t w_rows_per_group, int64_t up_offset, const c10::optional<at::Tensor>& blocks,
+          const c10::optional<at::Tensor>& num_blocks, int64_t dense_rows,
+          const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& row_scale,
+          bool swiglu, int64_t block_n, int64_t units_hint, std::vector<int64_t> peers,
+          int64_t peer_row_offset, std::vector<int64_t> flags, int64_t signal_value,
+          const c10::optional<at::Tensor>& done_counter, const c10::optional<at::Tensor>& status,
+          const c10::optional<at::Tensor>& epoch) {
+  CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
+  CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
+  CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(peers.size() <= (size_t)afd::kMaxPeers, "too many peers");
+  TORCH_CHECK(flags.size() <= (size_t)afd::kMaxPeers + 1, "too many flags");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(w.size(-1) == K, "K mismatch: w ", w.size(-1), " x ", K);
+  GemmLaunch p{};
+  afd::GemmArgs& a = p.args;
+  a.K = (int)K;
+  a.f_tiles = (int)f_tiles;
+  a.w_rows_per_group = (int)w_rows_per_group;
+  a.up_offset = (int)up_offset;
+  a.blocks = opt_ptr<const int4>(blocks);
+  a.num_blocks = opt_ptr<const int>(num_blocks);
+  TORCH_CHECK((a.blocks == nullptr) == (a.num_blocks == nullptr), "blocks/num_blocks pairing");
+  a.dense_rows = (int)dense_rows;
+  a.out = bf(out);
+  a.ld_out = (int)out.stride(-2);
+  if (residual.has_value() && residual->defined()) {
+    CHECK_BF16(*residual);
+    a.residual = cbf(*residual);
+    a.ld_res = (int)residual->stride(-2);
+  }
+  a.row_scale = opt_ptr<const float>(row_scale);
+  for (size_t i = 0; i < peers.size(); ++i) a.peer_out[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
+  a.n_peers = (int)peers.size();
+  a.peer_row_offset = (int)peer_row_offset;
+  for (size_t i = 0; i < flags.size(); ++i) a.flags[i] = reinterpret_cast<int*>(flags[i]);
+  a.n_flags = (int)flags.size();
+  a.signal_value = (int)signal_value;
+  a.epoch = opt_ptr<const int>(epoch);
+  a.done_counter = opt_ptr<int>(done_counter);
+  a.status = opt_ptr<int>(status);
+  p.w = w.data_ptr();
+  p.w_rows_total = w.numel() / K;
+  p.ld_w = w.stride(-2);
+  p.x = x.data_ptr();
+  p.x_rows = x.numel() / K;
+  p.ld_x = x.stride(-2);
+  p.swiglu = swiglu;
+  p.block_n = (int)block_n;
+  p.units_hint = (int)units_hint;
+  p.num_sms = num_sms();
+  if (a.blocks == nullptr && dense_rows == 0) return;
+  check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_swapab");
+}
+
+void sum_rmsnorm(std::vector<at::Tensor> parts, const at::Tensor& weight,
+                 const c10::optional<at::Tensor>& x_out, at::Tensor& y_out, double eps) {
+  TORCH_CHECK(!parts.empty() && parts.size() <= (size_t)afd::kMaxParts, "1..8 parts");
+  afd::SumNormArgs a{};
+  const int64_t H = parts[0].size(-1);
+  const int64_t rows = parts[0].numel() / H;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    CHECK_CUDA(parts[i]); CHECK_BF16(parts[i]); CHECK_ROWMAJOR(parts[i]);
+    TORCH_CHECK(parts[i].stride(-2) == parts[0].stride(-2), "parts must share a row stride");
+    a.parts[i] = cbf(parts[i]);
+  }
+  a.n_parts = (int)parts.size();
+  a.ld_in = (int)(parts[0].dim() > 1 ? parts[0].stride(-2) : H);
+  a.weight = cbf(weight);
+  a.x_out = x_out.has_value() && x_out->defined() ? bf(*x_out) : nullptr;
+  a.y_out = bf(y_out);
+  a.ld_out = (int)(y_out.dim() > 1 ? y_out.stride(-2) : H);
+  a.H = (int)H;
+  a.eps = (float)eps;
+  check_rc(afd::launch_sum_rmsnorm(a, (int)rows, cur_stream()), "sum_rmsnorm");
+}
+
+void qk_norm_rope_cache(const at::Tensor& qkv, const at::Tensor& q_norm, const at::Tensor& k_norm,
+                        const at::Tensor& rope, at::Tensor& q_out, at::Tensor& k_cache,
+                        at::Tensor& v_cache, const at::Tensor& start_pos, int64_t q_len,
+                        int64_t batch_offset, int64_t nq, int64_t nkv, double eps) {
+  CHECK_BF16(qkv); CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(q_out);
+  TORCH_CHECK(rope.scalar_type() == at::kFloat, "rope table must be fp32");
+  TORCH_CHECK(start_pos.scalar_type() == at::kInt, "start_pos must be int32");
+  afd::QKRopeArgs a{};
+  a.qkv = cbf(qkv);
+  a.ld_qkv = (int)qkv.stride(0);
+  a.q_norm = cbf(q_norm);
+  a.k_norm = cbf(k_norm);
+  a.rope = rope.data_ptr<float>();
+  a.q_out = bf(q_out);
+  a.k_cache = bf(k_cache);
+  a.v_cache = bf(v_cache);
+  a.start_pos = start_pos.data_ptr<int>();
+  a.T = (int)qkv.size(0);
+  a.q_len = (int)q_len;
+  a.batch_offset = (int)batch_offset;
+  a.nq = (int)nq;
+  a.nkv = (int)nkv;
+  a.D = (int)k_cache.size(-1);
+  a.s_max = (int)k_cache.size(-2);
+  a.eps = (float)eps;
+  check_rc(afd::launch_qk_norm_rope_cache(a, cur_stream()), "qk_norm_rope_cache");
+}
+
+void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      at::Tensor& out, const at::Tensor& start_pos, int64_t batch_offset,
+                      int64_t nsplit, const c10::optional<at::Tensor>& o_part,
+                      const c10::optional<at::Tensor>& ml_part) {
+  afd::DecodeAttnArgs a{};
+  a.q = cbf(q);
+  a.k_cache = cbf(k_cache);
+  a.v_cache = cbf(v_cache);
+  a.out = bf(out);
+  a.o_part = opt_ptr<float>(o_part);
+  a.ml_part = opt_ptr<float>(ml_part);
+  a.start_pos = start_pos.data_ptr<int>();
+  a.batch_offset = (int)batch_offset;
+  a.nq = (int)q.size(1);
+  a.nkv = (int)k_cache.size(1);
+  a.D = (int)q.size(2);
+  a.s_max = (int)k_cache.size(2);
+  check_rc(afd::launch_decode_attention(a, (int)q.size(0), (int)nsplit, cur_stream()),
+           "decode_attention");
+}
+
+void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                       at::Tensor& out, const at::Tensor& start_pos, int64_t q_len,
+                       int64_t batch_offset) {
+  afd::PrefillAttnArgs a{};
+  a.q = cbf(q);
+  a.k_cache = cbf(k_cache);
+  a.v_cache = cbf(v_cache);
+  a.out = bf(out);
+  a.start_pos = start_pos.data_ptr<int>();
+  a.q_len = (int)q_len;
+  a.batch_offset = (int)batch_offset;
+  a.nq = (int)q.size(1);
+  a.nkv = (int)k_cache.size(1);
+  a.D = (int)q.size(2);
+  a.s_max = (int)k_cache.size(2);
+  const int B = (int)(q.size(0) / q_len);
+  check_rc(afd::launch_prefill_attention(a, B, cur_stream()), "prefill_attention");
+}
+
+void router_topk(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, int64_t top_k,
+                 bool renorm) {
+  afd::RouterArgs a{};
+  a.logits = cbf(logits);
+  a.ld_logits = (int)logits.stride(0);
+  a.ids = ids.data_ptr<int32_t>();
+  a.weights = weights.data_ptr<float>();
+  a.T = (int)logits.size(0);
+  a.E = (int)logits.size(1);
+  a.top_k = (int)top_k;
+  a.renorm = renorm ? 1 : 0;
+  check_rc(afd::launch_router_topk(a, cur_stream()), "router_topk");
+}
+
+void moe_align(const at::Tensor& ids, const at::Tensor& weights, int64_t expert_start,
+               int64_t n_local, int64_t block_n, at::Tensor& inv, at::Tensor& row_token,
+               at::Tensor& row_weight, at::Tensor& expert_offsets, at::Tensor& blocks,
+               at::Tensor& num_blocks, at::Tensor& num_rows) {
+  afd::MoeAlignArgs a{};
+  a.ids = ids.data_ptr<int32_t>();
+  a.weights = weights.data_ptr<float>();
+  a.T = (int)ids.size(0);
+  a.top_k = (int)ids.size(1);
+  a.expert_start = (int)expert_start;
+  a.n_local = (int)n_local;
+  a.block_n = (int)block_n;
+  a.inv = inv.data_ptr<int32_t>();
+  a.row_token = row_token.data_ptr<int32_t>();
+  a.row_weight = row_weight.data_ptr<float>();
+  a.expert_offsets = expert_offsets.data_ptr<int32_t>();
+  a.blocks = reinterpret_cast<int4*>(blocks.data_ptr<int32_t>());
+  a.num_blocks = num_blocks.data_ptr<int32_t>();
+  a.num_rows = num_rows.data_ptr<int32_t>();
+  check_rc(afd::launch_moe_align(a, cur_stream()), "moe_align");
+}
+
+void moe_gather(const at::Tensor& x, const at::Tensor& row_token, const at::Tensor& num_rows,
+                at::Tensor& out, int64_t max_rows) {
+  afd::MoeGatherArgs a{};
+  a.x = cbf(x);
+  a.ld_x = (int)x.stride(0);
+  a.row_token = row_token.data_ptr<int32_t>();
+  a.num_rows = num_rows.data_ptr<int32_t>();
+  a.out = bf(out);
+  a.H = (int)x.size(1);
+  check_rc(afd::launch_moe_gather(a, (int)max_rows, cur_stream()), "moe_gather");
+}
+
+void moe_combine(const at::Tensor& y, const at::Tensor& inv, int64_t T, int64_t top_k,
+                 const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& out,
+                 std::vector<int64_t> peers, std::vector<int64_t> seg_offsets,
+                 int64_t peer_row_offset, std::vector<int64_t> flags, int64_t signal_value,
+                 const c10::optional<at::Tensor>& done_counter,
+                 const c10::optional<at::Tensor>& epoch) {
+  TORCH_CHECK(peers.size() <= 8 && flags.size() <= (size_t)afd::kMaxFlagPeers, "too many peers");
+  TORCH_CHECK(peers.empty() || seg_offsets.size() == peers.size() + 1,
+              "seg_offsets needs one entry per peer plus the end");
+  afd::MoeCombineArgs a{};
+  a.y = cbf(y);
+  a.inv = inv.data_ptr<int32_t>();
+  a.H = (int)y.size(1);
+  a.top_k = (int)top_k;
+  if (residual.has_value() && residual->defined()) {
+    a.residual = cbf(*residual);
+    a.ld_res = (int)residual->stride(0);
+  }
+  if (out.has_value() && out->defined()) {
+    a.out = bf(*out);
+    a.ld_out = (int)out->stride(0);
+  } else {
+    a.ld_out = a.H;
+  }
+  for (size_t i = 0; i < peers.size(); ++i) a.peer_out[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
+  for (size_t i = 0; i < seg_offsets.size() && i < 9; ++i) a.seg_offsets[i] = (int)seg_offsets[i];
+  a.n_peers = (int)peers.size();
+  a.peer_row_offset = (int)peer_row_offset;
+  for (size_t i = 0; i < flags.size(); ++i) a.flags[i] = reinterpret_cast<int*>(flags[i]);
+  a.n_flags = (int)flags.size();
+  a.signal_value = (int)signal_value;
+  a.epoch = opt_ptr<const int>(epoch);
+  a.done_counter = opt_ptr<int>(done_counter);
+  check_rc(afd::launch_moe_combine(a, (int)T, cur_stream()), "moe_combine");
+}
+
+void argmax(const at::Tensor& logits, at::Tensor& out) {
+  CHECK_BF16(logits);
+  check_rc(afd::launch_argmax(cbf(logits), (int)logits.size(0), (int)logits.size(1),
+                              (int)logits.stride(0), out.data_ptr<int64_t>(), cur_stream()),
+           "argmax");
+}
+
+afd::FlagArgs flag_args(const std::vector<int64_t>& flags, int64_t value,
+                        const c10::optional<at::Tensor>& status, int64_t timeout_ns,
+                        const c10::optional<at::Tensor>& epoch) {
+  TORCH_CHECK(flags.size() <= 32, "at most 32 flags");
+  afd::FlagArgs a{};
+  for (size_t i = 0; i < flags.size(); ++i) a.flags[i] = reinterpret_cast<int*>(flags[i]);
+  a.n = (int)flags.size();
+  a.value = (int)value;
+  a.epoch = opt_ptr<const int>(epoch);
+  a.status = opt_ptr<int>(status);
+  a.timeout_ns = (unsigned long long)timeout_ns;
+  return a;
+}
+
+void signal_flags(std::vector<int64_t> flags, int64_t value,
+                  const c10::optional<at::Tensor>& epoch) {
+  check_rc(afd::launch_signal_flags(flag_args(flags, value, c10::nullopt, 0, epoch), cur_stream()),
+           "signal_flags");
+}
+
+// Bounded device-side wait (never a host block): the stream stalls until all
+// flags reach the target or `timeout_ns` passes, in which case the status
+// word records kTimeoutPeerFlag and the stream continues.
+void wait_flags(std::vector<int64_t> flags, int64_t value, const c10::optional<at::Tensor>& status,
+                int64_t timeout_ns, const c10::optional<at::Tensor>& epoch) {
+  check_rc(afd::launch_wait_flags(flag_args(flags, value, status, timeout_ns, epoch), cur_stream()),
+           "wait_flags");
+}
+
+void add_i32(at::Tensor& t, int64_t by) {
+  check_rc(afd::launch_add_i32(t.data_ptr<int>(), (int)by, cur_stream()), "add_i32");
+}
+
+// ---------------------------------------------------------------- IPC ---
+// Peer-visible buffers are separate cudaMalloc allocations (not sub-blocks of
+// PyTorch's caching allocator), so the IPC handle of the tensor's base
+// pointer names exactly that buffer. The tensor frees the memory when the
+// last reference goes away.
+at::Tensor ipc_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)nbytes);
+  TORCH_CHECK(e == cudaSuccess, "cudaMalloc(", nbytes, "): ", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, (size_t)nbytes);
+  TORCH_CHECK(e == cudaSuccess, "cudaMemset: ", cudaGetErrorString(e));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, (c10::DeviceIndex)device);
+  return torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+}
+
+pybind11::bytes ipc_handle(const at::Tensor& t) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, t.data_ptr());
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcGetMemHandle: ", cudaGetErrorString(e));
+  return pybind11::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+int64_t ipc_open(const std::string& handle) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcOpenMemHandle: ", cudaGetErrorString(e));
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+
+void ipc_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "afd_demo_b200 sm_100a kernels";
+  m.def("num_sms", &num_sms);
+  m.def("gemm", &gemm);
+  m.def("sum_rmsnorm", &sum_rmsnorm);
+  m.def("qk_norm_rope_cache", &qk_norm_rope_cache);
+  m.def("decode_attention", &decode_attention);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("router_topk", &router_topk);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  m.def("argmax", &argmax);
+  m.def("signal_flags", &signal_flags);
+  m.def("wait_flags", &wait_flags);
+  m.def("add_i32", &add_i32);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+}

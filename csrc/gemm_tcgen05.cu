@@ -1,0 +1,332 @@
+// Grouped "swap-AB" GEMM on the 5th-generation tensor cores (tcgen05 + TMEM),
+// operands staged by TMA. One kernel serves every projection of the model:
+//
+//   out[row, f] = epilogue( sum_k X[row, k] * W[group, f, k] )
+//
+// The weight matrix is the MMA's A operand (M = 128 output features per
+// tile) and the token rows are the B operand (N = 32..256 rows per tile), so
+// the accumulator D^T[f, row] lives in TMEM with one feature per lane. A
+// decode step with a handful of tokens per expert therefore pays for N = 32
+// token columns, not for a 128-row M tile, and the kernel streams each
+// expert's weight tile from HBM exactly once.
+//
+// Work units are (row block, feature tile). Row blocks come from a device
+// list written by the MoE routing kernel (grouped mode: one or more blocks
+// per expert, <= BN rows each) or are derived from a host row count (dense
+// mode: a single group). Units are dealt round-robin to a persistent grid.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator
+// + MMA issuer, warps 2..5 = epilogue (TMEM -> registers -> global). Smem
+// stages are guarded by full/empty mbarriers; the TMEM accumulator by
+// tmem_full (tcgen05.commit) / tmem_empty (epilogue arrivals).
+//
+// Epilogues: plain store (+ residual), SwiGLU over a gate/up accumulator
+// pair (two A tiles per stage: gate rows and up rows of the same expert),
+// per-row scale (routing weight), and optional peer stores: the same bf16
+// tile is written to up to 8 peer-GPU buffers (NVLink P2P stores), after
+// which the last CTA to finish raises a release flag on every peer. That is
+// the fused attention->FFN hand-off of the o_proj GEMM.
+//
+// No cluster launch and no multicast: every TMA load reads this GPU's memory.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "gemm_tcgen05.h"
+
+namespace afd {
+
+constexpr int kBM = 128;        // output features per tile (MMA M)
+constexpr int kBK = 64;         // K per pipeline stage (one 128-byte swizzle atom)
+constexpr int kBoxRows = 32;    // token rows per TMA box
+constexpr int kThreads = 192;
+
+template <bool SWIGLU, int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;             // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;               // BN x 128 B
+  static constexpr int kStageBytes = kABytes * (SWIGLU ? 2 : 1) + kBBytes;
+  static constexpr int kDataBytes = kStageBytes * STAGES;
+  static constexpr int kTotal = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTmemCols = SWIGLU ? 512 : (BN <= 128 ? 128 : 256);
+  static constexpr int kUpCol = SWIGLU ? 256 : 0;
+};
+
+__device__ __forceinline__ int4 unit_block(const GemmArgs& a, int b) {
+  if (a.blocks != nullptr) return a.blocks[b];
+  int rs = b * a.block_n;
+  int n = min(a.block_n, a.dense_rows - rs);
+  return make_int4(rs, n, 0, 0);
+}
+
+__device__ __forceinline__ int total_units(const GemmArgs& a) {
+  int nb = a.blocks != nullptr ? *a.num_blocks : (a.dense_rows + a.block_n - 1) / a.block_n;
+  return nb * a.f_tiles;
+}
+
+template <bool SWIGLU, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                       const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
+  using L = GemmSmem<SWIGLU, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kDataBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, 4);  // one arrival per epilogue warp
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int k_iters = args.K / kBK;
+  const int units = total_units(args);
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int4 blk = unit_block(args, u / args.f_tiles);
+        const int ft = u % args.f_tiles;
+        const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
+        const int w_row = blk.z * args.w_rows_per_group + ft * kBM;
+        const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
+        for (int k = 0; k < k_iters; ++k) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.status, 10)) break;
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
+          mbar_arrive_expect_tx(&full_bar[stage], bytes);
+          tma_load_2d(sa, &tmap_w, &full_bar[stage], k * kBK, w_row);
+          if (SWIGLU)
+            tma_load_2d(sa + L::kABytes, &tmap_w, &full_bar[stage], k * kBK,
+                        w_row + args.up_offset);
+          for (int b = 0; b < n_boxes; ++b)
+            tma_load_2d(sb + b * kBoxRows * kBK * 2, &tmap_x, &full_bar[stage], k * kBK,
+                        blk.x + b * kBoxRows);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: the last STAGES fills must have landed before the CTA may
+      // exit (their full barriers complete on TMA arrival, independent of
+      // the MMA warp). Fills that never happened refer to phases before the
+      // barrier's first one and complete immediately.
+      volatile int no_abort = 0;
+      for (int s = 0; s < STAGES; ++s) {
+        if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+        mbar_wait(&full_bar[stage], phase, &no_abort, args.status, 11);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t tphase = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int4 blk = unit_block(args, u / args.f_tiles);
+        const int n_mma = max(32, ((blk.y + 31) / 32) * 32);
+        const uint32_t idesc = umma_idesc_bf16(kBM, n_mma);
+        // the epilogue must have drained the previous accumulator
+        if (!mbar_wait(tempty_bar, tphase ^ 1, abort_flag, args.status, 20)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int k = 0; k < k_iters; ++k) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, 21)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
+            umma_bf16(tmem_base, umma_desc_sw128(sa + kk * 32), bdesc, idesc,
+                      (k | kk) != 0);
+            if (SWIGLU)
+              umma_bf16(tmem_base + L::kUpCol, umma_desc_sw128(sa + L::kABytes + kk * 32), bdesc,
+                        idesc, (k | kk) != 0);
+          }
+          umma_commit(&empty_bar[stage]);  // smem stage free once these MMAs retire
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar);  // accumulator ready for the epilogue
+        tphase ^= 1;
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int f_local = q * 32 + lane;
+    uint32_t tphase = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      const int4 blk = unit_block(args, u / args.f_tiles);
+      const int ft = u % args.f_tiles;
+      const int f = ft * kBM + f_local;
+      if (!mbar_wait(tfull_bar, tphase, abort_flag, args.status, 30)) break;
+      tphase ^= 1;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16);
+      for (int c = 0; c < blk.y; c += 16) {
+        float acc[16];
+        tmem_ld16(t_row + c, acc);
+        if (SWIGLU) {
+          float up[16];
+          tmem_ld16(t_row + L::kUpCol + c, up);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            // HF rounds gate/up to bf16 before the activation
+            const float g = round_bf16(acc[j]);
+            const float s = g / (1.0f + __expf(-g));
+            acc[j] = round_bf16(s) * round_bf16(up[j]);
+          }
+        }
+        const int jmax = min(16, blk.y - c);
+        for (int j = 0; j < jmax; ++j) {
+          const int row = blk.x + c + j;
+          float v = acc[j];
+          if (args.row_scale != nullptr) v = round_bf16(v) * args.row_scale[row];
+          if (args.residual != nullptr)
+            v = round_bf16(v) + bf16_to_f(args.residual[(size_t)row * args.ld_res + f]);
+          const __nv_bfloat16 o = f_to_bf16(v);
+          args.out[(size_t)row * args.ld_out + f] = o;
+          for (int p = 0; p < args.n_peers; ++p)
+            args.peer_out[p][(size_t)(row + args.peer_row_offset) * args.ld_out + f] = o;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+
+  // Fused completion signal: the last CTA to finish publishes `signal_value`
+  // to every peer flag (and the local one), after a system-scope fence that
+  // orders this CTA's peer stores before its counter increment.
+  // An aborted CTA never signals: the consumer's bounded wait then reports
+  // the failure instead of reading a half-written tile.
+  if (args.done_counter != nullptr && threadIdx.x == 0 && !*abort_flag) {
+    fence_sys();
+    const int prev = atomicAdd(args.done_counter, 1);
+    if (prev == (int)gridDim.x - 1) {
+      fence_sys();
+      const int v = args.signal_value + (args.epoch != nullptr ? *args.epoch : 0);
+      for (int p = 0; p < args.n_flags; ++p) st_release_sys(args.flags[p], v);
+      *args.done_counter = 0;
+    }
+  }
+}
+
+// ============================================================ host side ===
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr) return nullptr;
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] (row stride `ld` elements), box
+// {64 cols, box_rows rows}, 128-byte swizzle, zero fill out of bounds.
+static int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+template <bool SWIGLU, int BN, int STAGES>
+static cudaError_t launch_variant(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
+                                  int grid, cudaStream_t stream) {
+  using L = GemmSmem<SWIGLU, BN, STAGES>;
+  auto kern = gemm_swapab_kernel<SWIGLU, BN, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kTotal);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, L::kTotal, stream>>>(tw, tx, a);
+  return cudaGetLastError();
+}
+
+int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
+  if (p.args.K % kBK != 0) return 1001;
+  if (p.w_rows_total <= 0) return 1002;
+  if (p.block_n != 64 && p.block_n != 256) return 1003;
+  if (((uintptr_t)p.w & 15) || ((uintptr_t)p.x & 15)) return 1004;
+  if (p.args.f_tiles <= 0) return 1005;
+  CUtensorMap tw, tx;
+  int r = make_tmap(&tw, p.w, p.w_rows_total, p.args.K, p.ld_w, kBM);
+  if (r) return 2000 + r;
+  r = make_tmap(&tx, p.x, p.x_rows, p.args.K, p.ld_x, kBoxRows);
+  if (r) return 3000 + r;
+  GemmArgs a = p.args;
+  a.block_n = p.block_n;
+  int units_hint = p.units_hint > 0 ? p.units_hint : p.num_sms;
+  int grid = units_hint < p.num_sms ? units_hint : p.num_sms;
+  if (grid < 1) grid = 1;
+  cudaError_t e;
+  if (p.swiglu) {
+    if (p.block_n == 64) e = launch_variant<true, 64, 5>(tw, tx, a, grid, stream);
+    else e = launch_variant<true, 256, 3>(tw, tx, a, grid, stream);
+  } else {
+    if (p.block_n == 64) e = launch_variant<false, 64, 8>(tw, tx, a, grid, stream);
+    else e = launch_variant<false, 256, 4>(tw, tx, a, grid, stream);
+  }
+  return e == cudaSuccess ? 0 : 4000 + (int)e;
+}
+
+}  // namespace afd

@@ -1,0 +1,58 @@
+// Host/device interface of the tcgen05 swap-AB GEMM (see gemm_tcgen05.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace afd {
+
+constexpr int kMaxPeers = 8;
+
+struct GemmArgs {
+  int K;                    // reduction length (multiple of 64)
+  int f_tiles;              // output-feature tiles of 128 per group
+  int w_rows_per_group;     // weight rows per group (2I gate_up, H down, N dense)
+  int up_offset;            // SwiGLU: row offset of the up half within a group
+  // row blocks: device list {row_start, n_rows, group, 0} + device count, or
+  // dense mode (blocks == nullptr): ceil(dense_rows / block_n) blocks, group 0
+  const int4* blocks;
+  const int* num_blocks;
+  int dense_rows;
+  int block_n;              // filled by the launcher
+  // epilogue
+  __nv_bfloat16* out;
+  int ld_out;
+  const __nv_bfloat16* residual;   // optional, [rows, ld_res]
+  int ld_res;
+  const float* row_scale;          // optional, per row
+  // fused peer stores + completion flag
+  __nv_bfloat16* peer_out[kMaxPeers];
+  int n_peers;
+  int peer_row_offset;
+  int* flags[kMaxPeers + 1];
+  int n_flags;
+  int signal_value;                // published value = *epoch + signal_value
+  const int* epoch;                // optional device epoch base (CUDA-graph replays)
+  int* done_counter;               // nullptr: no signal
+  int* status;                     // device status word pair (may be nullptr)
+};
+
+struct GemmLaunch {
+  GemmArgs args;
+  const void* w;            // bf16 [w_rows_total, K] (row stride ld_w)
+  int64_t w_rows_total;
+  int64_t ld_w;
+  const void* x;            // bf16 [x_rows, K] (row stride ld_x)
+  int64_t x_rows;
+  int64_t ld_x;
+  bool swiglu;
+  int block_n;              // 64 (decode-sized) or 256
+  int units_hint;           // upper bound on work units (<= 0: unknown)
+  int num_sms;
+};
+
+// Returns 0 on success, a non-zero code describing the failure otherwise.
+int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream);
+
+}  // namespace afd

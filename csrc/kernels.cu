@@ -1,0 +1,476 @@
+// Memory-bound kernels of the Qwen3-MoE step: RMSNorm over a sum of partial
+// hidden states, fused q/k RMSNorm + RoPE + KV-cache append, router
+// softmax/top-k, MoE routing (histogram, prefix sums, row blocks for the
+// grouped GEMM), token gather, weighted combine (+ residual, + peer stores),
+// argmax, and the flag signal / bounded wait kernels.
+//
+// Numerics follow HF Qwen3-MoE: fp32 math with a bf16 rounding at every point
+// where the eager PyTorch code materialises a bf16 tensor.
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace afd {
+
+// ------------------------------------------------------------ helpers ---
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffff, v, o));
+  return v;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < NT / 32) ? red[l] : 0.f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+struct Vec8 {
+  uint4 u;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  unpack_bf16x2(u.x, f[0], f[1]);
+  unpack_bf16x2(u.y, f[2], f[3]);
+  unpack_bf16x2(u.z, f[4], f[5]);
+  unpack_bf16x2(u.w, f[6], f[7]);
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(f[0], f[1]);
+  u.y = pack_bf16x2(f[2], f[3]);
+  u.z = pack_bf16x2(f[4], f[5]);
+  u.w = pack_bf16x2(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// ------------------------------------------------------- sum + RMSNorm ---
+// x = sum_p parts[p][row] (fp32 sum, one bf16 rounding); y = w * bf16(x * rstd)
+// One CTA (256 threads) per row; H % 8 == 0, H <= 256 * 8 * 4.
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) sum_rmsnorm_kernel(SumNormArgs a) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const int H = a.H;
+  constexpr int kMaxChunks = 4;
+  float xv[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * kNormThreads + threadIdx.x) * 8;
+    if (col < H) {
+      float acc[8];
+      load8(a.parts[0] + (size_t)row * a.ld_in + col, acc);
+      for (int p = 1; p < a.n_parts; ++p) {
+        float t[8];
+        load8(a.parts[p] + (size_t)row * a.ld_in + col, t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xv[c][i] = round_bf16(acc[i]);
+        ss += xv[c][i] * xv[c][i];
+      }
+      if (a.x_out != nullptr) store8(a.x_out + (size_t)row * H + col, xv[c]);
+    }
+  }
+  const float tot = block_sum<kNormThreads>(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + a.eps);
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * kNormThreads + threadIdx.x) * 8;
+    if (col < H) {
+      float w[8], y[8];
+      load8(a.weight + col, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(xv[c][i] * rstd);
+      store8(a.y_out + (size_t)row * a.ld_out + col, y);
+    }
+  }
+}
+
+// --------------------------------------- q/k RMSNorm + RoPE + KV append ---
+// One warp per (token, head); heads [0, nq) are queries, [nq, nq+nkv) keys,
+// [nq+nkv, nq+2nkv) values (copied to the cache unchanged). Lane l owns the
+// rotation pairs (j, j + D/2) for j = l + 32 * i.
+__global__ void qk_norm_rope_cache_kernel(QKRopeArgs a) {
+  const int warps_per_block = blockDim.x / 32;
+  const int gw = blockIdx.x * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int n_heads = a.nq + 2 * a.nkv;
+  if (gw >= a.T * n_heads) return;
+  const int t = gw / n_heads;
+  const int h = gw % n_heads;
+  const int D = a.D;
+  const int half = D / 2;
+  const int npair = half / 32;  // 1 (D=64) or 2 (D=128)
+  const int start = *a.start_pos;
+  const int pos = start + t % a.q_len;
+  const int b = a.batch_offset + t / a.q_len;
+  const __nv_bfloat16* src = a.qkv + (size_t)t * a.ld_qkv + (size_t)h * D;
+
+  float lo[2], hi[2];
+  for (int i = 0; i < npair; ++i) {
+    lo[i] = bf16_to_f(src[lane + 32 * i]);
+    hi[i] = bf16_to_f(src[half + lane + 32 * i]);
+  }
+  if (h >= a.nq + a.nkv) {  // value head: straight copy into the cache
+    const int kvh = h - a.nq - a.nkv;
+    __nv_bfloat16* dst = a.v_cache + (((size_t)b * a.nkv + kvh) * a.s_max + pos) * D;
+    for (int i = 0; i < npair; ++i) {
+      dst[lane + 32 * i] = f_to_bf16(lo[i]);
+      dst[half + lane + 32 * i] = f_to_bf16(hi[i]);
+    }
+    return;
+  }
+  const bool is_q = h < a.nq;
+  const __nv_bfloat16* nw = is_q ? a.q_norm : a.k_norm;
+  float ss = 0.f;
+  for (int i = 0; i < npair; ++i) ss += lo[i] * lo[i] + hi[i] * hi[i];
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)D + a.eps);
+  for (int i = 0; i < npair; ++i) {
+    const int j = lane + 32 * i;
+    const float xl = round_bf16(bf16_to_f(nw[j]) * round_bf16(lo[i] * rstd));
+    const float xh = round_bf16(bf16_to_f(nw[half + j]) * round_bf16(hi[i] * rstd));
+    const float c = a.rope[(size_t)pos * D + j];
+    const float s = a.rope[(size_t)pos * D + half + j];
+    // HF: x * cos + rotate_half(x) * sin, each product and the sum in bf16
+    lo[i] = round_bf16(round_bf16(xl * c) + round_bf16(-xh * s));
+    hi[i] = round_bf16(round_bf16(xh * c) + round_bf16(xl * s));
+  }
+  __nv_bfloat16* dst;
+  if (is_q) {
+    dst = a.q_out + ((size_t)t * a.nq + h) * D;
+  } else {
+    const int kvh = h - a.nq;
+    dst = a.k_cache + (((size_t)b * a.nkv + kvh) * a.s_max + pos) * D;
+  }
+  for (int i = 0; i < npair; ++i) {
+    dst[lane + 32 * i] = f_to_bf16(lo[i]);
+    dst[half + lane + 32 * i] = f_to_bf16(hi[i]);
+  }
+}
+
+// ------------------------------------------------------- router top-k ---
+// logits [T, E] bf16 (E <= 256) -> softmax (fp32) -> top-k -> renormalise.
+// One warp per token. Ties resolve to the lower expert index.
+__global__ void router_topk_kernel(RouterArgs a) {
+  const int warps_per_block = blockDim.x / 32;
+  const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= a.T) return;
+  constexpr int kMaxPer = 8;  // E <= 256
+  const int per = (a.E + 31) / 32;
+  float v[kMaxPer];
+  float m = -INFINITY;
+  for (int i = 0; i < per; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < a.E ? bf16_to_f(a.logits[(size_t)t * a.ld_logits + e]) : -INFINITY;
+    m = fmaxf(m, v[i]);
+  }
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = 0; i < per; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < a.E ? __expf(v[i] - m) : 0.f;
+    s += v[i];
+  }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+  for (int i = 0; i < per; ++i) v[i] *= inv;
+  float sel_w[16];
+  int sel_e[16];
+  float wsum = 0.f;
+  for (int k = 0; k < a.top_k; ++k) {
+    float best = -1.f;
+    int be = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (e < a.E && (v[i] > best || (v[i] == best && e < be))) { best = v[i]; be = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffff, best, o);
+      const int oe = __shfl_xor_sync(0xffffffff, be, o);
+      if (ob > best || (ob == best && oe < be)) { best = ob; be = oe; }
+    }
+    sel_w[k] = best;
+    sel_e[k] = be;
+    wsum += best;
+    for (int i = 0; i < per; ++i)
+      if (lane + 32 * i == be) v[i] = -2.f;  // remove from further rounds
+  }
+  if (lane == 0) {
+    const float r = a.renorm ? 1.f / wsum : 1.f;
+    for (int k = 0; k < a.top_k; ++k) {
+      a.ids[(size_t)t * a.top_k + k] = sel_e[k];
+      a.weights[(size_t)t * a.top_k + k] = sel_w[k] * r;
+    }
+  }
+}
+
+// ------------------------------------------------------- MoE routing ---
+// Single CTA. Counts the (token, k) pairs that land on local experts,
+// assigns each a row in expert-sorted order, writes the row's source token
+// and routing weight, the inverse map inv[t*k + j] (-1 if not local), the
+// expert row offsets and the row-block list for the grouped GEMM
+// ({row_start, n_rows, expert, 0}, at most block_n rows per block).
+constexpr int kAlignThreads = 1024;
+constexpr int kMaxLocalExperts = 256;
+
+__global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a) {
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int n = a.T * a.top_k;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = a.ids[i] - a.expert_start;
+    int slot = -1;
+    if (e >= 0 && e < a.n_local) slot = atomicAdd(&cnt[e], 1);
+    a.inv[i] = slot;  // provisional: slot within the expert
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, bacc = 0;
+    for (int e = 0; e < a.n_local; ++e) {
+      off[e] = acc;
+      boff[e] = bacc;
+      acc += cnt[e];
+      bacc += (cnt[e] + a.block_n - 1) / a.block_n;
+    }
+    off[a.n_local] = acc;
+    boff[a.n_local] = bacc;
+    *a.num_blocks = bacc;
+    *a.num_rows = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= a.n_local; e += blockDim.x) a.expert_offsets[e] = off[e];
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) {
+    int b = boff[e];
+    for (int r = 0; r < cnt[e]; r += a.block_n, ++b)
+      a.blocks[b] = make_int4(off[e] + r, min(a.block_n, cnt[e] - r), e, 0);
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int slot = a.inv[i];
+    if (slot < 0) continue;
+    const int e = a.ids[i] - a.expert_start;
+    const int row = off[e] + slot;
+    a.inv[i] = row;
+    a.row_token[row] = i / a.top_k;
+    a.row_weight[row] = a.weights[i];
+  }
+}
+
+// X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
+__global__ void moe_gather_kernel(MoeGatherArgs a) {
+  const int row = blockIdx.x;
+  if (row >= *a.num_rows) return;
+  const int t = a.row_token[row];
+  const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * a.ld_x);
+  uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)row * a.H);
+  for (int i = threadIdx.x; i < a.H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// out[t] = (residual ? h[t] : 0) + sum_j y[inv[t, j]]   (bf16 out, fp32 math)
+// Also stored to up to kMaxPeers peer buffers; the last CTA raises the flags.
+__global__ void __launch_bounds__(kNormThreads) moe_combine_kernel(MoeCombineArgs a) {
+  const int t = blockIdx.x;
+  const int H = a.H;
+  int rows[16];
+  for (int j = 0; j < a.top_k; ++j) rows[j] = a.inv[(size_t)t * a.top_k + j];
+  int seg = -1;
+  for (int s = 0; s < a.n_peers; ++s)
+    if (t >= a.seg_offsets[s] && t < a.seg_offsets[s + 1]) seg = s;
+  for (int col = threadIdx.x * 8; col < H; col += kNormThreads * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < a.top_k; ++j) {
+      if (rows[j] < 0) continue;
+      float y[8];
+      load8(a.y + (size_t)rows[j] * H + col, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += y[i];
+    }
+    if (a.residual != nullptr) {
+      float r[8];
+      load8(a.residual + (size_t)t * a.ld_res + col, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = round_bf16(acc[i]) + r[i];
+    }
+    uint4 u;
+    u.x = pack_bf16x2(acc[0], acc[1]);
+    u.y = pack_bf16x2(acc[2], acc[3]);
+    u.z = pack_bf16x2(acc[4], acc[5]);
+    u.w = pack_bf16x2(acc[6], acc[7]);
+    if (a.out != nullptr) *reinterpret_cast<uint4*>(a.out + (size_t)t * a.ld_out + col) = u;
+    if (seg >= 0)
+      *reinterpret_cast<uint4*>(a.peer_out[seg] +
+                                (size_t)(t - a.seg_offsets[seg] + a.peer_row_offset) * H + col) = u;
+  }
+  if (a.done_counter != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      fence_sys();
+      const int prev = atomicAdd(a.done_counter, 1);
+      if (prev == (int)gridDim.x - 1) {
+        fence_sys();
+        const int v = a.signal_value + (a.epoch != nullptr ? *a.epoch : 0);
+        for (int p = 0; p < a.n_flags; ++p) st_release_sys(a.flags[p], v);
+        *a.done_counter = 0;
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------- argmax ---
+// One CTA per row; first index of the maximum (torch.argmax semantics).
+__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logits, int V, int ld,
+                                                      int64_t* out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* p = logits + (size_t)row * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = bf16_to_f(p[i]);
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffff, best, o);
+    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) { sv[w] = best; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x / 32;
+    best = l < nw ? sv[l] : -INFINITY;
+    bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffff, best, o);
+      const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (l == 0) out[row] = bi;
+  }
+}
+
+// ---------------------------------------------------------------- flags ---
+__global__ void signal_flags_kernel(FlagArgs a) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    fence_sys();
+    const int v = a.value + (a.epoch != nullptr ? *a.epoch : 0);
+    for (int i = 0; i < a.n; ++i) st_release_sys(a.flags[i], v);
+  }
+}
+
+// Waits until every flag >= value; bounded by timeout_ns (status on expiry).
+__global__ void wait_flags_kernel(FlagArgs a) {
+  if (threadIdx.x < a.n && blockIdx.x == 0) {
+    const int v = a.value + (a.epoch != nullptr ? *a.epoch : 0);
+    wait_flag_geq(a.flags[threadIdx.x], v, a.status, 100 + threadIdx.x, a.timeout_ns);
+  }
+  __syncthreads();
+}
+
+// Increments a device counter (the step epoch) by `by`.
+__global__ void add_i32_kernel(int* p, int by) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *p += by;
+}
+
+// ============================================================== launchers ===
+int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s) {
+  if (a.H % 8 != 0 || a.H > kNormThreads * 8 * 4 || a.n_parts < 1 || a.n_parts > kMaxParts)
+    return 1;
+  if (rows == 0) return 0;
+  sum_rmsnorm_kernel<<<rows, kNormThreads, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s) {
+  if (a.D % 64 != 0 || a.D > 128) return 1;
+  const int warps = a.T * (a.nq + 2 * a.nkv);
+  if (warps == 0) return 0;
+  const int wpb = 8;
+  qk_norm_rope_cache_kernel<<<(warps + wpb - 1) / wpb, wpb * 32, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_router_topk(const RouterArgs& a, cudaStream_t s) {
+  if (a.E > 256 || a.top_k > 16) return 1;
+  if (a.T == 0) return 0;
+  const int wpb = 8;
+  router_topk_kernel<<<(a.T + wpb - 1) / wpb, wpb * 32, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s) {
+  if (a.n_local > kMaxLocalExperts || a.block_n <= 0) return 1;
+  moe_align_kernel<<<1, kAlignThreads, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s) {
+  if (a.H % 8 != 0) return 1;
+  if (max_rows == 0) return 0;
+  moe_gather_kernel<<<max_rows, 256, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s) {
+  if (a.H % 8 != 0 || a.top_k > 16) return 1;
+  if (T == 0) return 0;
+  moe_combine_kernel<<<T, kNormThreads, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
+                  cudaStream_t s) {
+  if (rows == 0) return 0;
+  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, ld, out);
+  return (int)cudaGetLastError();
+}
+
+int launch_signal_flags(const FlagArgs& a, cudaStream_t s) {
+  signal_flags_kernel<<<1, 32, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_wait_flags(const FlagArgs& a, cudaStream_t s) {
+  if (a.n > 32) return 1;
+  wait_flags_kernel<<<1, 32, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_add_i32(int* p, int by, cudaStream_t s) {
+  add_i32_kernel<<<1, 32, 0, s>>>(p, by);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace afd

@@ -1,0 +1,134 @@
+// Argument structs and launchers of the memory-bound kernels (kernels.cu)
+// and the attention kernels (attention.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace afd {
+
+constexpr int kMaxParts = 8;
+constexpr int kMaxFlagPeers = 9;
+
+struct SumNormArgs {
+  const __nv_bfloat16* parts[kMaxParts];  // each [rows, ld_in]
+  int n_parts;
+  int ld_in;
+  const __nv_bfloat16* weight;            // [H]
+  __nv_bfloat16* x_out;                   // optional [rows, H]: the summed input
+  __nv_bfloat16* y_out;                   // [rows, ld_out]
+  int ld_out;
+  int H;
+  float eps;
+};
+
+struct QKRopeArgs {
+  const __nv_bfloat16* qkv;   // [T, ld_qkv]  q | k | v
+  int ld_qkv;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* rope;          // [max_pos, D]: cos | sin (half-dim each)
+  __nv_bfloat16* q_out;       // [T, nq, D]
+  __nv_bfloat16* k_cache;     // [B_max, nkv, s_max, D]
+  __nv_bfloat16* v_cache;
+  const int* start_pos;       // device scalar
+  int T, q_len, batch_offset, nq, nkv, D, s_max;
+  float eps;
+};
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;     // [B, nq, D]
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;         // [B, nq, D]
+  float* o_part;              // split workspace [B, nq, nsplit, D]
+  float* ml_part;             // [B, nq, nsplit, 2]
+  const int* start_pos;       // position of the query token (kv_len = start + 1)
+  int batch_offset, nq, nkv, D, s_max;
+};
+
+struct PrefillAttnArgs {
+  const __nv_bfloat16* q;     // [B * q_len, nq, D]
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;         // [B * q_len, nq, D]
+  const int* start_pos;
+  int q_len, batch_offset, nq, nkv, D, s_max;
+};
+
+struct RouterArgs {
+  const __nv_bfloat16* logits;  // [T, ld_logits]
+  int ld_logits;
+  int32_t* ids;                 // [T, top_k]
+  float* weights;               // [T, top_k]
+  int T, E, top_k, renorm;
+};
+
+struct MoeAlignArgs {
+  const int32_t* ids;           // [T, top_k] global expert ids
+  const float* weights;         // [T, top_k]
+  int T, top_k, expert_start, n_local, block_n;
+  int32_t* inv;                 // [T * top_k]: sorted row or -1
+  int32_t* row_token;           // [T * top_k]
+  float* row_weight;            // [T * top_k]
+  int32_t* expert_offsets;      // [n_local + 1]
+  int4* blocks;                 // [max blocks]
+  int32_t* num_blocks;          // device scalar
+  int32_t* num_rows;            // device scalar
+};
+
+struct MoeGatherArgs {
+  const __nv_bfloat16* x;
+  int ld_x;
+  const int32_t* row_token;
+  const int32_t* num_rows;
+  __nv_bfloat16* out;           // [rows, H]
+  int H;
+};
+
+struct MoeCombineArgs {
+  const __nv_bfloat16* y;       // [rows, H] weighted expert outputs
+  const int32_t* inv;           // [T * top_k]
+  const __nv_bfloat16* residual;  // optional [T, ld_res]
+  int ld_res;
+  __nv_bfloat16* out;           // optional [T, ld_out]
+  int ld_out;
+  int H, top_k;
+  // F2A stores: token t of segment s (seg_offsets[s] <= t < seg_offsets[s+1])
+  // goes to row t - seg_offsets[s] + peer_row_offset of peer_out[s]
+  __nv_bfloat16* peer_out[8];
+  int seg_offsets[9];
+  int n_peers;
+  int peer_row_offset;
+  int* flags[kMaxFlagPeers];
+  int n_flags;
+  int signal_value;
+  const int* epoch;
+  int* done_counter;
+};
+
+struct FlagArgs {
+  int* flags[32];
+  int n;
+  int value;            // target = *epoch + value (epoch optional)
+  const int* epoch;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s);
+int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s);
+int launch_router_topk(const RouterArgs& a, cudaStream_t s);
+int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s);
+int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s);
+int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s);
+int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
+                  cudaStream_t s);
+int launch_signal_flags(const FlagArgs& a, cudaStream_t s);
+int launch_wait_flags(const FlagArgs& a, cudaStream_t s);
+int launch_add_i32(int* p, int by, cudaStream_t s);
+int launch_decode_attention(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s);
+int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s);
+
+}  // namespace afd

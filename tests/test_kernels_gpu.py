@@ -1,0 +1,180 @@
+"""sm_100a kernels against PyTorch fp32 statements of the same ops."""
+
+import math
+
+import pytest
+import torch
+
+from afd_demo_b200 import ops
+from afd_demo_b200.ops import torch_ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-12))
+
+
+def _randn(*s, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*s, generator=g, device=DEV) * scale).to(torch.bfloat16)
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ops.ext()  # must load: no silent fallback
+
+
+@pytest.mark.parametrize("T", [1, 5, 32, 37, 64, 100, 300, 513])
+@pytest.mark.parametrize("N,K", [(256, 2048), (5120, 2048), (2048, 4096), (128, 2048)])
+def test_dense_gemm(T, N, K):
+    x = _randn(T, K, seed=1)
+    w = _randn(N, K, scale=0.02, seed=2)
+    ref = x.float() @ w.float().t()
+    out = ops.linear(x, w)
+    torch.cuda.synchronize()
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("T", [3, 64, 200])
+def test_dense_gemm_residual(T):
+    K, N = 4096, 2048
+    x = _randn(T, K, seed=3)
+    w = _randn(N, K, scale=0.02, seed=4)
+    r = _randn(T, N, seed=5)
+    ref = x.float() @ w.float().t() + r.float()
+    out = ops.linear(x, w, residual=r)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 128, 8), (16, 128, 8), (64, 128, 8), (333, 128, 8),
+                                   (2048, 128, 8), (40, 32, 8)])
+def test_moe_experts(T, E, k):
+    H, I = 2048, 768
+    torch.manual_seed(0)
+    xn = _randn(T, H, seed=6)
+    wgu = _randn(E, 2 * I, H, scale=0.02, seed=7)
+    wd = _randn(E, H, I, scale=0.02, seed=8)
+    logits = torch.randn(T, 128, device=DEV)
+    probs = logits.softmax(-1)
+    w, ids = probs.topk(k, -1)
+    w = (w / w.sum(-1, keepdim=True)).float()
+    ids = ids.to(torch.int32)
+    start = 0 if E == 128 else 32  # expert-parallel slice [32, 64)
+    ref = torch_ref.moe_experts(xn, ids, w, wgu, wd, start)
+    out = ops.moe_experts(xn, ids, w, wgu, wd, start)
+    assert _rel(out, ref) < 2e-2
+
+
+def test_moe_residual_and_ep_partials_sum():
+    T, H, I, E = 48, 2048, 768, 128
+    xn = _randn(T, H, seed=9)
+    h = _randn(T, H, seed=10)
+    wgu = _randn(E, 2 * I, H, scale=0.02, seed=11)
+    wd = _randn(E, H, I, scale=0.02, seed=12)
+    w, ids = torch.rand(T, 128, device=DEV).softmax(-1).topk(8, -1)
+    w = (w / w.sum(-1, keepdim=True)).float()
+    ids = ids.to(torch.int32)
+    full = ops.moe_experts(xn, ids, w, wgu, wd, 0, residual=h).float()
+    parts = [ops.moe_experts(xn, ids, w, wgu[e0:e0 + 32], wd[e0:e0 + 32], e0,
+                             residual=h if e0 == 0 else None).float() for e0 in (0, 32, 64, 96)]
+    assert _rel(sum(parts), full) < 1e-2
+
+
+@pytest.mark.parametrize("parts", [1, 2, 4])
+def test_sum_rmsnorm(parts):
+    T, H = 37, 2048
+    xs = [_randn(T, H, seed=20 + i) for i in range(parts)]
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    x_ref, y_ref = torch_ref.sum_rmsnorm(xs, w, 1e-6)
+    x, y = ops.sum_rmsnorm(xs, w, 1e-6)
+    assert _rel(x, x_ref) < 5e-3
+    assert _rel(y, y_ref) < 1e-2
+
+
+@pytest.mark.parametrize("q_len,start", [(1, 0), (1, 200), (7, 0), (64, 0), (100, 30)])
+def test_qk_norm_rope_cache(q_len, start):
+    B, nq, nkv, D, S = 3, 32, 4, 128, 512
+    T = B * q_len
+    qkv = _randn(T, (nq + 2 * nkv) * D, seed=30)
+    qn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    rope = ops.rope_table(S, D, 1e6, DEV)
+    kc = torch.zeros(4, nkv, S, D, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    q_ref = torch_ref.qk_norm_rope_cache(qkv.float(), qn.float(), kn.float(), rope, kc2, vc2, 1,
+                                         q_len, start, nq, nkv, 1e-6)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    q = ops.qk_norm_rope_cache(qkv, qn, kn, rope, kc, vc, start, pos, q_len, 1, nq, nkv, 1e-6)
+    assert _rel(q, q_ref) < 1e-2
+    sl = slice(start, start + q_len)
+    assert _rel(kc[1:1 + B, :, sl], kc2[1:1 + B, :, sl]) < 1e-2
+    assert torch.equal(vc[1:1 + B, :, sl], vc2[1:1 + B, :, sl])
+
+
+@pytest.mark.parametrize("B,kv_len", [(1, 1), (3, 77), (16, 276), (64, 300), (2, 2049)])
+def test_decode_attention(B, kv_len):
+    nq, nkv, D, S = 32, 4, 128, 2304
+    kc = _randn(B + 1, nkv, S, D, seed=40)
+    vc = _randn(B + 1, nkv, S, D, seed=41)
+    q = _randn(B, nq, D, seed=42)
+    start = kv_len - 1
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 1, 1, start)
+    out = ops.attention(q, kc, vc, 1, 1, start, pos)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("B,q_len,start", [(1, 16, 0), (2, 128, 0), (3, 100, 0), (2, 64, 40),
+                                           (1, 512, 0)])
+def test_prefill_attention(B, q_len, start):
+    nq, nkv, D, S = 32, 4, 128, 1024
+    kc = _randn(B, nkv, S, D, seed=50)
+    vc = _randn(B, nkv, S, D, seed=51)
+    q = _randn(B * q_len, nq, D, seed=52)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, q_len, start)
+    out = ops.attention(q, kc, vc, 0, q_len, start, pos)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("T", [1, 9, 256])
+def test_router_topk(T):
+    H, E = 2048, 128
+    h = _randn(T, H, seed=60)
+    pw = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    wr = _randn(E, H, scale=0.02, seed=61)
+    xn_r, ids_r, w_r = torch_ref.router_topk(h, pw, wr, 8, 1e-6)
+    xn, ids, w = ops.router_topk(h, pw, wr, 8, 1e-6)
+    assert _rel(xn, xn_r) < 1e-2
+    # compare as (expert -> weight) maps: near-ties may swap order
+    dense = torch.zeros(T, E, device=DEV).scatter_(1, ids.long(), w)
+    dense_r = torch.zeros(T, E, device=DEV).scatter_(1, ids_r.long(), w_r)
+    assert (dense - dense_r).abs().max() < 2e-2
+
+
+def test_argmax():
+    x = _randn(5, 151936, seed=70)
+    x[2, 12345] = 100.0
+    assert torch.equal(ops.argmax(x), x.float().argmax(-1))
+
+
+def test_flags_roundtrip_and_timeout():
+    C = ops.ext()
+    buf = C.ipc_alloc(4096, torch.cuda.current_device())
+    base = buf.data_ptr()
+    status = torch.zeros(2, dtype=torch.int32, device=DEV)
+    C.signal_flags([base, base + 4], 7, None)
+    C.wait_flags([base, base + 4], 7, status, 1_000_000_000, None)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 0
+    # a flag nobody raises: the bounded wait gives up and reports
+    C.wait_flags([base + 8], 1, status, 50_000_000, None)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 2
