@@ -54,8 +54,11 @@ def parse():
     p.add_argument("--comm-impl", default="auto", choices=["auto", "fused", "nccl"])
     p.add_argument("--no-serial", action="store_true", help="skip the serial comparison")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--prefill-batch", type=int, default=None,
-                   help="prefill TTFT batch (default: the decode batch)")
+    p.add_argument("--profile", type=int, default=0, metavar="STEPS",
+                   help="profiling run: prefill, then STEPS eager decode steps (DBO, cross-"
+                        "layer); the last one inside the NVTX range 'profile_step'; no JSON")
+    p.add_argument("--layers", type=int, default=None,
+                   help="override the layer count (profiling small cases only)")
     return p.parse_args()
 
 
@@ -138,7 +141,14 @@ def main():
                                      backend="nccl", timeout_s=300))
     B = args.batch or args.batch_per_gpu * args.gpus
     S, T = args.seq, args.tokens
-    max_seq = S + max(T, args.warmup + args.steps + 2) + 8
+    max_seq = S + max(T, args.warmup + args.steps + 2, args.profile + 2) + 8
+    if args.layers is not None:
+        from afd_demo_b200.config import PRESETS
+        cfg = PRESETS[args.model]()
+        cfg.num_hidden_layers = args.layers
+        from afd_demo_b200 import config as _cfgmod
+        _cfgmod.PRESETS["_bench"] = lambda: cfg
+        args.model = "_bench"
     model = DisaggregatedQwenModel.from_pretrained(
         args.model, device=f"cuda:{local}", dtype=torch.bfloat16, max_seq_len=max_seq,
         max_batch_size=B, comm_impl=args.comm_impl, random_init=True, seed=0,
@@ -148,6 +158,22 @@ def main():
     ids_host = torch.randint(0, V, (B, S), generator=g).pin_memory()
     ids = ids_host.to(f"cuda:{local}", non_blocking=True)
     torch.cuda.synchronize()
+
+    if args.profile:
+        model.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
+        tok = torch.zeros(B, 1, dtype=torch.long, device=f"cuda:{local}")
+        for i in range(args.profile):
+            if i == args.profile - 1:
+                torch.cuda.synchronize()
+                torch.cuda.nvtx.range_push("profile_step")
+            model.run_forward(tok, "dbo", 2, crosslayer=True)
+            if i == args.profile - 1:
+                torch.cuda.synchronize()
+                torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        ctx.barrier()
+        ctx.cleanup()
+        return
 
     def bar():
         torch.cuda.synchronize()
