@@ -148,11 +148,21 @@ def small_qwen3_moe() -> ModelConfig:
     return ModelConfig(num_hidden_layers=2, vocab_size=4096)
 
 
+def mini_qwen3_moe() -> ModelConfig:
+    """A fast GPU-test model that exercises every sm_100a kernel path:
+    hidden 1024, 2 layers, 16q/2kv heads x 64, 128 experts top-8,
+    moe_intermediate 256, vocab 2048."""
+    return ModelConfig(vocab_size=2048, hidden_size=1024, num_hidden_layers=2,
+                       num_attention_heads=16, num_key_value_heads=2, head_dim=64,
+                       moe_intermediate_size=256, intermediate_size=2048)
+
+
 PRESETS = {
     "qwen3-30b-a3b": qwen3_30b_a3b,
     "Qwen/Qwen3-30B-A3B": qwen3_30b_a3b,
     "tiny": tiny_qwen3_moe,
     "small": small_qwen3_moe,
+    "mini": mini_qwen3_moe,
 }
 
 

@@ -240,7 +240,8 @@ class DisaggregatedQwenModel:
         streams, transport waits and signals, cache position update) is
         captured once per (batch, schedule) and replayed."""
         B = tokens.shape[0]
-        if not use_cuda_graph or self.device.type != "cuda":
+        # the NCCL baseline keeps host-side work handles: it runs eagerly
+        if not use_cuda_graph or self.device.type != "cuda" or self.comm_impl == "nccl":
             return self.run_forward(tokens, mode, num_mb, crosslayer)
         key = (B, mode, num_mb, crosslayer)
         g = self._graphs.get(key)

@@ -1,0 +1,104 @@
+"""Multi-process runs on CPU with gloo: 1 attention + 1 FFN rank and
+2 attention (data parallel) + 2 FFN (expert parallel) ranks must generate the
+same greedy tokens as the single-process model, in serial, DBO and
+cross-layer DBO schedules (the tiny Qwen3-MoE oracle configuration)."""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from afd_demo_b200.config import tiny_qwen3_moe
+from afd_demo_b200.models.weights import (random_attention_weights, random_ffn_weights,
+                                          save_checkpoint)
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.fixture(scope="module")
+def ckpt():
+    d = tempfile.mkdtemp(prefix="afd_tiny_")
+    cfg = tiny_qwen3_moe()
+    save_checkpoint(d, cfg, random_attention_weights(cfg, 0, "cpu", torch.float32),
+                    random_ffn_weights(cfg, None, 0, "cpu", torch.float32))
+    return d
+
+
+def _ids():
+    return torch.randint(0, 1024, (4, 24), generator=torch.Generator().manual_seed(3))
+
+
+def _worker(rank, world, port, ckpt, modes, out_dir):
+    import torch
+
+    from afd_demo_b200.models import DisaggregatedQwenModel
+    from afd_demo_b200.parallel.dist import DistributedConfig, get_distributed_context
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cpu")
+    ctx = get_distributed_context()
+    ctx.initialize(DistributedConfig(world_size=world, rank=rank, backend="gloo",
+                                     master_addr="127.0.0.1", master_port=str(port),
+                                     timeout_s=120))
+    m = DisaggregatedQwenModel.from_pretrained(ckpt, device="cpu", dtype=torch.float32,
+                                               max_seq_len=64, max_batch_size=4,
+                                               comm_impl="nccl")
+    res = {}
+    for name, kw in modes.items():
+        res[name] = m.generate(_ids(), max_new_tokens=5, do_sample=False, **kw)
+    if ctx.is_attention_node:
+        torch.save(res, os.path.join(out_dir, f"attn{ctx.attn_index}.pt"))
+    ctx.barrier()
+    ctx.cleanup()
+
+
+MODES = {
+    "serial": dict(use_decode_dbo=False),
+    "dbo": dict(use_decode_dbo=True, prefill_mode="dbo", num_prefill_micro_batches=2),
+    "xl": dict(use_decode_dbo=True, decode_use_crosslayer=True),
+}
+
+
+def _reference(ckpt):
+    from afd_demo_b200.models import DisaggregatedQwenModel
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cpu")
+    m = DisaggregatedQwenModel.from_pretrained(ckpt, device="cpu", dtype=torch.float32,
+                                               max_seq_len=64, max_batch_size=4)
+    return m.generate(_ids(), max_new_tokens=5, do_sample=False, use_decode_dbo=False)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_matches_single_process(ckpt, world):
+    want = _reference(ckpt)
+    out = tempfile.mkdtemp(prefix="afd_out_")
+    mp.start_processes(_worker, args=(world, _free_port(), ckpt, MODES, out), nprocs=world,
+                       join=True, start_method="spawn")
+    n_attn = world // 2
+    for name in MODES:
+        got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))[name]
+                         for a in range(n_attn)])
+        assert torch.equal(got, want), (world, name)
+
+
+def test_single_process_schedules_agree(ckpt):
+    from afd_demo_b200.models import DisaggregatedQwenModel
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cpu")
+    m = DisaggregatedQwenModel.from_pretrained(ckpt, device="cpu", dtype=torch.float32,
+                                               max_seq_len=64, max_batch_size=4)
+    outs = {k: m.generate(_ids(), max_new_tokens=5, do_sample=False, **kw)
+            for k, kw in MODES.items()}
+    assert torch.equal(outs["serial"], outs["dbo"])
+    assert torch.equal(outs["serial"], outs["xl"])
