@@ -138,7 +138,9 @@ def main():
     torch.cuda.set_device(local)
     ctx = get_distributed_context()
     ctx.initialize(DistributedConfig(world_size=world, rank=rank, local_rank=local,
-                                     backend="nccl", timeout_s=300))
+                                     backend="nccl", timeout_s=120,
+                                     master_addr=os.environ.get("MASTER_ADDR", "127.0.0.1"),
+                                     master_port=os.environ.get("MASTER_PORT", "29500")))
     B = args.batch or args.batch_per_gpu * args.gpus
     S, T = args.seq, args.tokens
     max_seq = S + max(T, args.warmup + args.steps + 2, args.profile + 2) + 8
