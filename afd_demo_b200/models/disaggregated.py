@@ -317,7 +317,7 @@ class DisaggregatedQwenModel:
                     next_tok = pinned.to(self.device, non_blocking=True)  # H2D: next input
                 r = self.local_batch(B)
                 step_in[r.start:r.stop] = next_tok
-            if sched is not None and step == sched.timing_step:
+            if sched is not None:  # timed runs stay eager; step 1 records events
                 logits = sched.forward_decode_dbo(step_in)
             else:
                 logits = self.decode_step(step_in, dec_mode, dec_mb, decode_use_crosslayer,

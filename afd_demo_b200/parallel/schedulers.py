@@ -193,10 +193,11 @@ class DecodeDBOScheduler:
         if track:
             devmod.synchronize()
             self._timing_data = _finish(tr, m.ctx)
-            td = self._timing_data
-            td.timed_decode_step = self.timing_step
-            td.timed_decode_step_base = "0-based"
-            td.timed_decode_step_note = "step 0 skipped to avoid warmup/cold-start timing"
+            for td in (self._timing_data, getattr(self._timing_data, "ffn_timing", None)):
+                if td is not None:
+                    td.timed_decode_step = self.timing_step
+                    td.timed_decode_step_base = "0-based"
+                    td.timed_decode_step_note = "step 0 skipped to avoid warmup/cold-start timing"
         self.stats = DecodeDBOStats(num_tokens=B, num_layers=m.num_layers,
                                     total_time=time.perf_counter() - t0)
         if self._timing_data is not None and track:
