@@ -21,7 +21,7 @@ _C = None
 # call launches (decode attention adds a merge kernel when split).
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
-                 "argmax", "signal_flags", "wait_flags", "add_i32"}
+                 "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy"}
 
 
 class LaunchCounter:
@@ -115,7 +115,15 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 # ------------------------------------------------------------------- GEMM --
 def _block_n(rows: int) -> int:
-    return 64 if rows <= 64 else 256
+    """Token rows per GEMM tile: the smallest of 64/128/256 that covers the
+    rows (decode), 256 for large dense GEMMs (prefill)."""
+    return 64 if rows <= 64 else (128 if rows <= 128 else 256)
+
+
+def _moe_block_n(rows: int) -> int:
+    """Row-block size of the grouped expert GEMMs: 64 for decode-sized
+    batches, 128 otherwise (keeps two TMEM accumulators for SwiGLU)."""
+    return 64 if rows <= 64 else 128
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
@@ -243,7 +251,7 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     E_loc, I2, _ = w_gate_up.shape
     I = I2 // 2
     k = ids.shape[1]
-    bn = _block_n(T)
+    bn = _moe_block_n(T)
     if ws is None:
         ws = MoEWorkspace(T, k, E_loc, H, I, bn, xn.device, xn.dtype)
     C = ext()

@@ -316,6 +316,24 @@ void wait_flags(std::vector<int64_t> flags, int64_t value, const c10::optional<a
            "wait_flags");
 }
 
+void peer_copy(const at::Tensor& src, std::vector<int64_t> dst, std::vector<int64_t> flags,
+               int64_t signal_value, const c10::optional<at::Tensor>& done_counter,
+               const c10::optional<at::Tensor>& epoch, int64_t grid) {
+  TORCH_CHECK(dst.size() <= 8 && flags.size() == dst.size(), "1..8 peers with one flag each");
+  afd::PeerCopyArgs a{};
+  a.src = src.data_ptr();
+  for (size_t i = 0; i < dst.size(); ++i) {
+    a.dst[i] = reinterpret_cast<void*>(dst[i]);
+    a.flags[i] = reinterpret_cast<int*>(flags[i]);
+  }
+  a.n_peers = (int)dst.size();
+  a.bytes = (size_t)src.numel() * src.element_size();
+  a.signal_value = (int)signal_value;
+  a.epoch = opt_ptr<const int>(epoch);
+  a.done_counter = opt_ptr<int>(done_counter);
+  check_rc(afd::launch_peer_copy(a, (int)grid, cur_stream()), "peer_copy");
+}
+
 void add_i32(at::Tensor& t, int64_t by) {
   check_rc(afd::launch_add_i32(t.data_ptr<int>(), (int)by, cur_stream()), "add_i32");
 }
@@ -373,6 +391,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("signal_flags", &signal_flags);
   m.def("wait_flags", &wait_flags);
   m.def("add_i32", &add_i32);
+  m.def("peer_copy", &peer_copy);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

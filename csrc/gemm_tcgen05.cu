@@ -43,16 +43,26 @@ constexpr int kBM = 128;        // output features per tile (MMA M)
 constexpr int kBK = 64;         // K per pipeline stage (one 128-byte swizzle atom)
 constexpr int kBoxRows = 32;    // token rows per TMA box
 constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
 
+// Two TMEM accumulator slots let the MMA warp start tile i+1 while the
+// epilogue drains tile i; SwiGLU tiles hold a gate and an up accumulator, so
+// BN = 256 SwiGLU keeps a single slot (512 columns).
 template <bool SWIGLU, int BN, int STAGES>
 struct GemmSmem {
-  static constexpr int kABytes = kBM * kBK * 2;             // 16 KB
+  static constexpr int kABytes = kBM * kBK * 2;              // 16 KB
   static constexpr int kBBytes = BN * kBK * 2;               // BN x 128 B
   static constexpr int kStageBytes = kABytes * (SWIGLU ? 2 : 1) + kBBytes;
   static constexpr int kDataBytes = kStageBytes * STAGES;
-  static constexpr int kTotal = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int kTmemCols = SWIGLU ? 512 : (BN <= 128 ? 128 : 256);
-  static constexpr int kUpCol = SWIGLU ? 256 : 0;
+  static constexpr int kSlots = (SWIGLU && BN > 128) ? 1 : 2;
+  static constexpr int kAccCols = BN;                        // fp32 columns per accumulator
+  static constexpr int kSlotCols = kAccCols * (SWIGLU ? 2 : 1);
+  static constexpr int kUsedCols = kSlotCols * kSlots;
+  static constexpr int kTmemCols = kUsedCols <= 32 ? 32 : kUsedCols <= 64 ? 64
+                                   : kUsedCols <= 128 ? 128 : kUsedCols <= 256 ? 256 : 512;
+  // epilogue staging: per warp 16 rows x 32 features bf16
+  static constexpr int kStageOutBytes = kEpiWarps * 16 * 32 * 2;
+  static constexpr int kTotal = kDataBytes + kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ int4 unit_block(const GemmArgs& a, int b) {
@@ -75,11 +85,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kDataBytes);
+  __nv_bfloat16* stage_out = reinterpret_cast<__nv_bfloat16*>(smem + L::kDataBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kDataBytes + L::kStageOutBytes);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
-  uint64_t* tempty_bar = tfull_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 1);
+  uint64_t* tfull_bar = empty_bar + STAGES;      // [kSlots]
+  uint64_t* tempty_bar = tfull_bar + 2;          // [kSlots]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -90,8 +101,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, 4);  // one arrival per epilogue warp
+    for (int s = 0; s < L::kSlots; ++s) {
+      mbar_init(&tfull_bar[s], 1);
+      mbar_init(&tempty_bar[s], kEpiWarps);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_w);
@@ -150,14 +163,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t tphase = 0;
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      int t = 0;  // local tile counter
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
         const int4 blk = unit_block(args, u / args.f_tiles);
         const int n_mma = max(32, ((blk.y + 31) / 32) * 32);
         const uint32_t idesc = umma_idesc_bf16(kBM, n_mma);
-        // the epilogue must have drained the previous accumulator
-        if (!mbar_wait(tempty_bar, tphase ^ 1, abort_flag, args.status, 20)) break;
+        const int slot = t % L::kSlots;
+        const uint32_t tpar = (uint32_t)((t / L::kSlots) & 1);
+        // the epilogue must have drained this slot's previous accumulator
+        if (!mbar_wait(&tempty_bar[slot], tpar ^ 1, abort_flag, args.status, 20)) break;
         tc_fence_after();
+        const uint32_t d_gate = tmem_base + slot * L::kSlotCols;
         bool ok = true;
         for (int k = 0; k < k_iters; ++k) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, 21)) { ok = false; break; }
@@ -167,63 +183,93 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
-            umma_bf16(tmem_base, umma_desc_sw128(sa + kk * 32), bdesc, idesc,
-                      (k | kk) != 0);
+            umma_bf16(d_gate, umma_desc_sw128(sa + kk * 32), bdesc, idesc, (k | kk) != 0);
             if (SWIGLU)
-              umma_bf16(tmem_base + L::kUpCol, umma_desc_sw128(sa + L::kABytes + kk * 32), bdesc,
+              umma_bf16(d_gate + L::kAccCols, umma_desc_sw128(sa + L::kABytes + kk * 32), bdesc,
                         idesc, (k | kk) != 0);
           }
           umma_commit(&empty_bar[stage]);  // smem stage free once these MMAs retire
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit(tfull_bar);  // accumulator ready for the epilogue
-        tphase ^= 1;
+        umma_commit(&tfull_bar[slot]);  // accumulator ready for the epilogue
       }
     }
   } else {
     // --------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int f_local = q * 32 + lane;
-    uint32_t tphase = 0;
-    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+    // TMEM lane quarter q holds features q*32..q*32+31 of the tile. Each
+    // 16-column chunk is rounded to bf16 in registers, transposed through a
+    // warp-private smem tile [16 rows][32 features], and written as 16-byte
+    // row vectors (4 lanes per row), with the residual read the same way.
+    const int q = warp & 3;
+    __nv_bfloat16* st = stage_out + (warp - 2) * 16 * 32;
+    int t = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
       const int4 blk = unit_block(args, u / args.f_tiles);
       const int ft = u % args.f_tiles;
-      const int f = ft * kBM + f_local;
-      if (!mbar_wait(tfull_bar, tphase, abort_flag, args.status, 30)) break;
-      tphase ^= 1;
+      const int slot = t % L::kSlots;
+      const uint32_t tpar = (uint32_t)((t / L::kSlots) & 1);
+      if (!mbar_wait(&tfull_bar[slot], tpar, abort_flag, args.status, 30)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16);
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + slot * L::kSlotCols;
+      const int f_base = ft * kBM + q * 32;
       for (int c = 0; c < blk.y; c += 16) {
         float acc[16];
         tmem_ld16(t_row + c, acc);
         if (SWIGLU) {
           float up[16];
-          tmem_ld16(t_row + L::kUpCol + c, up);
+          tmem_ld16(t_row + L::kAccCols + c, up);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            // HF rounds gate/up to bf16 before the activation
+            // HF rounds gate/up to bf16 before the activation and the product
             const float g = round_bf16(acc[j]);
             const float s = g / (1.0f + __expf(-g));
             acc[j] = round_bf16(s) * round_bf16(up[j]);
           }
+        } else if (args.row_scale != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int r = min(c + j, blk.y - 1);
+            acc[j] = round_bf16(acc[j]) * args.row_scale[blk.x + r];
+          }
         }
-        const int jmax = min(16, blk.y - c);
-        for (int j = 0; j < jmax; ++j) {
-          const int row = blk.x + c + j;
-          float v = acc[j];
-          if (args.row_scale != nullptr) v = round_bf16(v) * args.row_scale[row];
-          if (args.residual != nullptr)
-            v = round_bf16(v) + bf16_to_f(args.residual[(size_t)row * args.ld_res + f]);
-          const __nv_bfloat16 o = f_to_bf16(v);
-          args.out[(size_t)row * args.ld_out + f] = o;
-          for (int p = 0; p < args.n_peers; ++p)
-            args.peer_out[p][(size_t)(row + args.peer_row_offset) * args.ld_out + f] = o;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) st[j * 32 + lane] = f_to_bf16(acc[j]);
+        __syncwarp();
+        const int g8 = (lane & 3) * 8;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = (lane >> 2) + 8 * h;
+          if (c + j < blk.y) {
+            const int row = blk.x + c + j;
+            uint4 v = *reinterpret_cast<const uint4*>(st + j * 32 + g8);
+            const int col = f_base + g8;
+            if (args.residual != nullptr) {
+              const uint4 r = *reinterpret_cast<const uint4*>(
+                  args.residual + (size_t)row * args.ld_res + col);
+              const uint32_t* pv = &v.x;
+              const uint32_t* pr = &r.x;
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float a0, a1, b0, b1;
+                unpack_bf16x2(pv[e], a0, a1);
+                unpack_bf16x2(pr[e], b0, b1);
+                o[e] = pack_bf16x2(a0 + b0, a1 + b1);
+              }
+              v = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+            *reinterpret_cast<uint4*>(args.out + (size_t)row * args.ld_out + col) = v;
+            for (int p = 0; p < args.n_peers; ++p)
+              *reinterpret_cast<uint4*>(
+                  args.peer_out[p] + (size_t)(row + args.peer_row_offset) * args.ld_out + col) = v;
+          }
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar);
+      if (lane == 0) mbar_arrive(&tempty_bar[slot]);
     }
   }
 
@@ -234,11 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
 
-  // Fused completion signal: the last CTA to finish publishes `signal_value`
+  // Fused completion signal: the last CTA to finish publishes the flag value
   // to every peer flag (and the local one), after a system-scope fence that
-  // orders this CTA's peer stores before its counter increment.
-  // An aborted CTA never signals: the consumer's bounded wait then reports
-  // the failure instead of reading a half-written tile.
+  // orders this CTA's peer stores before its counter increment. An aborted
+  // CTA never signals: the consumer's bounded wait then reports the failure
+  // instead of reading a half-written tile.
   if (args.done_counter != nullptr && threadIdx.x == 0 && !*abort_flag) {
     fence_sys();
     const int prev = atomicAdd(args.done_counter, 1);
@@ -305,7 +351,7 @@ static cudaError_t launch_variant(const CUtensorMap& tw, const CUtensorMap& tx, 
 int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   if (p.args.K % kBK != 0) return 1001;
   if (p.w_rows_total <= 0) return 1002;
-  if (p.block_n != 64 && p.block_n != 256) return 1003;
+  if (p.block_n != 64 && p.block_n != 128 && p.block_n != 256) return 1003;
   if (((uintptr_t)p.w & 15) || ((uintptr_t)p.x & 15)) return 1004;
   if (p.args.f_tiles <= 0) return 1005;
   CUtensorMap tw, tx;
@@ -319,11 +365,14 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   int grid = units_hint < p.num_sms ? units_hint : p.num_sms;
   if (grid < 1) grid = 1;
   cudaError_t e;
+  // stage counts fill ~192 KB of shared memory per CTA (one CTA per SM)
   if (p.swiglu) {
     if (p.block_n == 64) e = launch_variant<true, 64, 5>(tw, tx, a, grid, stream);
+    else if (p.block_n == 128) e = launch_variant<true, 128, 4>(tw, tx, a, grid, stream);
     else e = launch_variant<true, 256, 3>(tw, tx, a, grid, stream);
   } else {
     if (p.block_n == 64) e = launch_variant<false, 64, 8>(tw, tx, a, grid, stream);
+    else if (p.block_n == 128) e = launch_variant<false, 128, 6>(tw, tx, a, grid, stream);
     else e = launch_variant<false, 256, 4>(tw, tx, a, grid, stream);
   }
   return e == cudaSuccess ? 0 : 4000 + (int)e;

@@ -399,6 +399,37 @@ __global__ void wait_flags_kernel(FlagArgs a) {
   __syncthreads();
 }
 
+// Copies `bytes` (multiple of 16) from src to every peer buffer with 16-byte
+// NVLink stores, then the last CTA raises the peers' flags (release, system
+// scope). The hand-off kernel of the transfer benchmark.
+__global__ void peer_copy_kernel(PeerCopyArgs a) {
+  const uint4* src = reinterpret_cast<const uint4*>(a.src);
+  const size_t n = a.bytes / 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+    for (int p = 0; p < a.n_peers; ++p) reinterpret_cast<uint4*>(a.dst[p])[i] = v;
+  }
+  if (a.done_counter != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      fence_sys();
+      if (atomicAdd(a.done_counter, 1) == (int)gridDim.x - 1) {
+        fence_sys();
+        const int v = a.signal_value + (a.epoch != nullptr ? *a.epoch : 0);
+        for (int p = 0; p < a.n_peers; ++p) st_release_sys(a.flags[p], v);
+        *a.done_counter = 0;
+      }
+    }
+  }
+}
+
+int launch_peer_copy(const PeerCopyArgs& a, int grid, cudaStream_t s) {
+  if (a.bytes % 16 != 0 || a.n_peers > 8) return 1;
+  peer_copy_kernel<<<grid, 512, 0, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
 // Increments a device counter (the step epoch) by `by`.
 __global__ void add_i32_kernel(int* p, int by) {
   if (threadIdx.x == 0 && blockIdx.x == 0) *p += by;

@@ -117,6 +117,18 @@ struct FlagArgs {
   unsigned long long timeout_ns;
 };
 
+struct PeerCopyArgs {
+  const void* src;
+  void* dst[8];
+  int* flags[8];
+  int n_peers;
+  size_t bytes;
+  int signal_value;
+  const int* epoch;
+  int* done_counter;
+};
+
+int launch_peer_copy(const PeerCopyArgs& a, int grid, cudaStream_t s);
 int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s);
 int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s);
 int launch_router_topk(const RouterArgs& a, cudaStream_t s);
