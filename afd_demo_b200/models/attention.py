@@ -69,11 +69,17 @@ class AttentionWorker:
         x, xn = ops.sum_rmsnorm(list(x_parts), lw.in_norm, cfg.rms_norm_eps)
         qkv = ops.linear(xn, lw.w_qkv)
         k_l, v_l = self.cache.layer(layer_idx)
-        q = ops.qk_norm_rope_cache(qkv, lw.q_norm, lw.k_norm, self.rope, k_l, v_l, start,
-                                   self.cache.pos_dev, q_len, batch_offset,
-                                   cfg.num_attention_heads, cfg.num_key_value_heads,
-                                   cfg.rms_norm_eps)
-        o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev)
+        if q_len == 1:  # decode: norm + RoPE + append folded into the attention kernel
+            o = ops.decode_attention_fused(qkv, lw.q_norm, lw.k_norm, self.rope, k_l, v_l, start,
+                                           self.cache.pos_dev, batch_offset,
+                                           cfg.num_attention_heads, cfg.num_key_value_heads,
+                                           cfg.rms_norm_eps)
+        else:
+            q = ops.qk_norm_rope_cache(qkv, lw.q_norm, lw.k_norm, self.rope, k_l, v_l, start,
+                                       self.cache.pos_dev, q_len, batch_offset,
+                                       cfg.num_attention_heads, cfg.num_key_value_heads,
+                                       cfg.rms_norm_eps)
+            o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev)
         if sink is not None:
             return ops.linear(o, lw.w_o, residual=x, out=out, **sink.gemm_kwargs())
         return ops.linear(o, lw.w_o, residual=x, out=out)

@@ -21,7 +21,8 @@ _C = None
 # call launches (decode attention adds a merge kernel when split).
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
-                 "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy"}
+                 "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
+                 "decode_attention_fused"}
 
 
 class LaunchCounter:
@@ -126,6 +127,39 @@ def _moe_block_n(rows: int) -> int:
     return 64 if rows <= 64 else 128
 
 
+def _k_splits(tiles: int, k_iters: int) -> int:
+    """Split-K factor for GEMMs with too few output tiles to fill the GPU:
+    the largest power of two with tiles * s <= SMs and >= 2 k-steps per split."""
+    s = 1
+    n = num_sms()
+    while tiles * s * 2 <= n and k_iters % (s * 2) == 0 and k_iters // (s * 2) >= 2:
+        s *= 2
+    return s
+
+
+class _SplitKWorkspace:
+    """Zero-initialised fp32 partial-sum buffer and tile counters for split-K
+    GEMMs. The kernel leaves both zeroed after every launch, so one buffer is
+    reused forever; it is private to one stream (two streams never share)."""
+
+    _pool: dict = {}
+
+    @classmethod
+    def get(cls, device, tiles: int, block_n: int):
+        stream = torch.cuda.current_stream(device)
+        key = (device.index, stream.cuda_stream)
+        need = tiles * block_n * 128
+        ws = cls._pool.get(key)
+        if ws is None or ws[0].numel() < need or ws[1].numel() < tiles:
+            old = ws
+            n = max(need, old[0].numel() if old else 0)
+            t = max(tiles, old[1].numel() if old else 0)
+            ws = (torch.zeros(n, device=device, dtype=torch.float32),
+                  torch.zeros(t, device=device, dtype=torch.int32))
+            cls._pool[key] = ws
+        return ws
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None, peers: Sequence[int] = (), peer_row_offset: int = 0,
            flags: Sequence[int] = (), signal_value: int = 0,
@@ -144,10 +178,14 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
     if N % 128 != 0:
         raise ValueError(f"linear: output features {N} must be a multiple of 128")
     bn = _block_n(T)
-    units = ((T + bn - 1) // bn) * (N // 128)
-    ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn, units,
-               list(peers), int(peer_row_offset), list(flags), int(signal_value), done_counter,
-               status, epoch)
+    tiles = ((T + bn - 1) // bn) * (N // 128)
+    splits = _k_splits(tiles, K // 64) if T <= 256 else 1
+    ws = cnt = None
+    if splits > 1:
+        ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn)
+    ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn,
+               tiles * splits, list(peers), int(peer_row_offset), list(flags), int(signal_value),
+               done_counter, status, epoch, splits, ws, cnt)
     return out
 
 
@@ -165,6 +203,25 @@ def qk_norm_rope_cache(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Te
     ext().qk_norm_rope_cache(qkv, q_norm, k_norm, rope, q, k_cache, v_cache, start_pos_dev,
                              q_len, batch_offset, nq, nkv, float(eps))
     return q
+
+
+def decode_attention_fused(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                           rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           start_pos: int, start_pos_dev: Optional[torch.Tensor],
+                           batch_offset: int, nq: int, nkv: int, eps: float) -> torch.Tensor:
+    """One decode step of attention for B sequences: q/k RMSNorm + RoPE of the
+    new token, K/V append at `start_pos`, attention over positions
+    0..start_pos. qkv [B, (nq + 2 nkv) D] -> [B, nq * D]."""
+    if not _cuda(qkv):
+        q = torch_ref.qk_norm_rope_cache(qkv, q_norm, k_norm, rope, k_cache, v_cache,
+                                         batch_offset, 1, start_pos, nq, nkv, eps)
+        return torch_ref.attention(q, k_cache, v_cache, batch_offset, 1, start_pos)
+    B = qkv.shape[0]
+    D = k_cache.shape[-1]
+    out = torch.empty(B, nq, D, device=qkv.device, dtype=qkv.dtype)
+    ext().decode_attention_fused(qkv, q_norm, k_norm, rope, k_cache, v_cache, out,
+                                 start_pos_dev, batch_offset, nq, float(eps))
+    return out.view(B, nq * D)
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, batch_offset: int,
@@ -261,10 +318,11 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     C.moe_gather(xn, ws.row_token, ws.num_rows, ws.x_sorted, R)
     units = ws.max_blocks * (I // 128)
     C.gemm(w_gate_up.view(E_loc * I2, H), ws.x_sorted, ws.act, I // 128, I2, I, ws.blocks,
-           ws.num_blocks, 0, None, None, True, bn, units, [], 0, [], 0, None, None, None)
+           ws.num_blocks, 0, None, None, True, bn, units, [], 0, [], 0, None, None, None, 1,
+           None, None)
     units = ws.max_blocks * (H // 128)
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
-           None, ws.row_weight, False, bn, units, [], 0, [], 0, None, None, None)
+           None, ws.row_weight, False, bn, units, [], 0, [], 0, None, None, None, 1, None, None)
     if out is None and not peers:
         out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
     C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
@@ -284,7 +342,7 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     bn = _block_n(T)
     units = ((T + bn - 1) // bn) * (I // 128)
     ext().gemm(w_gate_up, xn, act, I // 128, I2, I, None, None, T, None, None, True, bn, units,
-               [], 0, [], 0, None, None, None)
+               [], 0, [], 0, None, None, None, 1, None, None)
     return linear(act, w_down, residual=residual)
 
 

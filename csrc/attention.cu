@@ -377,6 +377,283 @@ __global__ void __launch_bounds__(128) prefill_attention_kernel(PrefillAttnArgs 
   }
 }
 
+// ================================================= fused decode attention ===
+// One CTA per (sequence, kv head), 8 warps. Prologue (optional): the CTA
+// itself applies q/k RMSNorm + RoPE to its G query heads and its kv head for
+// the new token and appends k, v to the cache (the qk_norm_rope_cache kernel
+// folded in). Main loop: warp w takes 32-key tiles w, w+8, ... of the cache:
+// cp.async into a warp-private padded tile, S = Q K^T and O += P V on m16n8k16
+// tensor-core MMAs with the G query heads as rows (padded to 16), online
+// softmax in the log2 domain. Epilogue: the 8 warps' (m, l, O) merge in
+// shared memory -- no split workspace and no second kernel.
+constexpr int kFdWarps = 8;
+constexpr int kFdKeys = 32;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// q/k head: RMSNorm over D, then RoPE at `pos`; lane owns pairs (j, j+D/2),
+// j = lane + 32 i. Rounds like HF (bf16 after norm, weight, each product).
+template <int D>
+__device__ __forceinline__ void norm_rope_head(const __nv_bfloat16* src, const __nv_bfloat16* nw,
+                                               const float* rope, int pos, float eps, int lane,
+                                               float (&lo)[D / 64], float (&hi)[D / 64]) {
+  constexpr int half = D / 2;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    lo[i] = bf16_to_f(src[lane + 32 * i]);
+    hi[i] = bf16_to_f(src[half + lane + 32 * i]);
+    ss += lo[i] * lo[i] + hi[i] * hi[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  const float rstd = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    const int j = lane + 32 * i;
+    const float xl = round_bf16(bf16_to_f(nw[j]) * round_bf16(lo[i] * rstd));
+    const float xh = round_bf16(bf16_to_f(nw[half + j]) * round_bf16(hi[i] * rstd));
+    const float c = rope[(size_t)pos * D + j];
+    const float s = rope[(size_t)pos * D + half + j];
+    lo[i] = round_bf16(round_bf16(xl * c) + round_bf16(-xh * s));
+    hi[i] = round_bf16(round_bf16(xh * c) + round_bf16(xl * s));
+  }
+}
+
+template <int G, int D>
+__global__ void __launch_bounds__(kFdWarps * 32) decode_attention_fused_kernel(FusedDecodeArgs a) {
+  constexpr int P = D + 8;                 // padded row (ldmatrix conflict-free)
+  constexpr int TILE = kFdKeys * P;        // elements per K or V tile
+  extern __shared__ __align__(16) uint8_t fsm[];
+  __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(fsm);          // [16][P]
+  __nv_bfloat16* kv_s = q_s + 16 * P;                                  // [warps][2][32][P]
+  const int b = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int pos = *a.start_pos;
+  const int kv_len = pos + 1;
+  const int cb = a.batch_offset + b;
+  __nv_bfloat16* kbase = a.k_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
+  __nv_bfloat16* vbase = a.v_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
+
+  // ---------------------------------------------------------------- Q (+K/V)
+  for (int i = tid; i < 16 * P; i += blockDim.x) q_s[i] = f_to_bf16(0.f);
+  __syncthreads();
+  if (a.qkv != nullptr) {
+    const __nv_bfloat16* row = a.qkv + (size_t)b * a.ld_qkv;
+    for (int hr = warp; hr < G + 2; hr += kFdWarps) {
+      float lo[D / 64], hi[D / 64];
+      if (hr < G + 1) {
+        const bool is_q = hr < G;
+        const int head = is_q ? kvh * G + hr : a.nq + kvh;
+        norm_rope_head<D>(row + (size_t)head * D, is_q ? a.q_norm : a.k_norm, a.rope, pos,
+                          a.eps, lane, lo, hi);
+        __nv_bfloat16* dst = is_q ? q_s + hr * P : kbase + (size_t)pos * D;
+#pragma unroll
+        for (int i = 0; i < D / 64; ++i) {
+          dst[lane + 32 * i] = f_to_bf16(lo[i]);
+          dst[D / 2 + lane + 32 * i] = f_to_bf16(hi[i]);
+        }
+      } else {  // value head: copy into the cache
+        const __nv_bfloat16* src = row + (size_t)(a.nq + a.nkv + kvh) * D;
+        for (int j = lane; j < D; j += 32) vbase[(size_t)pos * D + j] = src[j];
+      }
+    }
+    __threadfence_block();
+  } else {
+    for (int i = tid; i < G * D; i += blockDim.x)
+      q_s[(i / D) * P + i % D] = a.q[((size_t)b * a.nq + kvh * G) * D + i];
+  }
+  __syncthreads();
+
+  uint32_t qf[D / 16][4];
+  {
+    const int r = lane % 16, cofs = (lane / 16) * 8;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      ldsm_x4(smem_u32(q_s + r * P + kk * 16 + cofs), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sl2 = rsqrtf((float)D) * 1.4426950408889634f;
+  __nv_bfloat16* ks = kv_s + warp * 2 * TILE;
+  __nv_bfloat16* vs = ks + TILE;
+  const int n_tiles = (kv_len + kFdKeys - 1) / kFdKeys;
+  constexpr int VPR = D / 8;
+
+  for (int tile = warp; tile < n_tiles; tile += kFdWarps) {
+    const int key0 = tile * kFdKeys;
+    const int nk = min(kFdKeys, kv_len - key0);
+    for (int i = lane; i < kFdKeys * VPR; i += 32) {
+      const int r = i / VPR, c = (i % VPR) * 8;
+      if (r < nk) {
+        cp_async16(ks + r * P + c, kbase + (size_t)(key0 + r) * D + c);
+        cp_async16(vs + r * P + c, vbase + (size_t)(key0 + r) * D + c);
+      } else {
+        *reinterpret_cast<uint4*>(ks + r * P + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vs + r * P + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    float s[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int key = np * 16 + (lane % 8) + ((lane / 16) * 8);
+        const int dofs = kk * 16 + ((lane / 8) % 2) * 8;
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(smem_u32(ks + key * P + dofs), r0, r1, r2, r3);
+        mma_bf16_16816(s[np * 2], qf[kk], r0, r1);
+        mma_bf16_16816(s[np * 2 + 1], qf[kk], r2, r3);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = nt * 8 + (lane % 4) * 2 + e < nk;
+        const float v0 = valid ? s[nt][e] * sl2 : -INFINITY;
+        const float v1 = valid ? s[nt][2 + e] * sl2 : -INFINITY;
+        s[nt][e] = v0;
+        s[nt][2 + e] = v1;
+        mx0 = fmaxf(mx0, v0);
+        mx1 = fmaxf(mx1, v1);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffff, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffff, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffff, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffff, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float al0 = (mn0 == -INFINITY) ? 1.f : exp2f(m0 - mn0);
+    const float al1 = (mn1 == -INFINITY) ? 1.f : exp2f(m1 - mn1);
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float p0 = (s[nt][e] == -INFINITY) ? 0.f : exp2f(s[nt][e] - mn0);
+        const float p1 = (s[nt][2 + e] == -INFINITY) ? 0.f : exp2f(s[nt][2 + e] - mn1);
+        s[nt][e] = p0;
+        s[nt][2 + e] = p1;
+        rs0 += p0;
+        rs1 += p1;
+      }
+    }
+    rs0 += __shfl_xor_sync(0xffffffff, rs0, 1);
+    rs0 += __shfl_xor_sync(0xffffffff, rs0, 2);
+    rs1 += __shfl_xor_sync(0xffffffff, rs1, 1);
+    rs1 += __shfl_xor_sync(0xffffffff, rs1, 2);
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= al0; o[i][1] *= al0;
+      o[i][2] *= al1; o[i][3] *= al1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[kk * 2][0], s[kk * 2][1]);
+      pa[1] = pack_bf16x2(s[kk * 2][2], s[kk * 2][3]);
+      pa[2] = pack_bf16x2(s[kk * 2 + 1][0], s[kk * 2 + 1][1]);
+      pa[3] = pack_bf16x2(s[kk * 2 + 1][2], s[kk * 2 + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int key = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+        const int dofs = dp * 16 + (lane / 16) * 8;
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(smem_u32(vs + key * P + dofs), r0, r1, r2, r3);
+        mma_bf16_16816(o[dp * 2], pa, r0, r1);
+        mma_bf16_16816(o[dp * 2 + 1], pa, r2, r3);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------ merge 8 warps
+  __syncthreads();  // tiles no longer needed: reuse their smem
+  float* wm = reinterpret_cast<float*>(kv_s);          // [warps][16]
+  float* wl = wm + kFdWarps * 16;                      // [warps][16]
+  float* wo = wl + kFdWarps * 16;                      // [warps][G][D]
+  const int r0 = lane / 4, r1 = r0 + 8;
+  if (lane % 4 == 0) {
+    wm[warp * 16 + r0] = m0; wl[warp * 16 + r0] = l0;
+    wm[warp * 16 + r1] = m1; wl[warp * 16 + r1] = l1;
+  }
+#pragma unroll
+  for (int nt = 0; nt < D / 8; ++nt) {
+    const int d = nt * 8 + (lane % 4) * 2;
+    if (r0 < G) {
+      wo[(warp * G + r0) * D + d] = o[nt][0];
+      wo[(warp * G + r0) * D + d + 1] = o[nt][1];
+    }
+    if (r1 < G) {
+      wo[(warp * G + r1) * D + d] = o[nt][2];
+      wo[(warp * G + r1) * D + d + 1] = o[nt][3];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kFdWarps; ++w) M = fmaxf(M, wm[w * 16 + h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFdWarps; ++w) {
+      const float mw = wm[w * 16 + h];
+      if (mw == -INFINITY) continue;
+      const float sc = exp2f(mw - M);
+      L += wl[w * 16 + h] * sc;
+      O += wo[(w * G + h) * D + d] * sc;
+    }
+    a.out[((size_t)b * a.nq + kvh * G + h) * D + d] = f_to_bf16(L > 0.f ? O / L : 0.f);
+  }
+}
+
+template <int G, int D>
+static int fused_launch(const FusedDecodeArgs& a, int B, cudaStream_t s) {
+  constexpr int P = D + 8;
+  const int smem = (16 * P + kFdWarps * 2 * kFdKeys * P) * 2;
+  static_assert((kFdWarps * 2 * kFdKeys * (D + 8)) * 2 >=
+                    (2 * kFdWarps * 16 + kFdWarps * G * D) * 4,
+                "merge buffers must fit in the tile region");
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(decode_attention_fused_kernel<G, D>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    set = true;
+  }
+  decode_attention_fused_kernel<G, D><<<dim3(B, a.nkv), kFdWarps * 32, smem, s>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_decode_attention_fused(const FusedDecodeArgs& a, int B, cudaStream_t s) {
+  if (B == 0) return 0;
+  const int G = a.nq / a.nkv;
+  if (G == 8 && a.D == 128) return fused_launch<8, 128>(a, B, s);
+  if (G == 2 && a.D == 64) return fused_launch<2, 64>(a, B, s);
+  if (G == 4 && a.D == 128) return fused_launch<4, 128>(a, B, s);
+  if (G == 8 && a.D == 64) return fused_launch<8, 64>(a, B, s);
+  return 1;
+}
+
 // ============================================================= launchers ===
 template <int G, int D>
 static void dec_launch(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s) {

@@ -57,7 +57,8 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
           bool swiglu, int64_t block_n, int64_t units_hint, std::vector<int64_t> peers,
           int64_t peer_row_offset, std::vector<int64_t> flags, int64_t signal_value,
           const c10::optional<at::Tensor>& done_counter, const c10::optional<at::Tensor>& status,
-          const c10::optional<at::Tensor>& epoch) {
+          const c10::optional<at::Tensor>& epoch, int64_t k_splits,
+          const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters) {
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
@@ -92,6 +93,15 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   a.epoch = opt_ptr<const int>(epoch);
   a.done_counter = opt_ptr<int>(done_counter);
   a.status = opt_ptr<int>(status);
+  a.k_splits = (int)k_splits;
+  a.ws = opt_ptr<float>(ws);
+  a.tile_counters = opt_ptr<int>(tile_counters);
+  if (k_splits > 1) {
+    const int64_t tiles = ((dense_rows + block_n - 1) / block_n) * f_tiles;
+    TORCH_CHECK(a.ws != nullptr && ws->numel() >= tiles * block_n * 128, "split-K workspace too small");
+    TORCH_CHECK(a.tile_counters != nullptr && tile_counters->numel() >= tiles,
+                "split-K tile counters too small");
+  }
   p.w = w.data_ptr();
   p.w_rows_total = w.numel() / K;
   p.ld_w = w.stride(-2);
@@ -175,6 +185,32 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   a.s_max = (int)k_cache.size(2);
   check_rc(afd::launch_decode_attention(a, (int)q.size(0), (int)nsplit, cur_stream()),
            "decode_attention");
+}
+
+void decode_attention_fused(const at::Tensor& qkv, const at::Tensor& q_norm,
+                            const at::Tensor& k_norm, const at::Tensor& rope, at::Tensor& k_cache,
+                            at::Tensor& v_cache, at::Tensor& out, const at::Tensor& start_pos,
+                            int64_t batch_offset, int64_t nq, double eps) {
+  CHECK_BF16(qkv); CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(out);
+  TORCH_CHECK(rope.scalar_type() == at::kFloat, "rope table must be fp32");
+  afd::FusedDecodeArgs a{};
+  a.qkv = cbf(qkv);
+  a.ld_qkv = (int)qkv.stride(0);
+  a.q_norm = cbf(q_norm);
+  a.k_norm = cbf(k_norm);
+  a.rope = rope.data_ptr<float>();
+  a.k_cache = bf(k_cache);
+  a.v_cache = bf(v_cache);
+  a.out = bf(out);
+  a.start_pos = start_pos.data_ptr<int>();
+  a.batch_offset = (int)batch_offset;
+  a.nq = (int)nq;
+  a.nkv = (int)k_cache.size(1);
+  a.D = (int)k_cache.size(3);
+  a.s_max = (int)k_cache.size(2);
+  a.eps = (float)eps;
+  check_rc(afd::launch_decode_attention_fused(a, (int)qkv.size(0), cur_stream()),
+           "decode_attention_fused");
 }
 
 void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
@@ -383,6 +419,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_cache", &qk_norm_rope_cache);
   m.def("decode_attention", &decode_attention);
   m.def("prefill_attention", &prefill_attention);
+  m.def("decode_attention_fused", &decode_attention_fused);
   m.def("router_topk", &router_topk);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

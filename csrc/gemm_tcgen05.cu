@@ -72,9 +72,20 @@ __device__ __forceinline__ int4 unit_block(const GemmArgs& a, int b) {
   return make_int4(rs, n, 0, 0);
 }
 
-__device__ __forceinline__ int total_units(const GemmArgs& a) {
+__device__ __forceinline__ int total_tiles(const GemmArgs& a) {
   int nb = a.blocks != nullptr ? *a.num_blocks : (a.dense_rows + a.block_n - 1) / a.block_n;
   return nb * a.f_tiles;
+}
+
+// Unit u -> (tile, k split). Splits of one tile are tiles-apart so that they
+// run on different CTAs at the same time.
+struct Unit {
+  int tile, split;
+};
+__device__ __forceinline__ Unit unit_of(int u, int tiles) { return {u % tiles, u / tiles}; }
+
+__device__ __forceinline__ void epi_bar() {  // the 4 epilogue warps only
+  asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 template <bool SWIGLU, int BN, int STAGES>
@@ -119,8 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int k_iters = args.K / kBK;
-  const int units = total_units(args);
+  const int k_splits = args.k_splits > 1 ? args.k_splits : 1;
+  const int k_iters = args.K / kBK / k_splits;  // per split
+  const int tiles = total_tiles(args);
+  const int units = tiles * k_splits;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -128,12 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-        const int4 blk = unit_block(args, u / args.f_tiles);
-        const int ft = u % args.f_tiles;
+        const Unit un = unit_of(u, tiles);
+        const int4 blk = unit_block(args, un.tile / args.f_tiles);
+        const int ft = un.tile % args.f_tiles;
         const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
         const int w_row = blk.z * args.w_rows_per_group + ft * kBM;
         const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
-        for (int k = 0; k < k_iters; ++k) {
+        for (int k = un.split * k_iters; k < (un.split + 1) * k_iters; ++k) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.status, 10)) break;
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
@@ -165,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int t = 0;  // local tile counter
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
-        const int4 blk = unit_block(args, u / args.f_tiles);
+        const int4 blk = unit_block(args, unit_of(u, tiles).tile / args.f_tiles);
         const int n_mma = max(32, ((blk.y + 31) / 32) * 32);
         const uint32_t idesc = umma_idesc_bf16(kBM, n_mma);
         const int slot = t % L::kSlots;
@@ -203,19 +217,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     // row vectors (4 lanes per row), with the residual read the same way.
     const int q = warp & 3;
     __nv_bfloat16* st = stage_out + (warp - 2) * 16 * 32;
+    volatile int* last_flag = abort_flag + 1;
     int t = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
-      const int4 blk = unit_block(args, u / args.f_tiles);
-      const int ft = u % args.f_tiles;
+      const Unit un = unit_of(u, tiles);
+      const int4 blk = unit_block(args, un.tile / args.f_tiles);
+      const int ft = un.tile % args.f_tiles;
       const int slot = t % L::kSlots;
       const uint32_t tpar = (uint32_t)((t / L::kSlots) & 1);
       if (!mbar_wait(&tfull_bar[slot], tpar, abort_flag, args.status, 30)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + slot * L::kSlotCols;
       const int f_base = ft * kBM + q * 32;
-      for (int c = 0; c < blk.y; c += 16) {
+      bool emit = true;
+      float* wsp = nullptr;
+      if (!SWIGLU && k_splits > 1) {
+        // split-K: add this split's partial tile into the fp32 workspace
+        wsp = args.ws + (size_t)un.tile * BN * kBM + q * 32 + lane;
+        for (int c = 0; c < blk.y; c += 16) {
+          float acc[16];
+          tmem_ld16(t_row + c, acc);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c + j < blk.y) atomicAdd(wsp + (c + j) * kBM, acc[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[slot]);  // TMEM slot free already
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64)
+          *last_flag = (atomicAdd(&args.tile_counters[un.tile], 1) == k_splits - 1);
+        epi_bar();
+        emit = *last_flag != 0;
+        if (emit) __threadfence();
+      }
+      for (int c = 0; c < blk.y && emit; c += 16) {
         float acc[16];
-        tmem_ld16(t_row + c, acc);
+        if (wsp != nullptr) {
+          // last split: read the reduced tile back and leave zeros behind
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            acc[j] = 0.f;
+            if (c + j < blk.y) {
+              acc[j] = __ldcg(wsp + (c + j) * kBM);
+              __stcg(wsp + (c + j) * kBM, 0.f);
+            }
+          }
+        } else {
+          tmem_ld16(t_row + c, acc);
+        }
         if (SWIGLU) {
           float up[16];
           tmem_ld16(t_row + L::kAccCols + c, up);
@@ -266,6 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
+      }
+      if (wsp != nullptr) {
+        if (emit && threadIdx.x == 64) args.tile_counters[un.tile] = 0;
+        continue;  // TMEM slot was released before the reduction
       }
       tc_fence_before();
       __syncwarp();
@@ -361,6 +416,11 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   if (r) return 3000 + r;
   GemmArgs a = p.args;
   a.block_n = p.block_n;
+  if (a.k_splits > 1) {
+    if (p.swiglu || a.blocks != nullptr) return 1006;  // dense, non-SwiGLU only
+    if ((p.args.K / kBK) % a.k_splits != 0) return 1007;
+    if (a.ws == nullptr || a.tile_counters == nullptr) return 1008;
+  }
   int units_hint = p.units_hint > 0 ? p.units_hint : p.num_sms;
   int grid = units_hint < p.num_sms ? units_hint : p.num_sms;
   if (grid < 1) grid = 1;

@@ -36,6 +36,14 @@ struct GemmArgs {
   const int* epoch;                // optional device epoch base (CUDA-graph replays)
   int* done_counter;               // nullptr: no signal
   int* status;                     // device status word pair (may be nullptr)
+  // split-K (dense, non-SwiGLU only): k_splits CTAs share a tile; partial
+  // sums go to ws[tile][row][128] (fp32) and tile_counters[tile] elects the
+  // last split, which reduces, re-zeroes ws and the counter, and runs the
+  // epilogue. ws and the counters must start zeroed and stay private to one
+  // stream.
+  int k_splits;
+  float* ws;
+  int* tile_counters;
 };
 
 struct GemmLaunch {

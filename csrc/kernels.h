@@ -48,6 +48,25 @@ struct DecodeAttnArgs {
   int batch_offset, nq, nkv, D, s_max;
 };
 
+// Decode attention with the new token's q/k RMSNorm + RoPE + KV append folded
+// in (qkv != nullptr), or over precomputed q [B, nq, D] (qkv == nullptr).
+struct FusedDecodeArgs {
+  const __nv_bfloat16* qkv;   // [B, ld_qkv]: q | k | v of the new token
+  int ld_qkv;
+  const __nv_bfloat16* q;     // used when qkv == nullptr
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* rope;          // [max_pos, D]
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;         // [B, nq, D]
+  const int* start_pos;
+  int batch_offset, nq, nkv, D, s_max;
+  float eps;
+};
+
+int launch_decode_attention_fused(const FusedDecodeArgs& a, int B, cudaStream_t s);
+
 struct PrefillAttnArgs {
   const __nv_bfloat16* q;     // [B * q_len, nq, D]
   const __nv_bfloat16* k_cache;

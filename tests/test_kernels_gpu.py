@@ -131,6 +131,31 @@ def test_decode_attention(B, kv_len):
     assert _rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("B,kv_len,G,D", [(1, 1, 8, 128), (3, 77, 8, 128), (16, 276, 8, 128),
+                                           (64, 300, 8, 128), (2, 2049, 8, 128), (5, 100, 2, 64),
+                                           (4, 500, 8, 64)])
+def test_decode_attention_fused(B, kv_len, G, D):
+    nkv = 4 if D == 128 else 2
+    nq = G * nkv
+    S = 2304
+    kc = _randn(B + 1, nkv, S, D, seed=43)
+    vc = _randn(B + 1, nkv, S, D, seed=44)
+    qkv = _randn(B, (nq + 2 * nkv) * D, seed=45)
+    qn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    rope = ops.rope_table(S, D, 1e6, DEV)
+    start = kv_len - 1
+    kc2, vc2 = kc.clone(), vc.clone()
+    q_ref = torch_ref.qk_norm_rope_cache(qkv.float(), qn.float(), kn.float(), rope, kc2, vc2, 1,
+                                         1, start, nq, nkv, 1e-6)
+    ref = torch_ref.attention(q_ref, kc2.float(), vc2.float(), 1, 1, start)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    out = ops.decode_attention_fused(qkv, qn, kn, rope, kc, vc, start, pos, 1, nq, nkv, 1e-6)
+    assert _rel(out, ref) < 1e-2
+    assert _rel(kc[1:1 + B, :, start], kc2[1:1 + B, :, start]) < 1e-2
+    assert torch.equal(vc[1:1 + B, :, start], vc2[1:1 + B, :, start])
+
+
 @pytest.mark.parametrize("B,q_len,start", [(1, 16, 0), (2, 128, 0), (3, 100, 0), (2, 64, 40),
                                            (1, 512, 0)])
 def test_prefill_attention(B, q_len, start):
