@@ -29,6 +29,8 @@ constexpr int kDecKeys = 64;
 
 template <int G, int D>
 __global__ void __launch_bounds__(D) decode_attention_kernel(DecodeAttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int NT = D;          // threads
   constexpr int NW = NT / 32;
   constexpr int KP = D + 8;      // padded K row (conflict-free row-per-thread reads)
@@ -162,6 +164,8 @@ __global__ void __launch_bounds__(D) decode_attention_kernel(DecodeAttnArgs a) {
 
 // Merge split partials: one CTA of D threads per (sequence, q head).
 __global__ void decode_combine_kernel(DecodeAttnArgs a, int nsplit, int D) {
+  pdl_wait();
+  pdl_trigger();
   const size_t hq = blockIdx.x;
   const int d = threadIdx.x;
   float m = -INFINITY;
@@ -206,6 +210,8 @@ constexpr int kPBN = 64;   // keys per step
 
 template <int D>
 __global__ void __launch_bounds__(128) prefill_attention_kernel(PrefillAttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int P = D + 8;  // padded smem row (ldmatrix conflict-free)
   extern __shared__ __align__(16) uint8_t psm[];
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(psm);
@@ -428,6 +434,8 @@ __device__ __forceinline__ void norm_rope_head(const __nv_bfloat16* src, const _
 
 template <int G, int D>
 __global__ void __launch_bounds__(kFdWarps * 32) decode_attention_fused_kernel(FusedDecodeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int P = D + 8;                 // padded row (ldmatrix conflict-free)
   constexpr int TILE = kFdKeys * P;        // elements per K or V tile
   extern __shared__ __align__(16) uint8_t fsm[];
@@ -640,8 +648,7 @@ static int fused_launch(const FusedDecodeArgs& a, int B, cudaStream_t s) {
                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     set = true;
   }
-  decode_attention_fused_kernel<G, D><<<dim3(B, a.nkv), kFdWarps * 32, smem, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(decode_attention_fused_kernel<G, D>, dim3(B, a.nkv), dim3(kFdWarps * 32), smem, s, a);
 }
 
 int launch_decode_attention_fused(const FusedDecodeArgs& a, int B, cudaStream_t s) {
@@ -658,7 +665,7 @@ int launch_decode_attention_fused(const FusedDecodeArgs& a, int B, cudaStream_t 
 template <int G, int D>
 static void dec_launch(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s) {
   dim3 grid(B, a.nkv, nsplit);
-  decode_attention_kernel<G, D><<<grid, D, 0, s>>>(a);
+  launch_k(decode_attention_kernel<G, D>, grid, dim3(D), 0, s, a);
 }
 
 int launch_decode_attention(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s) {
@@ -670,7 +677,7 @@ int launch_decode_attention(const DecodeAttnArgs& a, int B, int nsplit, cudaStre
   else if (G == 4 && a.D == 128) dec_launch<4, 128>(a, B, nsplit, s);
   else if (G == 8 && a.D == 64) dec_launch<8, 64>(a, B, nsplit, s);
   else return 1;
-  if (nsplit > 1) decode_combine_kernel<<<B * a.nq, a.D, 0, s>>>(a, nsplit, a.D);
+  if (nsplit > 1) launch_k(decode_combine_kernel, dim3(B * a.nq), dim3(a.D), 0, s, a, nsplit, a.D);
   return (int)cudaGetLastError();
 }
 
@@ -685,10 +692,10 @@ int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       set = true;
     }
-    prefill_attention_kernel<128><<<grid, 128, smem, s>>>(a);
+    launch_k(prefill_attention_kernel<128>, grid, dim3(128), smem, s, a);
   } else if (a.D == 64) {
     const int smem = (kPBM + 2 * kPBN) * (64 + 8) * 2;
-    prefill_attention_kernel<64><<<grid, 128, smem, s>>>(a);
+    launch_k(prefill_attention_kernel<64>, grid, dim3(128), smem, s, a);
   } else {
     return 1;
   }

@@ -11,6 +11,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace afd {
 
@@ -34,6 +35,47 @@ __device__ __forceinline__ void report_status(int* status, int code, int where) 
     // first error wins; `where` identifies the call site for debugging
     if (atomicCAS(status, 0, code) == 0) status[1] = where;
   }
+}
+
+// ------------------------------------------- programmatic dependent launch ---
+// Every kernel of this library is launched with programmatic stream
+// serialization: it may be scheduled while its predecessor in the stream is
+// still running. The rule that keeps this correct: a kernel touches no
+// global memory that a predecessor writes or reads (no dependent load, no
+// store at all) before pdl_wait(), and it calls pdl_trigger() only after its
+// own pdl_wait(). Then, when kernel N starts, every kernel up to N-2 has
+// completed, so static data (weights) and outputs of kernels <= N-2 may be
+// read before the wait.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+inline bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("AFD_PDL");
+    on = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return on == 1;
+}
+
+// cudaLaunchKernelEx with the programmatic-serialization attribute (off when
+// AFD_PDL=0).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // ------------------------------------------------------------------ bf16 ---

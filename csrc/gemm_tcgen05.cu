@@ -140,6 +140,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
+      // Weight tiles are static and the row-block list comes from a kernel
+      // at least two launches back (see pdl_wait in common.cuh), so the first
+      // unit's weight tiles are requested before waiting on the previous
+      // kernel; only the activation tiles wait.
+      int pre = 0;
+      if ((int)blockIdx.x < units) {
+        const Unit un = unit_of(blockIdx.x, tiles);
+        const int4 blk = unit_block(args, un.tile / args.f_tiles);
+        const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
+        const int w_row = blk.z * args.w_rows_per_group + (un.tile % args.f_tiles) * kBM;
+        const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
+        pre = min(STAGES, k_iters);
+        for (int i = 0; i < pre; ++i) {  // fresh stages: nothing to wait for
+          uint8_t* sa = smem + i * L::kStageBytes;
+          const int k = un.split * k_iters + i;
+          mbar_arrive_expect_tx(&full_bar[i], bytes);
+          tma_load_2d(sa, &tmap_w, &full_bar[i], k * kBK, w_row);
+          if (SWIGLU)
+            tma_load_2d(sa + L::kABytes, &tmap_w, &full_bar[i], k * kBK, w_row + args.up_offset);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const Unit un = unit_of(u, tiles);
         const int4 blk = unit_block(args, un.tile / args.f_tiles);
@@ -148,14 +171,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w_row = blk.z * args.w_rows_per_group + ft * kBM;
         const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
         for (int k = un.split * k_iters; k < (un.split + 1) * k_iters; ++k) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.status, 10)) break;
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
-          mbar_arrive_expect_tx(&full_bar[stage], bytes);
-          tma_load_2d(sa, &tmap_w, &full_bar[stage], k * kBK, w_row);
-          if (SWIGLU)
-            tma_load_2d(sa + L::kABytes, &tmap_w, &full_bar[stage], k * kBK,
-                        w_row + args.up_offset);
+          if (pre > 0) {
+            --pre;  // weight tile already requested; add the activation boxes
+          } else {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.status, 10)) break;
+            mbar_arrive_expect_tx(&full_bar[stage], bytes);
+            tma_load_2d(sa, &tmap_w, &full_bar[stage], k * kBK, w_row);
+            if (SWIGLU)
+              tma_load_2d(sa + L::kABytes, &tmap_w, &full_bar[stage], k * kBK,
+                          w_row + args.up_offset);
+          }
           for (int b = 0; b < n_boxes; ++b)
             tma_load_2d(sb + b * kBoxRows * kBK * 2, &tmap_x, &full_bar[stage], k * kBK,
                         blk.x + b * kBoxRows);
@@ -174,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
+    pdl_wait();
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
@@ -215,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 16-column chunk is rounded to bf16 in registers, transposed through a
     // warp-private smem tile [16 rows][32 features], and written as 16-byte
     // row vectors (4 lanes per row), with the residual read the same way.
+    pdl_wait();  // residual / row scale / outputs belong to earlier kernels
     const int q = warp & 3;
     __nv_bfloat16* st = stage_out + (warp - 2) * 16 * 32;
     volatile int* last_flag = abort_flag + 1;
@@ -399,8 +428,7 @@ static cudaError_t launch_variant(const CUtensorMap& tw, const CUtensorMap& tx, 
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, kThreads, L::kTotal, stream>>>(tw, tx, a);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(kThreads), L::kTotal, stream, tw, tx, a);
 }
 
 int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {

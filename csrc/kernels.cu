@@ -69,6 +69,8 @@ constexpr int kNormThreads = 256;
 
 __global__ void __launch_bounds__(kNormThreads) sum_rmsnorm_kernel(SumNormArgs a) {
   __shared__ float red[kNormThreads / 32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int H = a.H;
   constexpr int kMaxChunks = 4;
@@ -114,6 +116,8 @@ __global__ void __launch_bounds__(kNormThreads) sum_rmsnorm_kernel(SumNormArgs a
 // [nq+nkv, nq+2nkv) values (copied to the cache unchanged). Lane l owns the
 // rotation pairs (j, j + D/2) for j = l + 32 * i.
 __global__ void qk_norm_rope_cache_kernel(QKRopeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int warps_per_block = blockDim.x / 32;
   const int gw = blockIdx.x * warps_per_block + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -176,6 +180,8 @@ __global__ void qk_norm_rope_cache_kernel(QKRopeArgs a) {
 // logits [T, E] bf16 (E <= 256) -> softmax (fp32) -> top-k -> renormalise.
 // One warp per token. Ties resolve to the lower expert index.
 __global__ void router_topk_kernel(RouterArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int warps_per_block = blockDim.x / 32;
   const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -243,6 +249,8 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int off[kMaxLocalExperts + 1];
   __shared__ int boff[kMaxLocalExperts + 1];
+  pdl_wait();
+  pdl_trigger();
   for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   const int n = a.T * a.top_k;
@@ -286,6 +294,8 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
 
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
 __global__ void moe_gather_kernel(MoeGatherArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   if (row >= *a.num_rows) return;
   const int t = a.row_token[row];
@@ -297,6 +307,8 @@ __global__ void moe_gather_kernel(MoeGatherArgs a) {
 // out[t] = (residual ? h[t] : 0) + sum_j y[inv[t, j]]   (bf16 out, fp32 math)
 // Also stored to up to kMaxPeers peer buffers; the last CTA raises the flags.
 __global__ void __launch_bounds__(kNormThreads) moe_combine_kernel(MoeCombineArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int H = a.H;
   int rows[16];
@@ -350,6 +362,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logit
                                                       int64_t* out) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const __nv_bfloat16* p = logits + (size_t)row * ld;
   float best = -INFINITY;
@@ -383,6 +397,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logit
 
 // ---------------------------------------------------------------- flags ---
 __global__ void signal_flags_kernel(FlagArgs a) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     fence_sys();
     const int v = a.value + (a.epoch != nullptr ? *a.epoch : 0);
@@ -392,6 +408,8 @@ __global__ void signal_flags_kernel(FlagArgs a) {
 
 // Waits until every flag >= value; bounded by timeout_ns (status on expiry).
 __global__ void wait_flags_kernel(FlagArgs a) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x < a.n && blockIdx.x == 0) {
     const int v = a.value + (a.epoch != nullptr ? *a.epoch : 0);
     wait_flag_geq(a.flags[threadIdx.x], v, a.status, 100 + threadIdx.x, a.timeout_ns);
@@ -403,6 +421,8 @@ __global__ void wait_flags_kernel(FlagArgs a) {
 // NVLink stores, then the last CTA raises the peers' flags (release, system
 // scope). The hand-off kernel of the transfer benchmark.
 __global__ void peer_copy_kernel(PeerCopyArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const uint4* src = reinterpret_cast<const uint4*>(a.src);
   const size_t n = a.bytes / 16;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
@@ -426,12 +446,13 @@ __global__ void peer_copy_kernel(PeerCopyArgs a) {
 
 int launch_peer_copy(const PeerCopyArgs& a, int grid, cudaStream_t s) {
   if (a.bytes % 16 != 0 || a.n_peers > 8) return 1;
-  peer_copy_kernel<<<grid, 512, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(peer_copy_kernel, dim3(grid), dim3(512), 0, s, a);
 }
 
 // Increments a device counter (the step epoch) by `by`.
 __global__ void add_i32_kernel(int* p, int by) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) *p += by;
 }
 
@@ -440,8 +461,7 @@ int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s) {
   if (a.H % 8 != 0 || a.H > kNormThreads * 8 * 4 || a.n_parts < 1 || a.n_parts > kMaxParts)
     return 1;
   if (rows == 0) return 0;
-  sum_rmsnorm_kernel<<<rows, kNormThreads, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(sum_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s, a);
 }
 
 int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s) {
@@ -449,59 +469,50 @@ int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s) {
   const int warps = a.T * (a.nq + 2 * a.nkv);
   if (warps == 0) return 0;
   const int wpb = 8;
-  qk_norm_rope_cache_kernel<<<(warps + wpb - 1) / wpb, wpb * 32, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(qk_norm_rope_cache_kernel, dim3((warps + wpb - 1) / wpb), dim3(wpb * 32), 0, s, a);
 }
 
 int launch_router_topk(const RouterArgs& a, cudaStream_t s) {
   if (a.E > 256 || a.top_k > 16) return 1;
   if (a.T == 0) return 0;
   const int wpb = 8;
-  router_topk_kernel<<<(a.T + wpb - 1) / wpb, wpb * 32, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(router_topk_kernel, dim3((a.T + wpb - 1) / wpb), dim3(wpb * 32), 0, s, a);
 }
 
 int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s) {
   if (a.n_local > kMaxLocalExperts || a.block_n <= 0) return 1;
-  moe_align_kernel<<<1, kAlignThreads, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(moe_align_kernel, dim3(1), dim3(kAlignThreads), 0, s, a);
 }
 
 int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s) {
   if (a.H % 8 != 0) return 1;
   if (max_rows == 0) return 0;
-  moe_gather_kernel<<<max_rows, 256, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(moe_gather_kernel, dim3(max_rows), dim3(256), 0, s, a);
 }
 
 int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s) {
   if (a.H % 8 != 0 || a.top_k > 16) return 1;
   if (T == 0) return 0;
-  moe_combine_kernel<<<T, kNormThreads, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(moe_combine_kernel, dim3(T), dim3(kNormThreads), 0, s, a);
 }
 
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
                   cudaStream_t s) {
   if (rows == 0) return 0;
-  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, ld, out);
-  return (int)cudaGetLastError();
+  return (int)launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, logits, V, ld, out);
 }
 
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s) {
-  signal_flags_kernel<<<1, 32, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(signal_flags_kernel, dim3(1), dim3(32), 0, s, a);
 }
 
 int launch_wait_flags(const FlagArgs& a, cudaStream_t s) {
   if (a.n > 32) return 1;
-  wait_flags_kernel<<<1, 32, 0, s>>>(a);
-  return (int)cudaGetLastError();
+  return (int)launch_k(wait_flags_kernel, dim3(1), dim3(32), 0, s, a);
 }
 
 int launch_add_i32(int* p, int by, cudaStream_t s) {
-  add_i32_kernel<<<1, 32, 0, s>>>(p, by);
-  return (int)cudaGetLastError();
+  return (int)launch_k(add_i32_kernel, dim3(1), dim3(32), 0, s, p, by);
 }
 
 }  // namespace afd
