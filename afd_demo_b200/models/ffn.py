@@ -66,12 +66,10 @@ class FFNWorker:
             y = ops.dense_mlp(xn, lw.w_dense_gate_up, lw.w_dense_down, residual=residual)
             self._mark(False, EventType.MOE_SHARED_OR_DENSE, layer_idx, mb_idx)
             return y
-        self._mark(True, EventType.MOE_ROUTER, layer_idx, mb_idx)
-        xn, ids, w = ops.router_topk(h, lw.post_norm, lw.w_router, cfg.num_experts_per_tok,
-                                     cfg.rms_norm_eps, cfg.norm_topk_prob)
-        self._mark(False, EventType.MOE_ROUTER, layer_idx, mb_idx)
-        self._mark(True, EventType.MOE_EXPERTS, layer_idx, mb_idx)
-        y = ops.moe_experts(xn, ids, w, lw.w_gate_up, lw.w_down, lw.expert_start,
-                            residual=residual, out=out, **kw)
-        self._mark(False, EventType.MOE_EXPERTS, layer_idx, mb_idx)
-        return y
+        stage = {"router": EventType.MOE_ROUTER, "experts": EventType.MOE_EXPERTS}
+        return ops.moe_ffn(h, lw.post_norm, lw.w_router, lw.w_gate_up, lw.w_down,
+                           cfg.num_experts_per_tok, cfg.rms_norm_eps, cfg.norm_topk_prob,
+                           lw.expert_start, add_residual=residual is not None, out=out,
+                           tracker_marks=lambda start, name: self._mark(start, stage[name],
+                                                                        layer_idx, mb_idx),
+                           **kw)

@@ -22,7 +22,7 @@ _C = None
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
                  "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
-                 "decode_attention_fused"}
+                 "decode_attention_fused", "moe_route"}
 
 
 class LaunchCounter:
@@ -185,7 +185,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn)
     ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn,
                tiles * splits, list(peers), int(peer_row_offset), list(flags), int(signal_value),
-               done_counter, status, epoch, splits, ws, cnt)
+               done_counter, status, epoch, splits, ws, cnt, None)
     return out
 
 
@@ -267,6 +267,9 @@ def router_topk(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tens
     return xn, ids, w
 
 
+_GATHER4_MAX_TOKENS = 512
+
+
 class MoEWorkspace:
     """Device buffers of one MoE call (sized for T tokens)."""
 
@@ -282,10 +285,43 @@ class MoEWorkspace:
         self.blocks = mk(max_blocks, 4)
         self.num_blocks = mk(1)
         self.num_rows = mk(1)
-        self.x_sorted = mk(R, H, dt=dtype)
         self.act = mk(R, I, dt=dtype)
         self.y = mk(R, H, dt=dtype)
+        self.ids = mk(T, top_k)
+        self.weights = mk(T, top_k, dt=torch.float32)
         self.max_blocks = max_blocks
+        self.block_n = block_n
+
+
+def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T, k, peers,
+                       seg_offsets, peer_row_offset, flags, signal_value, done_counter, epoch):
+    """Grouped gate_up GEMM (SwiGLU epilogue) -> grouped down GEMM
+    (routing-weight epilogue) -> combine (+ residual, + peer stores). For
+    decode-sized batches the gate_up producer gathers token rows straight from
+    xn with TMA tile::gather4; prefill-sized batches gather once into expert
+    order so the producer issues one TMA box per 32 rows."""
+    C = ext()
+    E_loc, I2, H = w_gate_up.shape
+    I = I2 // 2
+    bn = ws.block_n
+    if T <= _GATHER4_MAX_TOKENS:
+        x, row_ids = xn, ws.row_token
+    else:
+        R = T * k
+        x = torch.empty(R, H, device=xn.device, dtype=xn.dtype)
+        C.moe_gather(xn, ws.row_token, ws.num_rows, x, R)
+        row_ids = None
+    C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
+           0, None, None, True, bn, ws.max_blocks * (I // 128), [], 0, [], 0, None, None, None,
+           1, None, None, row_ids)
+    C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
+           None, ws.row_weight, False, bn, ws.max_blocks * (H // 128), [], 0, [], 0, None, None,
+           None, 1, None, None, None)
+    if out is None and not peers:
+        out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
+    C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
+                  int(peer_row_offset), list(flags), int(signal_value), done_counter, epoch)
+    return out
 
 
 def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
@@ -296,9 +332,8 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                 done_counter: Optional[torch.Tensor] = None, epoch: Optional[torch.Tensor] = None,
                 ws: Optional[MoEWorkspace] = None) -> torch.Tensor:
     """(residual +) sum over the token's local top-k experts of
-    w * down(silu(gate x) * up x); bf16 [T, H]. GPU path: routing/permute
-    kernel, grouped tcgen05 GEMM with SwiGLU epilogue, grouped tcgen05 GEMM
-    with routing-weight epilogue, combine (+ residual, + peer stores)."""
+    w * down(silu(gate x) * up x); bf16 [T, H]. GPU path: routing kernel,
+    grouped tcgen05 GEMMs, combine (+ residual, + peer stores)."""
     T, H = xn.shape
     if not _cuda(xn):
         y = torch_ref.moe_experts(xn, ids, weights, w_gate_up, w_down, expert_start)
@@ -306,28 +341,59 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
             y = y + residual.float()
         return y.to(xn.dtype)
     E_loc, I2, _ = w_gate_up.shape
-    I = I2 // 2
     k = ids.shape[1]
-    bn = _moe_block_n(T)
     if ws is None:
-        ws = MoEWorkspace(T, k, E_loc, H, I, bn, xn.device, xn.dtype)
+        ws = MoEWorkspace(T, k, E_loc, H, I2 // 2, _moe_block_n(T), xn.device, xn.dtype)
+    ext().moe_align(ids, weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+    return _moe_gemms_combine(xn, ws, w_gate_up, w_down, residual, out, T, k, peers, seg_offsets,
+                              peer_row_offset, flags, signal_value, done_counter, epoch)
+
+
+def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
+            w_gate_up: torch.Tensor, w_down: torch.Tensor, top_k: int, eps: float,
+            norm_topk_prob: bool = True, expert_start: int = 0, add_residual: bool = True,
+            out: Optional[torch.Tensor] = None, peers: Sequence[int] = (),
+            seg_offsets: Sequence[int] = (), peer_row_offset: int = 0, flags: Sequence[int] = (),
+            signal_value: int = 0, done_counter: Optional[torch.Tensor] = None,
+            epoch: Optional[torch.Tensor] = None, tracker_marks=None) -> torch.Tensor:
+    """The whole sparse-MoE block on h = attn_out + residual: post-attention
+    RMSNorm, router GEMM, softmax/top-k/renormalise + routing (one kernel for
+    up to 4096 routed pairs), grouped expert GEMMs, combine. Returns
+    h + moe(norm(h)) (or the local experts' partial sum)."""
+    mark = tracker_marks or (lambda *_: None)
+    if not _cuda(h):
+        mark(True, "router")
+        xn, ids, w = torch_ref.router_topk(h, post_norm_w, w_router, top_k, eps, norm_topk_prob)
+        mark(False, "router")
+        mark(True, "experts")
+        y = moe_experts(xn, ids, w, w_gate_up, w_down, expert_start,
+                        residual=h if add_residual else None)
+        mark(False, "experts")
+        return y
+    T, H = h.shape
+    E = w_router.shape[0]
+    E_loc, I2, _ = w_gate_up.shape
+    mark(True, "router")
+    xn = rmsnorm(h, post_norm_w, eps)
+    logits = linear(xn, w_router) if E % 128 == 0 else torch.nn.functional.linear(xn, w_router)
+    ws = MoEWorkspace(T, top_k, E_loc, H, I2 // 2, _moe_block_n(T), h.device, h.dtype)
     C = ext()
-    C.moe_align(ids, weights, expert_start, E_loc, bn, ws.inv, ws.row_token, ws.row_weight,
-                ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
-    R = T * k
-    C.moe_gather(xn, ws.row_token, ws.num_rows, ws.x_sorted, R)
-    units = ws.max_blocks * (I // 128)
-    C.gemm(w_gate_up.view(E_loc * I2, H), ws.x_sorted, ws.act, I // 128, I2, I, ws.blocks,
-           ws.num_blocks, 0, None, None, True, bn, units, [], 0, [], 0, None, None, None, 1,
-           None, None)
-    units = ws.max_blocks * (H // 128)
-    C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
-           None, ws.row_weight, False, bn, units, [], 0, [], 0, None, None, None, 1, None, None)
-    if out is None and not peers:
-        out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
-    C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
-                  int(peer_row_offset), list(flags), int(signal_value), done_counter, epoch)
-    return out
+    if T * top_k <= 4096 and E <= 256:
+        C.moe_route(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob), expert_start, E_loc,
+                    ws.block_n, ws.inv, ws.row_token, ws.row_weight, ws.expert_offsets,
+                    ws.blocks, ws.num_blocks, ws.num_rows)
+    else:
+        C.router_topk(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob))
+        C.moe_align(ws.ids, ws.weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+    mark(False, "router")
+    mark(True, "experts")
+    y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T, top_k,
+                           peers, seg_offsets, peer_row_offset, flags, signal_value,
+                           done_counter, epoch)
+    mark(False, "experts")
+    return y
 
 
 def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
@@ -342,7 +408,7 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     bn = _block_n(T)
     units = ((T + bn - 1) // bn) * (I // 128)
     ext().gemm(w_gate_up, xn, act, I // 128, I2, I, None, None, T, None, None, True, bn, units,
-               [], 0, [], 0, None, None, None, 1, None, None)
+               [], 0, [], 0, None, None, None, 1, None, None, None)
     return linear(act, w_down, residual=residual)
 
 

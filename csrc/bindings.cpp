@@ -58,7 +58,8 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
           int64_t peer_row_offset, std::vector<int64_t> flags, int64_t signal_value,
           const c10::optional<at::Tensor>& done_counter, const c10::optional<at::Tensor>& status,
           const c10::optional<at::Tensor>& epoch, int64_t k_splits,
-          const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters) {
+          const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters,
+          const c10::optional<at::Tensor>& row_ids) {
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
@@ -94,6 +95,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   a.done_counter = opt_ptr<int>(done_counter);
   a.status = opt_ptr<int>(status);
   a.k_splits = (int)k_splits;
+  a.row_ids = opt_ptr<const int>(row_ids);
   a.ws = opt_ptr<float>(ws);
   a.tile_counters = opt_ptr<int>(tile_counters);
   if (k_splits > 1) {
@@ -268,6 +270,38 @@ void moe_align(const at::Tensor& ids, const at::Tensor& weights, int64_t expert_
   check_rc(afd::launch_moe_align(a, cur_stream()), "moe_align");
 }
 
+// router softmax/top-k from logits + routing, one launch; ids / weights are
+// written too (for callers that want them)
+void moe_route(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, int64_t top_k,
+               bool renorm, int64_t expert_start, int64_t n_local, int64_t block_n,
+               at::Tensor& inv, at::Tensor& row_token, at::Tensor& row_weight,
+               at::Tensor& expert_offsets, at::Tensor& blocks, at::Tensor& num_blocks,
+               at::Tensor& num_rows) {
+  afd::RouterArgs r{};
+  r.logits = cbf(logits);
+  r.ld_logits = (int)logits.stride(0);
+  r.ids = ids.data_ptr<int32_t>();
+  r.weights = weights.data_ptr<float>();
+  r.T = (int)logits.size(0);
+  r.E = (int)logits.size(1);
+  r.top_k = (int)top_k;
+  r.renorm = renorm ? 1 : 0;
+  afd::MoeAlignArgs a{};
+  a.T = r.T;
+  a.top_k = r.top_k;
+  a.expert_start = (int)expert_start;
+  a.n_local = (int)n_local;
+  a.block_n = (int)block_n;
+  a.inv = inv.data_ptr<int32_t>();
+  a.row_token = row_token.data_ptr<int32_t>();
+  a.row_weight = row_weight.data_ptr<float>();
+  a.expert_offsets = expert_offsets.data_ptr<int32_t>();
+  a.blocks = reinterpret_cast<int4*>(blocks.data_ptr<int32_t>());
+  a.num_blocks = num_blocks.data_ptr<int32_t>();
+  a.num_rows = num_rows.data_ptr<int32_t>();
+  check_rc(afd::launch_moe_route(r, a, cur_stream()), "moe_route");
+}
+
 void moe_gather(const at::Tensor& x, const at::Tensor& row_token, const at::Tensor& num_rows,
                 at::Tensor& out, int64_t max_rows) {
   afd::MoeGatherArgs a{};
@@ -422,6 +456,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention_fused", &decode_attention_fused);
   m.def("router_topk", &router_topk);
   m.def("moe_align", &moe_align);
+  m.def("moe_route", &moe_route);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("argmax", &argmax);

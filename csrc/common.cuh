@@ -43,9 +43,9 @@ __device__ __forceinline__ void report_status(int* status, int code, int where) 
 // still running. The rule that keeps this correct: a kernel touches no
 // global memory that a predecessor writes or reads (no dependent load, no
 // store at all) before pdl_wait(), and it calls pdl_trigger() only after its
-// own pdl_wait(). Then, when kernel N starts, every kernel up to N-2 has
-// completed, so static data (weights) and outputs of kernels <= N-2 may be
-// read before the wait.
+// own pdl_wait(). Only static data (weights) may be read before the wait:
+// which kernel precedes which changes as kernels are fused, so nothing else
+// is assumed complete.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -171,6 +171,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Four-row gather: rows r0..r3 (any order, any rows of the tensor) at column
+// c0, one row-high box each, written as four consecutive 128-byte rows.
+__device__ __forceinline__ void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int c0,
+                                            int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
       : "memory");
 }
 

@@ -62,7 +62,9 @@ struct GemmSmem {
                                    : kUsedCols <= 128 ? 128 : kUsedCols <= 256 ? 256 : 512;
   // epilogue staging: per warp 16 rows x 32 features bf16
   static constexpr int kStageOutBytes = kEpiWarps * 16 * 32 * 2;
-  static constexpr int kTotal = kDataBytes + kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kRowIdBytes = BN * 4;                 // gathered rows of one block
+  static constexpr int kTotal =
+      kDataBytes + kStageOutBytes + kRowIdBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ int4 unit_block(const GemmArgs& a, int b) {
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;          // [kSlots]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* rows_s = reinterpret_cast<int*>(smem + L::kDataBytes + L::kStageOutBytes + 256);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -130,9 +133,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Grouped mode: the row-block list is written by the previous kernel, so
+  // every thread waits for it before reading. Dense mode: the unit list is
+  // arithmetic and the producer may request weight tiles before the wait.
+  const bool grouped = args.blocks != nullptr;
+  if (grouped) pdl_wait();
   const int k_splits = args.k_splits > 1 ? args.k_splits : 1;
   const int k_iters = args.K / kBK / k_splits;  // per split
-  const int tiles = total_tiles(args);
+  int tiles = total_tiles(args);
+  if (tiles < 0 || (args.max_units > 0 && tiles * k_splits > args.max_units)) {
+    // a corrupt block count: record it and do no work rather than stream
+    // from wild coordinates
+    if (threadIdx.x == 0) report_status(args.status, kBoundsViolation, 40);
+    tiles = 0;
+  }
   const int units = tiles * k_splits;
 
   if (warp == 0) {
@@ -140,12 +154,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
-      // Weight tiles are static and the row-block list comes from a kernel
-      // at least two launches back (see pdl_wait in common.cuh), so the first
-      // unit's weight tiles are requested before waiting on the previous
-      // kernel; only the activation tiles wait.
+      // Dense mode: weight tiles are static, so the first unit's weight tiles
+      // are requested before waiting on the previous kernel; only the
+      // activation tiles wait.
       int pre = 0;
-      if ((int)blockIdx.x < units) {
+      if (!grouped && (int)blockIdx.x < units) {
         const Unit un = unit_of(blockIdx.x, tiles);
         const int4 blk = unit_block(args, un.tile / args.f_tiles);
         const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
@@ -170,6 +183,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
         const int w_row = blk.z * args.w_rows_per_group + ft * kBM;
         const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
+        if (args.row_ids != nullptr) {
+          // source rows of this block; padding rows repeat the last real row
+          for (int j = 0; j < n_boxes * kBoxRows; ++j)
+            rows_s[j] = args.row_ids[blk.x + min(j, blk.y - 1)];
+        }
         for (int k = un.split * k_iters; k < (un.split + 1) * k_iters; ++k) {
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
@@ -183,9 +201,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sa + L::kABytes, &tmap_w, &full_bar[stage], k * kBK,
                           w_row + args.up_offset);
           }
-          for (int b = 0; b < n_boxes; ++b)
-            tma_load_2d(sb + b * kBoxRows * kBK * 2, &tmap_x, &full_bar[stage], k * kBK,
-                        blk.x + b * kBoxRows);
+          if (args.row_ids != nullptr) {
+            for (int j = 0; j < n_boxes * kBoxRows; j += 4)
+              tma_gather4(sb + j * kBK * 2, &tmap_x, &full_bar[stage], k * kBK, rows_s[j],
+                          rows_s[j + 1], rows_s[j + 2], rows_s[j + 3]);
+          } else {
+            for (int b = 0; b < n_boxes; ++b)
+              tma_load_2d(sb + b * kBoxRows * kBK * 2, &tmap_x, &full_bar[stage], k * kBK,
+                          blk.x + b * kBoxRows);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -440,7 +464,8 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   CUtensorMap tw, tx;
   int r = make_tmap(&tw, p.w, p.w_rows_total, p.args.K, p.ld_w, kBM);
   if (r) return 2000 + r;
-  r = make_tmap(&tx, p.x, p.x_rows, p.args.K, p.ld_x, kBoxRows);
+  // gathered rows: one-row boxes for tile::gather4
+  r = make_tmap(&tx, p.x, p.x_rows, p.args.K, p.ld_x, p.args.row_ids != nullptr ? 1 : kBoxRows);
   if (r) return 3000 + r;
   GemmArgs a = p.args;
   a.block_n = p.block_n;
@@ -450,6 +475,7 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
     if (a.ws == nullptr || a.tile_counters == nullptr) return 1008;
   }
   int units_hint = p.units_hint > 0 ? p.units_hint : p.num_sms;
+  a.max_units = p.units_hint > 0 ? p.units_hint : 0;
   int grid = units_hint < p.num_sms ? units_hint : p.num_sms;
   if (grid < 1) grid = 1;
   cudaError_t e;

@@ -44,6 +44,10 @@ struct GemmArgs {
   int k_splits;
   float* ws;
   int* tile_counters;
+  // gathered B operand: sorted row r of a block reads row row_ids[r] of x
+  // (TMA tile::gather4); nullptr: rows are contiguous in x
+  const int* row_ids;
+  int max_units;                   // upper bound on work units (set by the launcher)
 };
 
 struct GemmLaunch {

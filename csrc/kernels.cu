@@ -179,27 +179,25 @@ __global__ void qk_norm_rope_cache_kernel(QKRopeArgs a) {
 // ------------------------------------------------------- router top-k ---
 // logits [T, E] bf16 (E <= 256) -> softmax (fp32) -> top-k -> renormalise.
 // One warp per token. Ties resolve to the lower expert index.
-__global__ void router_topk_kernel(RouterArgs a) {
-  pdl_wait();
-  pdl_trigger();
-  const int warps_per_block = blockDim.x / 32;
-  const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (t >= a.T) return;
+// Softmax + top-k + renormalise of one token's router logits by one warp;
+// lane 0 writes ids / weights.
+__device__ __forceinline__ void topk_token(const __nv_bfloat16* logits, int E, int top_k,
+                                           int renorm, int lane, int32_t* ids_out,
+                                           float* w_out) {
   constexpr int kMaxPer = 8;  // E <= 256
-  const int per = (a.E + 31) / 32;
+  const int per = (E + 31) / 32;
   float v[kMaxPer];
   float m = -INFINITY;
   for (int i = 0; i < per; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < a.E ? bf16_to_f(a.logits[(size_t)t * a.ld_logits + e]) : -INFINITY;
+    v[i] = e < E ? bf16_to_f(logits[e]) : -INFINITY;
     m = fmaxf(m, v[i]);
   }
   m = warp_max(m);
   float s = 0.f;
   for (int i = 0; i < per; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < a.E ? __expf(v[i] - m) : 0.f;
+    v[i] = e < E ? __expf(v[i] - m) : 0.f;
     s += v[i];
   }
   s = warp_sum(s);
@@ -208,12 +206,12 @@ __global__ void router_topk_kernel(RouterArgs a) {
   float sel_w[16];
   int sel_e[16];
   float wsum = 0.f;
-  for (int k = 0; k < a.top_k; ++k) {
+  for (int k = 0; k < top_k; ++k) {
     float best = -1.f;
     int be = 0x7fffffff;
     for (int i = 0; i < per; ++i) {
       const int e = lane + 32 * i;
-      if (e < a.E && (v[i] > best || (v[i] == best && e < be))) { best = v[i]; be = e; }
+      if (e < E && (v[i] > best || (v[i] == best && e < be))) { best = v[i]; be = e; }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -228,12 +226,23 @@ __global__ void router_topk_kernel(RouterArgs a) {
       if (lane + 32 * i == be) v[i] = -2.f;  // remove from further rounds
   }
   if (lane == 0) {
-    const float r = a.renorm ? 1.f / wsum : 1.f;
-    for (int k = 0; k < a.top_k; ++k) {
-      a.ids[(size_t)t * a.top_k + k] = sel_e[k];
-      a.weights[(size_t)t * a.top_k + k] = sel_w[k] * r;
+    const float r = renorm ? 1.f / wsum : 1.f;
+    for (int k = 0; k < top_k; ++k) {
+      ids_out[k] = sel_e[k];
+      w_out[k] = sel_w[k] * r;
     }
   }
+}
+
+__global__ void router_topk_kernel(RouterArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int warps_per_block = blockDim.x / 32;
+  const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= a.T) return;
+  topk_token(a.logits + (size_t)t * a.ld_logits, a.E, a.top_k, a.renorm, lane,
+             a.ids + (size_t)t * a.top_k, a.weights + (size_t)t * a.top_k);
 }
 
 // ------------------------------------------------------- MoE routing ---
@@ -245,34 +254,56 @@ __global__ void router_topk_kernel(RouterArgs a) {
 constexpr int kAlignThreads = 1024;
 constexpr int kMaxLocalExperts = 256;
 
-__global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a) {
-  __shared__ int cnt[kMaxLocalExperts];
-  __shared__ int off[kMaxLocalExperts + 1];
-  __shared__ int boff[kMaxLocalExperts + 1];
-  pdl_wait();
-  pdl_trigger();
+// Body shared by moe_align_kernel and moe_route_kernel; every thread of the
+// (single) CTA calls it. `ids` / `weights` may live in global or shared memory.
+__device__ void align_body(const int32_t* ids, const float* weights, const MoeAlignArgs& a,
+                           int* cnt, int* off, int* boff) {
   for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   const int n = a.T * a.top_k;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = a.ids[i] - a.expert_start;
+    const int e = ids[i] - a.expert_start;
     int slot = -1;
     if (e >= 0 && e < a.n_local) slot = atomicAdd(&cnt[e], 1);
     a.inv[i] = slot;  // provisional: slot within the expert
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, bacc = 0;
-    for (int e = 0; e < a.n_local; ++e) {
-      off[e] = acc;
-      boff[e] = bacc;
-      acc += cnt[e];
-      bacc += (cnt[e] + a.block_n - 1) / a.block_n;
+  if (threadIdx.x < 32) {
+    // warp-wide exclusive scans of row counts and block counts; lane l owns
+    // experts [l * per, (l + 1) * per)
+    const int lane = threadIdx.x;
+    const int per = (a.n_local + 31) / 32;
+    int rows = 0, blocks = 0;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < a.n_local) {
+        rows += cnt[e];
+        blocks += (cnt[e] + a.block_n - 1) / a.block_n;
+      }
     }
-    off[a.n_local] = acc;
-    boff[a.n_local] = bacc;
-    *a.num_blocks = bacc;
-    *a.num_rows = acc;
+    int rs = rows, bs = blocks;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int r2 = __shfl_up_sync(0xffffffff, rs, o);
+      const int b2 = __shfl_up_sync(0xffffffff, bs, o);
+      if (lane >= o) { rs += r2; bs += b2; }
+    }
+    int racc = rs - rows, bacc = bs - blocks;  // exclusive prefix
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < a.n_local) {
+        off[e] = racc;
+        boff[e] = bacc;
+        racc += cnt[e];
+        bacc += (cnt[e] + a.block_n - 1) / a.block_n;
+      }
+    }
+    if (lane == 31) {
+      off[a.n_local] = rs;
+      boff[a.n_local] = bs;
+      *a.num_blocks = bs;
+      *a.num_rows = rs;
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e <= a.n_local; e += blockDim.x) a.expert_offsets[e] = off[e];
@@ -284,12 +315,54 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int slot = a.inv[i];
     if (slot < 0) continue;
-    const int e = a.ids[i] - a.expert_start;
+    const int e = ids[i] - a.expert_start;
     const int row = off[e] + slot;
     a.inv[i] = row;
     a.row_token[row] = i / a.top_k;
-    a.row_weight[row] = a.weights[i];
+    a.row_weight[row] = weights[i];
   }
+}
+
+__global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a) {
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  pdl_wait();
+  pdl_trigger();
+  align_body(a.ids, a.weights, a, cnt, off, boff);
+}
+
+// Router softmax/top-k for all T tokens (one warp per token) followed by the
+// routing of moe_align_kernel, in one single-CTA launch (T * top_k <= 4096).
+constexpr int kRouteMaxEntries = 4096;
+
+__global__ void __launch_bounds__(kAlignThreads) moe_route_kernel(RouterArgs r, MoeAlignArgs a) {
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  __shared__ int32_t s_ids[kRouteMaxEntries];
+  __shared__ float s_w[kRouteMaxEntries];
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int t = warp; t < r.T; t += blockDim.x / 32)
+    topk_token(r.logits + (size_t)t * r.ld_logits, r.E, r.top_k, r.renorm, lane,
+               s_ids + t * r.top_k, s_w + t * r.top_k);
+  __syncthreads();
+  const int n = r.T * r.top_k;
+  if (r.ids != nullptr)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      r.ids[i] = s_ids[i];
+      r.weights[i] = s_w[i];
+    }
+  align_body(s_ids, s_w, a, cnt, off, boff);
+}
+
+int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s) {
+  if (r.T * r.top_k > kRouteMaxEntries || r.E > 256 || r.top_k > 16 ||
+      a.n_local > kMaxLocalExperts || a.block_n <= 0)
+    return 1;
+  return (int)launch_k(moe_route_kernel, dim3(1), dim3(kAlignThreads), 0, s, r, a);
 }
 
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.

@@ -152,6 +152,8 @@ int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s);
 int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s);
 int launch_router_topk(const RouterArgs& a, cudaStream_t s);
 int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s);
+// router top-k + moe_align in one launch (T * top_k <= 4096)
+int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s);
 int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s);
 int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s);
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,

@@ -71,6 +71,22 @@ def test_moe_experts(T, E, k):
     assert _rel(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("T,E_loc,start", [(1, 128, 0), (16, 128, 0), (64, 128, 0), (300, 128, 0),
+                                           (1024, 128, 0), (48, 32, 32)])
+def test_moe_ffn_block(T, E_loc, start):
+    """RMSNorm + router + fused top-k/routing + gathered grouped GEMMs + combine."""
+    H, I, E = 2048, 768, 128
+    h = _randn(T, H, seed=13)
+    pw = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    wr = _randn(E, H, scale=0.02, seed=14)
+    wgu = _randn(E_loc, 2 * I, H, scale=0.02, seed=15)
+    wd = _randn(E_loc, H, I, scale=0.02, seed=16)
+    ref = torch_ref.ffn_layer(h, pw, wr, wgu, wd, 8, 1e-6, expert_start=start,
+                              add_residual=(start == 0))
+    out = ops.moe_ffn(h, pw, wr, wgu, wd, 8, 1e-6, True, start, add_residual=(start == 0))
+    assert _rel(out, ref) < 2e-2
+
+
 def test_moe_residual_and_ep_partials_sum():
     T, H, I, E = 48, 2048, 768, 128
     xn = _randn(T, H, seed=9)
