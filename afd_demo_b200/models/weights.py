@@ -231,66 +231,69 @@ def save_checkpoint(path: str, cfg: ModelConfig, attn: AttentionWeights, ffn: FF
 
 
 def write_random_checkpoint(path: str, cfg: ModelConfig, seed: int = 0,
-                            dtype=torch.bfloat16) -> None:
-    """Random-init checkpoint written layer by layer (bounded host memory)."""
+                            dtype=torch.bfloat16, device="cpu") -> None:
+    """Random-init checkpoint written layer by layer (bounded host memory).
+    `device` is where the random tensors are drawn (a GPU draws the 30B
+    parameters of Qwen3-30B-A3B in seconds); the values depend on it."""
     from safetensors.torch import save_file
 
     os.makedirs(path, exist_ok=True)
     cfg.save(path)
     weight_map: Dict[str, str] = {}
     one = ModelConfig(**{**cfg.__dict__, "num_hidden_layers": 1})
-    aw0 = random_attention_weights(one, seed=seed, dtype=dtype)
+    aw0 = random_attention_weights(one, seed=seed, device=device, dtype=dtype)
     head = {"model.embed_tokens.weight": aw0.embed, "model.norm.weight": aw0.final_norm,
             "lm_head.weight": aw0.lm_head}
-    save_file({k: v.contiguous() for k, v in head.items()},
+    save_file({k: v.contiguous().cpu() for k, v in head.items()},
               os.path.join(path, "model-embed-head.safetensors"), metadata={"format": "pt"})
     weight_map.update({k: "model-embed-head.safetensors" for k in head})
     for l in range(cfg.num_hidden_layers):
-        aw = _layer_only_attention(cfg, l, seed, dtype)
-        fw = _layer_only_ffn(cfg, l, seed, dtype)
+        aw = _layer_only_attention(cfg, l, seed, dtype, device)
+        fw = _layer_only_ffn(cfg, l, seed, dtype, device)
         t = _attn_layer_tensors(cfg, l, aw)
         t.update(_ffn_layer_tensors(cfg, l, fw))
         fname = f"model-layer-{l:05d}.safetensors"
-        save_file({k: v.contiguous() for k, v in t.items()}, os.path.join(path, fname),
+        save_file({k: v.contiguous().cpu() for k, v in t.items()}, os.path.join(path, fname),
                   metadata={"format": "pt"})
         weight_map.update({k: fname for k in t})
     with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
         json.dump({"metadata": {}, "weight_map": weight_map}, f, indent=1)
 
 
-def _layer_only_attention(cfg: ModelConfig, l: int, seed: int, dtype) -> AttentionLayerWeights:
+def _layer_only_attention(cfg: ModelConfig, l: int, seed: int, dtype,
+                          device="cpu") -> AttentionLayerWeights:
     std = cfg.initializer_range
     H, Q, KV, D = cfg.hidden_size, cfg.q_size, cfg.kv_size, cfg.head_dim
     p = f"layers.{l}."
     return AttentionLayerWeights(
-        in_norm=_norm_init(H, p + "in_norm", seed, "cpu", dtype),
-        w_qkv=torch.cat([_randn((Q, H), p + "q", seed, std, "cpu", dtype),
-                         _randn((KV, H), p + "k", seed, std, "cpu", dtype),
-                         _randn((KV, H), p + "v", seed, std, "cpu", dtype)]),
-        q_norm=_norm_init(D, p + "q_norm", seed, "cpu", dtype),
-        k_norm=_norm_init(D, p + "k_norm", seed, "cpu", dtype),
-        w_o=_randn((H, Q), p + "o", seed, std, "cpu", dtype),
+        in_norm=_norm_init(H, p + "in_norm", seed, device, dtype),
+        w_qkv=torch.cat([_randn((Q, H), p + "q", seed, std, device, dtype),
+                         _randn((KV, H), p + "k", seed, std, device, dtype),
+                         _randn((KV, H), p + "v", seed, std, device, dtype)]),
+        q_norm=_norm_init(D, p + "q_norm", seed, device, dtype),
+        k_norm=_norm_init(D, p + "k_norm", seed, device, dtype),
+        w_o=_randn((H, Q), p + "o", seed, std, device, dtype),
     )
 
 
-def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype) -> FFNLayerWeights:
+def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype, device="cpu") -> FFNLayerWeights:
     # same per-tensor seeds as random_ffn_weights, one layer at a time
     std = cfg.initializer_range
     H, I, E = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts
     p = f"layers.{l}."
-    lw = FFNLayerWeights(post_norm=_norm_init(H, p + "post_norm", seed, "cpu", dtype))
+    lw = FFNLayerWeights(post_norm=_norm_init(H, p + "post_norm", seed, device, dtype))
     if cfg.is_sparse_layer(l):
-        lw.w_router = _randn((E, H), p + "router", seed, std, "cpu", dtype)
+        lw.w_router = _randn((E, H), p + "router", seed, std, device, dtype)
         lw.w_gate_up = torch.stack([
-            torch.cat([_randn((I, H), p + f"e{e}.gate", seed, std, "cpu", dtype),
-                       _randn((I, H), p + f"e{e}.up", seed, std, "cpu", dtype)]) for e in range(E)])
-        lw.w_down = torch.stack([_randn((H, I), p + f"e{e}.down", seed, std, "cpu", dtype)
+            torch.cat([_randn((I, H), p + f"e{e}.gate", seed, std, device, dtype),
+                       _randn((I, H), p + f"e{e}.up", seed, std, device, dtype)]) for e in range(E)])
+        lw.w_down = torch.stack([_randn((H, I), p + f"e{e}.down", seed, std, device, dtype)
                                  for e in range(E)])
     else:
         DI = cfg.intermediate_size
-        lw.w_dense_gate_up = torch.cat([_randn((DI, H), p + "dense.gate", seed, std, "cpu", dtype),
-                                        _randn((DI, H), p + "dense.up", seed, std, "cpu", dtype)])
-        lw.w_dense_down = _randn((H, DI), p + "dense.down", seed, std, "cpu", dtype)
+        lw.w_dense_gate_up = torch.cat([_randn((DI, H), p + "dense.gate", seed, std, device, dtype),
+                                        _randn((DI, H), p + "dense.up", seed, std, device, dtype)])
+        lw.w_dense_down = _randn((H, DI), p + "dense.down", seed, std, device, dtype)
     return lw
 
 

@@ -27,7 +27,7 @@
 // which the last CTA to finish raises a release flag on every peer. That is
 // the fused attention->FFN hand-off of the o_proj GEMM.
 //
-// No cluster launch and no multicast: every TMA load reads this GPU's memory.
+// No cluster launch: every TMA load is issued per CTA and reads this GPU's memory.
 
 #include <cuda.h>
 #include <cuda_bf16.h>

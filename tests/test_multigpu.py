@@ -94,7 +94,7 @@ def _single_entry(i, d):
 
 
 @pytest.mark.parametrize("impl", ["fused", "nccl"])
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_matches_single(single, impl, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
