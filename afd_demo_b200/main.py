@@ -88,7 +88,13 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--prefill-warmup-rounds", type=int, default=None)
     p.add_argument("--backend", choices=["auto", "cuda", "cpu"], default="auto")
     p.add_argument("--comm-impl", choices=["auto", "fused", "nccl"], default="auto")
-    p.add_argument("--comm-timeout-ms", type=float, default=10000.0)
+    p.add_argument("--comm-timeout-ms", type=float, default=10000.0,
+                   help="bound of every device-side flag wait of the fused transport")
+    p.add_argument("--pg-timeout-s", type=float, default=None,
+                   help="process-group timeout (default max(60, 6 x comm timeout))")
+    p.add_argument("--detect-failures", action="store_true",
+                   help="heartbeats and a failure key in the rendezvous store; ranks stop "
+                        "before their next step when another rank failed")
     p.add_argument("--synthetic", action="store_true",
                    help="uniform random token ids instead of a tokenised prompt")
     p.add_argument("--random-init", action="store_true")
@@ -153,7 +159,9 @@ def build_distributed_config(args):
                              attn_node_rank=args.attn_node_rank,
                              ffn_node_rank=args.ffn_node_rank, n_attn=args.attn_gpus,
                              n_ffn=args.ffn_gpus,
-                             timeout_s=max(60.0, args.comm_timeout_ms / 1000 * 6))
+                             timeout_s=(args.pg_timeout_s if args.pg_timeout_s else
+                                        max(60.0, args.comm_timeout_ms / 1000 * 6)),
+                             detect_failures=args.detect_failures)
 
 
 def _load_tokenizer(model_name: str, logger):
@@ -417,11 +425,21 @@ def main(argv=None) -> int:
             run_generation_demo(args)
     except torch.cuda.OutOfMemoryError as e:
         logging.error(f"OutOfMemoryError: {e}")
+        _report(f"OutOfMemoryError: {e}")
         return 2
     except Exception as e:
         logging.error(f"Error: {e}", exc_info=True)
+        _report(f"{type(e).__name__}: {e}")
         return 1
     return 0
+
+
+def _report(reason: str) -> None:
+    from .parallel.dist import get_distributed_context
+
+    ctx = get_distributed_context()
+    if ctx.initialized:
+        ctx.report_failure(reason)
 
 
 if __name__ == "__main__":

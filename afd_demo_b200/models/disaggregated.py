@@ -30,7 +30,9 @@ import torch
 from .. import ops
 from ..config import ModelConfig, Topology, resolve_model_config
 from ..parallel.dist import DistributedContext, get_distributed_context
+from ..parallel import faults
 from ..parallel.engine import PipelineEngine
+from ..parallel.health import AFDPeerFailure
 from ..parallel.micro_batch import ForwardPlan, additive_causal_mask, make_plan
 from ..parallel.transport import LocalTransport, NcclTransport, PeerTransport, Transport
 from ..utils import device as devmod
@@ -165,6 +167,7 @@ class DisaggregatedQwenModel:
             from ..parallel.dist import DistributedConfig
             ctx.initialize(DistributedConfig(world_size=1, backend=devmod.DIST_BACKEND))
         device = device if device is not None else ctx.device
+        faults.plan().on_load()
         m = cls(cfg, device, dtype, ctx)
         m.load_weights(model_name, random_init=random_init, seed=seed,
                        max_batch_size=max_batch_size, max_seq_len=max_seq_len)
@@ -254,8 +257,19 @@ class DisaggregatedQwenModel:
         self._graphs.clear()
 
     # --------------------------------------------------------- generation
+    def generate(self, *args, **kwargs) -> torch.Tensor:
+        """See ``_generate``. A failure on this rank is published to the
+        others (when failure detection is on) before it propagates."""
+        try:
+            return self._generate(*args, **kwargs)
+        except AFDPeerFailure:
+            raise
+        except BaseException as e:
+            self.ctx.report_failure(f"{type(e).__name__}: {e}")
+            raise
+
     @torch.no_grad()
-    def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 50, temperature: float = 1.0,
+    def _generate(self, input_ids: torch.Tensor, max_new_tokens: int = 50, temperature: float = 1.0,
                  top_k: int = 50, top_p: float = 0.9, do_sample: bool = True,
                  eos_token_id: Optional[int] = None, pad_token_id: Optional[int] = None,
                  use_decode_dbo: bool = True, num_decode_micro_batches: int = 2,
@@ -309,7 +323,11 @@ class DisaggregatedQwenModel:
         ctx.barrier()
         steps = max(max_new_tokens - 1, 0)
         t_d0 = ev()
+        fault_plan = faults.plan()
         for step in range(steps):
+            if fault_plan.active:
+                fault_plan.before_step(ctx.rank, step)
+            ctx.check_health()
             if is_attn:
                 if host_io and cuda:
                     pinned.copy_(next_tok, non_blocking=True)     # D2H: the step's result

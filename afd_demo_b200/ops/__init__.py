@@ -138,24 +138,28 @@ def _k_splits(tiles: int, k_iters: int) -> int:
 
 
 class _SplitKWorkspace:
-    """Zero-initialised fp32 partial-sum buffer and tile counters for split-K
-    GEMMs. The kernel leaves both zeroed after every launch, so one buffer is
-    reused forever; it is private to one stream (two streams never share)."""
+    """fp32 partial-sum slices (one per split) and zero-initialised tile
+    counters for split-K GEMMs. The kernel resets the counters after every
+    launch, so one pair is reused forever; it is private to one stream (two
+    streams never share)."""
 
     _pool: dict = {}
+    _retired: list = []  # outgrown buffers stay alive: captured graphs may hold them
 
     @classmethod
-    def get(cls, device, tiles: int, block_n: int):
+    def get(cls, device, tiles: int, block_n: int, splits: int):
         stream = torch.cuda.current_stream(device)
         key = (device.index, stream.cuda_stream)
-        need = tiles * block_n * 128
+        need = splits * tiles * block_n * 128
         ws = cls._pool.get(key)
         if ws is None or ws[0].numel() < need or ws[1].numel() < tiles:
             old = ws
             n = max(need, old[0].numel() if old else 0)
             t = max(tiles, old[1].numel() if old else 0)
-            ws = (torch.zeros(n, device=device, dtype=torch.float32),
+            ws = (torch.empty(n, device=device, dtype=torch.float32),
                   torch.zeros(t, device=device, dtype=torch.int32))
+            if old is not None:
+                cls._retired.append(old)
             cls._pool[key] = ws
         return ws
 
@@ -182,7 +186,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
     splits = _k_splits(tiles, K // 64) if T <= 256 else 1
     ws = cnt = None
     if splits > 1:
-        ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn)
+        ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)
     ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn,
                tiles * splits, list(peers), int(peer_row_offset), list(flags), int(signal_value),
                done_counter, status, epoch, splits, ws, cnt, None)

@@ -46,6 +46,10 @@ class DistributedConfig:
     n_attn: Optional[int] = None
     n_ffn: Optional[int] = None
     timeout_s: float = 600.0
+    # host-side failure detection (heartbeats + failure key in the store)
+    detect_failures: bool = False
+    heartbeat_s: float = 0.2
+    dead_after_s: float = 5.0
 
 
 class DistributedContext:
@@ -69,6 +73,7 @@ class DistributedContext:
         self._a2f_group = None
         self._f2a_group = None
         self._warmup_result = None
+        self.monitor = None
 
     # ------------------------------------------------------------------
     def initialize(self, config: Optional[DistributedConfig] = None) -> None:
@@ -96,6 +101,11 @@ class DistributedContext:
             if config.backend == "nccl":
                 kwargs["device_id"] = torch.device(f"cuda:{config.local_rank}")
             dist.init_process_group(**kwargs)
+        if config.world_size > 1 and config.detect_failures:
+            from .health import PeerMonitor
+            store = dist.distributed_c10d._get_default_store()
+            self.monitor = PeerMonitor(store, config.rank, config.world_size,
+                                       config.heartbeat_s, config.dead_after_s)
         self._ready = True
         logger.info(f"distributed ready: rank={config.rank}/{config.world_size} role={self.role} "
                     f"topology={self.topology.tag()}")
@@ -206,9 +216,22 @@ class DistributedContext:
             else:
                 dist.barrier()
 
+    def check_health(self) -> None:
+        """Raise ``AFDPeerFailure`` if another rank failed (between steps)."""
+        if self.monitor is not None:
+            self.monitor.check()
+
+    def report_failure(self, reason: str) -> None:
+        """Tell the other ranks that this one is failing."""
+        if self.monitor is not None:
+            self.monitor.report(reason)
+
     def cleanup(self) -> None:
         """Destroy the process group (NCCL 2.28 tears down cleanly; the
         reference skips this for an NCCL 2.26 teardown crash)."""
+        if self.monitor is not None:
+            self.monitor.stop()
+            self.monitor = None
         if dist.is_initialized():
             try:
                 dist.destroy_process_group()

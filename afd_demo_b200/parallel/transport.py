@@ -27,6 +27,7 @@ whole forward and a captured CUDA graph can replay it.
 
 from __future__ import annotations
 
+import datetime
 import logging
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -34,6 +35,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
+from . import faults
 from .micro_batch import ForwardPlan
 
 logger = logging.getLogger(__name__)
@@ -139,16 +141,33 @@ class NcclTransport(Transport):
         (src/pipeline/decode_scheduler.py:122-125)."""
         return 10000 + l * (num_mb * 2) + m * 2 + (0 if direction == "a2f" else 1)
 
+    def _wait(self, w) -> None:
+        """Wait for a p2p work item, bounded by the process-group timeout so
+        that a peer that is gone or a message that never comes ends as an
+        error. gloo p2p work items wait forever unless given a timeout (and
+        cannot be polled); an NCCL wait only orders streams on the host, and
+        NCCL's watchdog aborts the communicator when the timeout expires."""
+        try:
+            if self.device.type == "cpu":
+                w.wait(timeout=datetime.timedelta(seconds=self.ctx.config.timeout_s))
+            else:
+                w.wait()
+        except RuntimeError as e:
+            if "Timed out" in str(e) or "timeout" in str(e).lower():
+                raise AFDCommTimeout(f"p2p wait timed out: {e}") from e
+            raise
+
     def _retire_sends(self, l: int, m: int) -> None:
         for w, _t in self._pending_send.pop((l, m), []):
-            w.wait()
+            self._wait(w)
 
     # attention side ---------------------------------------------------
     def a2f_send(self, l, m, h):
         if l > 0:
             self._retire_sends(l - 1, m)
         h = h.contiguous()
-        works = [(dist.isend(h, dst=f, group=self._a2f_group), h) for f in self.ctx.ffn_ranks()]
+        works = [] if faults.plan().drop("a2f", l, m) else \
+            [(dist.isend(h, dst=f, group=self._a2f_group), h) for f in self.ctx.ffn_ranks()]
         self._pending_send[(l, m)] = works
         if self.crosslayer:
             self.post_f2a_recv(l, m)
@@ -168,7 +187,7 @@ class NcclTransport(Transport):
         self.post_f2a_recv(l, m)
         works, bufs = self._posted_recv.pop((l, m))
         for w in works:
-            w.wait()
+            self._wait(w)
         return bufs
 
     # FFN side ------------------------------------------------------------
@@ -180,7 +199,7 @@ class NcclTransport(Transport):
             o, n = slot.seg_offsets[a], slot.seg_tokens[a]
             works.append(dist.irecv(buf[o:o + n], src=r, group=self._a2f_group))
         for w in works:
-            w.wait()
+            self._wait(w)
         return buf
 
     def f2a_send(self, l, m, out):
@@ -188,10 +207,11 @@ class NcclTransport(Transport):
             self._retire_sends(l - 1, m)
         slot = self.plan.ffn_slots[m]
         works = []
-        for a, r in enumerate(self.ctx.attn_ranks()):
-            o, n = slot.seg_offsets[a], slot.seg_tokens[a]
-            part = out[o:o + n].contiguous()
-            works.append((dist.isend(part, dst=r, group=self._f2a_group), part))
+        if not faults.plan().drop("f2a", l, m):
+            for a, r in enumerate(self.ctx.attn_ranks()):
+                o, n = slot.seg_offsets[a], slot.seg_tokens[a]
+                part = out[o:o + n].contiguous()
+                works.append((dist.isend(part, dst=r, group=self._f2a_group), part))
         self._pending_send[(l, m)] = works
 
     def end(self) -> None:
@@ -199,7 +219,7 @@ class NcclTransport(Transport):
             self._retire_sends(*key)
         for works, _ in self._posted_recv.values():
             for w in works:
-                w.wait()
+                self._wait(w)
         self._posted_recv.clear()
 
 
@@ -273,6 +293,7 @@ class PeerTransport(Transport):
         self.epoch = torch.zeros(1, device=device, dtype=torch.int32)
         self.status = torch.zeros(2, device=device, dtype=torch.int32)
         self.counters = torch.zeros(num_mb, device=device, dtype=torch.int32)
+        self._dropbox = torch.zeros(16, device=device, dtype=torch.int32)  # injected drops
         # exchange IPC handles (collective over all ranks)
         handle = bytes(self.C.ipc_handle(self.region))
         allh: List[Optional[bytes]] = [None] * ctx.world_size
@@ -330,7 +351,10 @@ class PeerTransport(Transport):
         a = self.ctx.attn_index
         off = self.plan.ffn_slots[m].seg_offsets[a]
         fr = self.ctx.ffn_ranks()
-        kw = self._common(l, m, [self._ffn_flag(self.peer_base[f], m, a) for f in fr])
+        flags = [self._ffn_flag(self.peer_base[f], m, a) for f in fr]
+        if faults.plan().drop("a2f", l, m):
+            flags = [self._dropbox.data_ptr()] * len(flags)  # raised here, seen by nobody
+        kw = self._common(l, m, flags)
         kw.update(peers=[self._ffn_data(self.peer_base[f], m) for f in fr], peer_row_offset=off,
                   status=self.status)
         return GemmSink(**kw)
@@ -354,7 +378,10 @@ class PeerTransport(Transport):
         f = self.ctx.ffn_index
         slot = self.plan.ffn_slots[m]
         ar = self.ctx.attn_ranks()
-        kw = self._common(l, m, [self._attn_flag(self.peer_base[a], m, f) for a in ar])
+        flags = [self._attn_flag(self.peer_base[a], m, f) for a in ar]
+        if faults.plan().drop("f2a", l, m):
+            flags = [self._dropbox.data_ptr()] * len(flags)
+        kw = self._common(l, m, flags)
         kw.update(peers=[self._attn_data(self.peer_base[a], m, f) for a in ar],
                   seg_offsets=list(slot.seg_offsets) + [slot.tokens], peer_row_offset=0)
         return GemmSink(**kw)

@@ -285,14 +285,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool emit = true;
       float* wsp = nullptr;
       if (!SWIGLU && k_splits > 1) {
-        // split-K: add this split's partial tile into the fp32 workspace
-        wsp = args.ws + (size_t)un.tile * BN * kBM + q * 32 + lane;
+        // split-K: store this split's partial tile into its own fp32 slice;
+        // the last split to finish sums the slices in split order, so the
+        // result does not depend on which split finished first
+        const size_t tile_elems = (size_t)BN * kBM;
+        wsp = args.ws + (size_t)un.tile * tile_elems + q * 32 + lane;
+        float* own = wsp + (size_t)un.split * tiles * tile_elems;
         for (int c = 0; c < blk.y; c += 16) {
           float acc[16];
           tmem_ld16(t_row + c, acc);
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c + j < blk.y) atomicAdd(wsp + (c + j) * kBM, acc[j]);
+            if (c + j < blk.y) __stcg(own + (c + j) * kBM, acc[j]);
         }
         tc_fence_before();
         __syncwarp();
@@ -308,14 +312,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < blk.y && emit; c += 16) {
         float acc[16];
         if (wsp != nullptr) {
-          // last split: read the reduced tile back and leave zeros behind
+          // last split: sum the partial slices in split order
+          const size_t split_stride = (size_t)tiles * BN * kBM;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             acc[j] = 0.f;
-            if (c + j < blk.y) {
-              acc[j] = __ldcg(wsp + (c + j) * kBM);
-              __stcg(wsp + (c + j) * kBM, 0.f);
-            }
+            if (c + j < blk.y)
+              for (int sp = 0; sp < k_splits; ++sp)
+                acc[j] += __ldcg(wsp + sp * split_stride + (c + j) * kBM);
           }
         } else {
           tmem_ld16(t_row + c, acc);

@@ -36,11 +36,11 @@ struct GemmArgs {
   const int* epoch;                // optional device epoch base (CUDA-graph replays)
   int* done_counter;               // nullptr: no signal
   int* status;                     // device status word pair (may be nullptr)
-  // split-K (dense, non-SwiGLU only): k_splits CTAs share a tile; partial
-  // sums go to ws[tile][row][128] (fp32) and tile_counters[tile] elects the
-  // last split, which reduces, re-zeroes ws and the counter, and runs the
-  // epilogue. ws and the counters must start zeroed and stay private to one
-  // stream.
+  // split-K (dense, non-SwiGLU only): k_splits CTAs share a tile; split s
+  // stores its partial sums to ws[s][tile][row][128] (fp32) and
+  // tile_counters[tile] elects the last split, which adds the slices in split
+  // order (deterministic), resets the counter and runs the epilogue. The
+  // counters must start zeroed; both buffers stay private to one stream.
   int k_splits;
   float* ws;
   int* tile_counters;

@@ -1,0 +1,135 @@
+"""Orchestration and reporting scripts on CPU: the experiment matrix over two
+gloo ranks with the tiny Qwen3-MoE, then the audit, report, Gantt and plot
+scripts on its output (the reference's integration testing is this matrix
+plus the baseline audit, scripts/run_experiment_matrix.sh and
+scripts/audit_experiment_baselines.py)."""
+
+import csv
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+from afd_demo_b200.scripts.experiment_baselines import (normalize_mode, resolve_serial_baseline,
+                                                        serial_cache_path)
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_mode_normalisation_and_baselines():
+    assert normalize_mode("prefill-dbo") == "prefill"
+    assert normalize_mode("decode_dbo_crosslayer") == "decode"
+    assert normalize_mode("serial") is None and normalize_mode(None) is None
+    cache = {"prefill_ms": 12.0, "decode_tpot_ms": 3.0, "decode_step_ms": 9.0}
+    assert resolve_serial_baseline(cache, "prefill-dbo").value_ms == 12.0
+    assert resolve_serial_baseline(cache, "decode-dbo").value_ms == 3.0
+    legacy = resolve_serial_baseline({"decode_step_ms": 9.0}, "decode")
+    assert not legacy.available and legacy.source == "legacy-decode-step-ms"
+    assert not resolve_serial_baseline({"total_time_ms": 5.0}, "prefill").available
+    assert not resolve_serial_baseline(cache, "serial").available
+    assert serial_cache_path(Path("r"), 4, 128, 20) == Path("r/serial/cache/b4_s128_t20.json")
+
+
+@pytest.fixture(scope="module")
+def matrix(tmp_path_factory):
+    res = tmp_path_factory.mktemp("matrix")
+    env = dict(os.environ, RESULTS_DIR=str(res), MODEL_PATH="tiny", GPUS="2",
+               MASTER_PORT=str(_free_port()), CUDA_VISIBLE_DEVICES="")
+    p = subprocess.run(["bash", "afd_demo_b200/scripts/run_experiment_matrix.sh", "--modes",
+                        "serial,prefill-dbo,decode-dbo,decode-dbo-crosslayer", "--batches", "2",
+                        "--seqs", "32", "--tokens", "4"],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    return res
+
+
+def test_matrix_summary_and_layout(matrix):
+    rows = list(csv.DictReader(open(matrix / "experiment_matrix_summary.csv")))
+    assert [r["mode"] for r in rows] == ["serial", "prefill-dbo", "decode-dbo",
+                                         "decode-dbo-crosslayer"]
+    assert all(r["status"] == "ok" for r in rows), rows
+    cache = json.load(open(matrix / "serial" / "cache" / "b2_s32_t4.json"))
+    assert cache["prefill_ms"] > 0 and cache["decode_tpot_ms"] > 0
+    for mode in ("prefill-dbo", "decode-dbo", "decode-dbo-crosslayer"):
+        for role in ("attention", "ffn"):
+            d = json.load(open(matrix / mode / f"timing_{role}_{mode}_b2_s32_t4.json"))
+            assert d["node"] == role and d["num_layers"] == 2 and d["events"]
+            assert {e["type"] for e in d["events"]} <= {
+                "attn_compute", "ffn_compute", "moe_router", "moe_experts",
+                "moe_shared_or_dense", "send_start", "send_transfer", "recv_post", "recv_wait"}
+        assert (matrix / mode / f"report_{mode}_b2_s32_t4.md").exists()
+
+
+def test_matrix_uses_serial_cache(matrix):
+    env = dict(os.environ, RESULTS_DIR=str(matrix), MODEL_PATH="tiny", GPUS="2",
+               MASTER_PORT=str(_free_port()), CUDA_VISIBLE_DEVICES="")
+    p = subprocess.run(["bash", "afd_demo_b200/scripts/run_experiment_matrix.sh", "--modes",
+                        "serial", "--batches", "2", "--seqs", "32", "--tokens", "4"],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0
+    rows = list(csv.DictReader(open(matrix / "experiment_matrix_summary.csv")))
+    assert rows[-1]["status"] == "cached"
+
+
+def test_audit_pairs_every_dbo_row(matrix, tmp_path):
+    out = tmp_path / "audit.csv"
+    p = subprocess.run([sys.executable, "-m", "afd_demo_b200.scripts.audit_experiment_baselines",
+                        "--root", str(matrix), "--output-csv", str(out)],
+                       cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stderr
+    rows = list(csv.DictReader(open(out)))
+    assert list(rows[0]) == ["root", "mode", "tag", "batch", "seq", "tokens", "status",
+                             "serial_cache", "serial_baseline_ms", "dbo_ms", "speedup", "note"]
+    assert len(rows) == 3 and all(r["status"] == "ok" for r in rows), rows
+    assert {r["mode"] for r in rows} == {"prefill", "decode"}
+
+
+def test_report_gantt_and_plot_all(matrix, tmp_path):
+    mode = "decode-dbo-crosslayer"
+    attn = matrix / mode / f"timing_attention_{mode}_b2_s32_t4.json"
+    ffn = matrix / mode / f"timing_ffn_{mode}_b2_s32_t4.json"
+    rep = tmp_path / "r.md"
+    p = subprocess.run([sys.executable, "-m", "afd_demo_b200.scripts.gen_experiment_report",
+                        "--attn-timing", str(attn), "--ffn-timing", str(ffn), "--output", str(rep),
+                        "--mode", mode, "--batch", "2", "--seq", "32", "--tokens", "4",
+                        "--serial-baseline", str(matrix / "serial/cache/b2_s32_t4.json")],
+                       cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stderr
+    text = rep.read_text()
+    assert "|" in text and "TPOT" in text
+    png = tmp_path / "g.png"
+    p = subprocess.run([sys.executable, "-m", "afd_demo_b200.scripts.visualize_dbo_pipeline",
+                        "--attn-timing", str(attn), "--ffn-timing", str(ffn), "--output", str(png),
+                        "--num-layers", "2"], cwd=ROOT, capture_output=True, text=True,
+                       timeout=120)
+    assert p.returncode == 0, p.stderr
+    assert png.read_bytes()[:8] == b"\x89PNG\r\n\x1a\n"
+    p = subprocess.run([sys.executable, "-m", "afd_demo_b200.scripts.plot_all_pipelines",
+                        "--root", str(matrix)], cwd=ROOT, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stderr
+    assert list(matrix.glob("*/pipelines_index.md"))
+
+
+def test_run_single_oom_exit_code(tmp_path):
+    """A run whose log shows an out-of-memory error exits 2 (the matrix's
+    stop-escalating signal); an impossible batch on a 4-sequence cache does."""
+    env = dict(os.environ, RESULTS_DIR=str(tmp_path), MODEL_PATH="tiny", GPUS="1",
+               CUDA_VISIBLE_DEVICES="", AFD_FAULT="oom")
+    p = subprocess.run(["bash", "afd_demo_b200/scripts/run_single.sh", "local", "2", "16",
+                        "--tokens", "2"], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 2, p.stdout[-2000:]
+    assert "OOM DETECTED" in p.stdout
