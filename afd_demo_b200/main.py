@@ -100,11 +100,43 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--random-init", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cuda-graph", action="store_true", help="capture decode steps")
+    p.add_argument("--config", type=str, default=None,
+                   help="YAML run configuration (flag defaults; the command line overrides)")
     return p
 
 
+def load_yaml_defaults(path: str, parser: argparse.ArgumentParser) -> dict:
+    """Flag defaults from a YAML run configuration: every leaf key (at any
+    nesting depth) that names a CLI flag (``-`` written as ``_``) becomes
+    that flag's default. Unknown keys are an error."""
+    import yaml
+
+    with open(path) as f:
+        tree = yaml.safe_load(f) or {}
+    known = {a.dest for a in parser._actions}
+    out = {}
+
+    def walk(node, where):
+        for k, v in node.items():
+            if isinstance(v, dict):
+                walk(v, f"{where}{k}.")
+            elif k in known:
+                out[k] = v
+            else:
+                raise ValueError(f"{path}: unknown key {where}{k}")
+
+    walk(tree, "")
+    return out
+
+
 def parse_args(argv=None):
-    return build_parser().parse_args(argv)
+    p = build_parser()
+    pre = argparse.ArgumentParser(add_help=False)
+    pre.add_argument("--config", default=None)
+    known, _ = pre.parse_known_args(argv)
+    if known.config:
+        p.set_defaults(**load_yaml_defaults(known.config, p))
+    return p.parse_args(argv)
 
 
 def get_dtype(name: str) -> torch.dtype:

@@ -305,3 +305,15 @@ def test_prompt_padding_fixed_and_dynamic():
     assert fixed["input_ids"].shape == (3, 8) and n == 8
     dyn, _ = tokenize_batch_prompts(tok, ["abcd"] * 2, None, 128)
     assert dyn["input_ids"].shape == (2, 4)
+
+
+def test_yaml_run_config(tmp_path):
+    from afd_demo_b200.main import parse_args
+
+    a = parse_args(["--config", "afd_demo_b200/configs/qwen3_30b.yaml", "--batch-size", "8"])
+    assert a.batch_size == 8  # command line wins
+    assert a.prefill_seq_len == 256 and a.crosslayer and a.cuda_graph and a.greedy
+    bad = tmp_path / "bad.yaml"
+    bad.write_text("pipeline:\n  not_a_flag: 1\n")
+    with pytest.raises(ValueError):
+        parse_args(["--config", str(bad)])
