@@ -22,7 +22,7 @@ _C = None
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
                  "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
-                 "decode_attention_fused", "moe_route"}
+                 "decode_attention_fused", "moe_route", "moe_gate"}
 
 
 class LaunchCounter:
@@ -354,6 +354,42 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                               peer_row_offset, flags, signal_value, done_counter, epoch)
 
 
+_GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate kernel
+
+
+def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
+    return (T * top_k <= _GATE_MAX_ENTRIES and H <= 4096 and H % 8 == 0 and E <= 256
+            and E % 8 == 0 and top_k <= 16 and _gate_groups(T, E) > 0)
+
+
+def _gate_groups(T: int, E: int) -> int:
+    """Expert groups per token for the fused gate: enough CTAs (T * G ~ 256)
+    to spread the router weight reads, at least one expert per warp."""
+    g = 1
+    while T * g < 256 and E % (g * 2 * 8) == 0:
+        g *= 2
+    return g if E % g == 0 else 0
+
+
+class _GateCounters:
+    """Zeroed int32 counters of the fused gate kernel (it leaves them zeroed),
+    one buffer per (device, stream); outgrown buffers stay alive for graphs."""
+
+    _pool: dict = {}
+    _retired: list = []
+
+    @classmethod
+    def get(cls, device, T: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        c = cls._pool.get(key)
+        if c is None or c.numel() < T + 1:
+            if c is not None:
+                cls._retired.append(c)
+            c = torch.zeros(max(T + 1, 257), device=device, dtype=torch.int32)
+            cls._pool[key] = c
+        return c
+
+
 def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
             w_gate_up: torch.Tensor, w_down: torch.Tensor, top_k: int, eps: float,
             norm_topk_prob: bool = True, expert_start: int = 0, add_residual: bool = True,
@@ -379,10 +415,25 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
     E = w_router.shape[0]
     E_loc, I2, _ = w_gate_up.shape
     mark(True, "router")
-    xn = rmsnorm(h, post_norm_w, eps)
-    logits = linear(xn, w_router) if E % 128 == 0 else torch.nn.functional.linear(xn, w_router)
     ws = MoEWorkspace(T, top_k, E_loc, H, I2 // 2, _moe_block_n(T), h.device, h.dtype)
     C = ext()
+    if _gate_fusable(T, H, E, top_k):
+        # decode sizes: norm + router + top-k + routing in one launch
+        xn = torch.empty_like(h)
+        logits = torch.empty(T, E, device=h.device, dtype=h.dtype)
+        C.moe_gate(h, post_norm_w, w_router, xn, logits, ws.ids, ws.weights,
+                   _GateCounters.get(h.device, T), top_k, bool(norm_topk_prob), float(eps),
+                   _gate_groups(T, E), expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                   ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+        mark(False, "router")
+        mark(True, "experts")
+        y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T,
+                               top_k, peers, seg_offsets, peer_row_offset, flags, signal_value,
+                               done_counter, epoch)
+        mark(False, "experts")
+        return y
+    xn = rmsnorm(h, post_norm_w, eps)
+    logits = linear(xn, w_router) if E % 128 == 0 else torch.nn.functional.linear(xn, w_router)
     if T * top_k <= 4096 and E <= 256:
         C.moe_route(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob), expert_start, E_loc,
                     ws.block_n, ws.inv, ws.row_token, ws.row_weight, ws.expert_offsets,

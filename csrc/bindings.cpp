@@ -302,6 +302,53 @@ void moe_route(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, i
   check_rc(afd::launch_moe_route(r, a, cur_stream()), "moe_route");
 }
 
+// post-attention RMSNorm + router + top-k + routing, one launch (decode
+// sizes); counters: int32 [>= T + 1], zeroed once and left zeroed
+void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w_router,
+              at::Tensor& xn, at::Tensor& logits, at::Tensor& ids, at::Tensor& weights,
+              at::Tensor& counters, int64_t top_k, bool renorm, double eps, int64_t groups,
+              int64_t expert_start, int64_t n_local, int64_t block_n, at::Tensor& inv,
+              at::Tensor& row_token, at::Tensor& row_weight, at::Tensor& expert_offsets,
+              at::Tensor& blocks, at::Tensor& num_blocks, at::Tensor& num_rows) {
+  TORCH_CHECK(h.stride(1) == 1 && xn.is_contiguous() && logits.is_contiguous() &&
+                  w_router.is_contiguous(),
+              "moe_gate: contiguous rows expected");
+  const int T = (int)h.size(0);
+  TORCH_CHECK(counters.numel() >= T + 1, "moe_gate: counter buffer too small");
+  afd::MoeGateArgs g{};
+  g.h = cbf(h);
+  g.ld_h = (int)h.stride(0);
+  g.norm_w = cbf(norm_w);
+  g.w_router = cbf(w_router);
+  g.xn = bf(xn);
+  g.logits = bf(logits);
+  g.ids = ids.data_ptr<int32_t>();
+  g.weights = weights.data_ptr<float>();
+  g.tok_cnt = counters.data_ptr<int32_t>();
+  g.done_cnt = counters.data_ptr<int32_t>() + T;
+  g.T = T;
+  g.H = (int)h.size(1);
+  g.E = (int)w_router.size(0);
+  g.G = (int)groups;
+  g.top_k = (int)top_k;
+  g.renorm = renorm ? 1 : 0;
+  g.eps = (float)eps;
+  afd::MoeAlignArgs a{};
+  a.T = T;
+  a.top_k = g.top_k;
+  a.expert_start = (int)expert_start;
+  a.n_local = (int)n_local;
+  a.block_n = (int)block_n;
+  a.inv = inv.data_ptr<int32_t>();
+  a.row_token = row_token.data_ptr<int32_t>();
+  a.row_weight = row_weight.data_ptr<float>();
+  a.expert_offsets = expert_offsets.data_ptr<int32_t>();
+  a.blocks = reinterpret_cast<int4*>(blocks.data_ptr<int32_t>());
+  a.num_blocks = num_blocks.data_ptr<int32_t>();
+  a.num_rows = num_rows.data_ptr<int32_t>();
+  check_rc(afd::launch_moe_gate(g, a, cur_stream()), "moe_gate");
+}
+
 void moe_gather(const at::Tensor& x, const at::Tensor& row_token, const at::Tensor& num_rows,
                 at::Tensor& out, int64_t max_rows) {
   afd::MoeGatherArgs a{};
@@ -457,6 +504,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &router_topk);
   m.def("moe_align", &moe_align);
   m.def("moe_route", &moe_route);
+  m.def("moe_gate", &moe_gate);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("argmax", &argmax);

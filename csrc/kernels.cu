@@ -365,6 +365,124 @@ int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s)
   return (int)launch_k(moe_route_kernel, dim3(1), dim3(kAlignThreads), 0, s, r, a);
 }
 
+// ------------------------------------------- fused MoE gate (decode) ---
+// Post-attention RMSNorm + router GEMV + softmax/top-k/renormalise + routing
+// in one launch for small token counts. CTA (t, g) normalises token t (same
+// roundings as sum_rmsnorm_kernel; group 0 stores xn), then computes the
+// router logits of experts [g * E/G, (g+1) * E/G) with CUDA-core dot products
+// (fp32 accumulation, one bf16 rounding). The last of a token's G CTAs (per-
+// token counter) runs that token's top-k; the last token to finish (global
+// counter) runs the routing of moe_align_kernel. Counters are reset by the
+// CTAs that consume them, so the buffer stays zeroed between launches.
+constexpr int kGateThreads = 256;
+constexpr int kGateMaxH = 4096;
+constexpr int kGateMaxEntries = 2048;
+
+__global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, MoeAlignArgs a) {
+  __shared__ float xn_s[kGateMaxH];
+  __shared__ float red[kGateThreads / 32];
+  __shared__ __nv_bfloat16 lg_s[256];
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  __shared__ int32_t s_ids[kGateMaxEntries];
+  __shared__ float s_w[kGateMaxEntries];
+  __shared__ int s_flag;
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x / g.G;
+  const int grp = blockIdx.x % g.G;
+  const int H = g.H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // 1. RMSNorm of token t
+  constexpr int kChunks = kGateMaxH / (kGateThreads * 8);
+  float xv[kChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) {
+      load8(g.h + (size_t)t * g.ld_h + col, xv[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += xv[c][i] * xv[c][i];
+    }
+  }
+  const float tot = block_sum<kGateThreads>(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + g.eps);
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) {
+      float w[8], y[8];
+      load8(g.norm_w + col, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[i] = round_bf16(w[i] * round_bf16(xv[c][i] * rstd));
+        xn_s[col + i] = y[i];
+      }
+      if (grp == 0) store8(g.xn + (size_t)t * H + col, y);
+    }
+  }
+  __syncthreads();
+
+  // 2. router logits of this CTA's experts: warp w takes experts w, w + 8, ...
+  const int per_grp = g.E / g.G;
+  for (int j = warp; j < per_grp; j += kGateThreads / 32) {
+    const int e = grp * per_grp + j;
+    const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
+    float acc = 0.f;
+    for (int col = lane * 8; col < H; col += 32 * 8) {
+      float w[8];
+      load8(wr + col, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += w[i] * xn_s[col + i];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
+  }
+
+  // 3. the token's last CTA: softmax / top-k / renormalise
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[t], 1) == g.G - 1);
+  __syncthreads();
+  if (!s_flag) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < g.E; e += kGateThreads)
+    lg_s[e] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
+                                          (size_t)t * g.E + e));
+  __syncthreads();
+  if (warp == 0)
+    topk_token(lg_s, g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
+               g.weights + (size_t)t * g.top_k);
+  if (threadIdx.x == 0) g.tok_cnt[t] = 0;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == g.T - 1);
+  __syncthreads();
+  if (!s_flag) return;
+
+  // 4. the last token: routing over all T tokens
+  __threadfence();
+  const int n = g.T * g.top_k;
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    s_ids[i] = __ldcg(g.ids + i);
+    s_w[i] = __ldcg(g.weights + i);
+  }
+  __syncthreads();
+  align_body(s_ids, s_w, a, cnt, off, boff);
+  if (threadIdx.x == 0) *g.done_cnt = 0;
+}
+
+int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
+  if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % g.G != 0 ||
+      g.top_k > 16 || g.H > kGateMaxH || g.H % 8 != 0 || a.n_local > kMaxLocalExperts ||
+      a.block_n <= 0)
+    return 1;
+  return (int)launch_k(moe_gate_kernel, dim3(g.T * g.G), dim3(kGateThreads), 0, s, g, a);
+}
+
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
 __global__ void moe_gather_kernel(MoeGatherArgs a) {
   pdl_wait();

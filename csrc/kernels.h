@@ -97,6 +97,22 @@ struct MoeAlignArgs {
   int32_t* num_rows;            // device scalar
 };
 
+// Fused post-attention RMSNorm + router + top-k + routing (moe_gate_kernel).
+struct MoeGateArgs {
+  const __nv_bfloat16* h;        // [T, ld_h] FFN input (attn_out + residual)
+  int ld_h;
+  const __nv_bfloat16* norm_w;   // [H]
+  const __nv_bfloat16* w_router; // [E, H]
+  __nv_bfloat16* xn;             // [T, H] normalised input (out)
+  __nv_bfloat16* logits;         // [T, E] scratch
+  int32_t* ids;                  // [T, top_k] (out)
+  float* weights;                // [T, top_k] (out)
+  int* tok_cnt;                  // [T] zeroed, self-cleaning
+  int* done_cnt;                 // [1] zeroed, self-cleaning
+  int T, H, E, G, top_k, renorm;
+  float eps;
+};
+
 struct MoeGatherArgs {
   const __nv_bfloat16* x;
   int ld_x;
@@ -155,6 +171,8 @@ int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s);
 // router top-k + moe_align in one launch (T * top_k <= 4096)
 int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s);
 int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s);
+// RMSNorm + router + top-k + routing in one launch (T * top_k <= 2048, H <= 4096)
+int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s);
 int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s);
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
                   cudaStream_t s);
