@@ -22,7 +22,7 @@ _C = None
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
                  "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
-                 "decode_attention_fused", "moe_route", "moe_gate"}
+                 "decode_attention_fused", "moe_route", "moe_gate", "gemm_down_combine"}
 
 
 class LaunchCounter:
@@ -297,6 +297,12 @@ class MoEWorkspace:
         self.block_n = block_n
 
 
+# token counts up to which the MoE combine runs inside the down GEMM (one CTA
+# per 128 output features sums every token's rows); larger batches use the
+# one-CTA-per-token combine kernel
+_FUSED_COMBINE_MAX_TOKENS = 256
+
+
 def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T, k, peers,
                        seg_offsets, peer_row_offset, flags, signal_value, done_counter, epoch):
     """Grouped gate_up GEMM (SwiGLU epilogue) -> grouped down GEMM
@@ -318,11 +324,19 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
            0, None, None, True, bn, ws.max_blocks * (I // 128), [], 0, [], 0, None, None, None,
            1, None, None, row_ids)
+    if out is None and not peers:
+        out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
+    if T <= _FUSED_COMBINE_MAX_TOKENS:
+        # combine (+ residual, + F2A stores, + flags) in the down GEMM's epilogue
+        C.gemm_down_combine(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, ws.blocks,
+                            ws.num_blocks, ws.row_weight, bn, ws.max_blocks * (H // 128), ws.inv,
+                            T, k, residual, out, list(peers), list(seg_offsets),
+                            int(peer_row_offset), list(flags), int(signal_value), done_counter,
+                            None, epoch, _CombineCounters.get(xn.device, H // 128))
+        return out
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
            None, ws.row_weight, False, bn, ws.max_blocks * (H // 128), [], 0, [], 0, None, None,
            None, 1, None, None, None)
-    if out is None and not peers:
-        out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
     C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
                   int(peer_row_offset), list(flags), int(signal_value), done_counter, epoch)
     return out
@@ -388,6 +402,13 @@ class _GateCounters:
             c = torch.zeros(max(T + 1, 257), device=device, dtype=torch.int32)
             cls._pool[key] = c
         return c
+
+
+class _CombineCounters(_GateCounters):
+    """Zeroed per-feature-tile counters of the fused combine."""
+
+    _pool: dict = {}
+    _retired: list = []
 
 
 def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,

@@ -100,7 +100,8 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   a.tile_counters = opt_ptr<int>(tile_counters);
   if (k_splits > 1) {
     const int64_t tiles = ((dense_rows + block_n - 1) / block_n) * f_tiles;
-    TORCH_CHECK(a.ws != nullptr && ws->numel() >= tiles * block_n * 128, "split-K workspace too small");
+    TORCH_CHECK(a.ws != nullptr && ws->numel() >= k_splits * tiles * block_n * 128,
+                "split-K workspace too small");
     TORCH_CHECK(a.tile_counters != nullptr && tile_counters->numel() >= tiles,
                 "split-K tile counters too small");
   }
@@ -116,6 +117,82 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   p.num_sms = num_sms();
   if (a.blocks == nullptr && dense_rows == 0) return;
   check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_swapab");
+}
+
+// Grouped down-projection GEMM (routing weight per row, rows to y) with the
+// MoE combine fused into its epilogue: combined rows (+ residual) go to `out`
+// (optional) and to the peers of each token segment, then the last CTA raises
+// the flags. cmb_counters: int32 [>= f_tiles], zeroed once, left zeroed.
+void gemm_down_combine(const at::Tensor& w, const at::Tensor& x, at::Tensor& y, int64_t f_tiles,
+                       int64_t w_rows_per_group, const at::Tensor& blocks,
+                       const at::Tensor& num_blocks, const at::Tensor& row_scale,
+                       int64_t block_n, int64_t units_hint, const at::Tensor& inv, int64_t T,
+                       int64_t top_k, const c10::optional<at::Tensor>& residual,
+                       const c10::optional<at::Tensor>& out, std::vector<int64_t> peers,
+                       std::vector<int64_t> seg_offsets, int64_t peer_row_offset,
+                       std::vector<int64_t> flags, int64_t signal_value,
+                       const c10::optional<at::Tensor>& done_counter,
+                       const c10::optional<at::Tensor>& status,
+                       const c10::optional<at::Tensor>& epoch, at::Tensor& cmb_counters) {
+  CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(y);
+  CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(y);
+  CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(y);
+  TORCH_CHECK(peers.size() <= (size_t)afd::kMaxPeers, "too many peers");
+  TORCH_CHECK(flags.size() <= (size_t)afd::kMaxPeers + 1, "too many flags");
+  TORCH_CHECK(seg_offsets.size() == (peers.empty() ? 0 : peers.size() + 1),
+              "seg_offsets needs n_peers + 1 entries");
+  TORCH_CHECK(cmb_counters.numel() >= f_tiles, "combine counters too small");
+  TORCH_CHECK(top_k <= 16 && inv.numel() >= T * top_k, "combine: bad inverse map");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(w.size(-1) == K, "K mismatch");
+  GemmLaunch p{};
+  afd::GemmArgs& a = p.args;
+  a.K = (int)K;
+  a.f_tiles = (int)f_tiles;
+  a.w_rows_per_group = (int)w_rows_per_group;
+  a.blocks = reinterpret_cast<const int4*>(blocks.data_ptr<int32_t>());
+  a.num_blocks = num_blocks.data_ptr<int32_t>();
+  a.out = bf(y);
+  a.ld_out = (int)y.stride(-2);
+  a.row_scale = row_scale.data_ptr<float>();
+  for (size_t i = 0; i < peers.size(); ++i) a.peer_out[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
+  a.n_peers = (int)peers.size();
+  for (size_t i = 0; i < seg_offsets.size(); ++i) a.cmb_seg_offsets[i] = (int)seg_offsets[i];
+  a.peer_row_offset = (int)peer_row_offset;
+  for (size_t i = 0; i < flags.size(); ++i) a.flags[i] = reinterpret_cast<int*>(flags[i]);
+  a.n_flags = (int)flags.size();
+  a.signal_value = (int)signal_value;
+  a.epoch = opt_ptr<const int>(epoch);
+  a.done_counter = opt_ptr<int>(done_counter);
+  a.status = opt_ptr<int>(status);
+  a.k_splits = 1;
+  a.cmb_inv = inv.data_ptr<int32_t>();
+  a.cmb_T = (int)T;
+  a.cmb_topk = (int)top_k;
+  if (residual.has_value() && residual->defined()) {
+    CHECK_BF16(*residual);
+    TORCH_CHECK(residual->stride(-1) == 1, "residual rows must be contiguous");
+    a.cmb_residual = cbf(*residual);
+    a.cmb_ld_res = (int)residual->stride(-2);
+  }
+  if (out.has_value() && out->defined()) {
+    CHECK_BF16(*out);
+    TORCH_CHECK(out->stride(-1) == 1, "out rows must be contiguous");
+    a.cmb_out = bf(*out);
+    a.cmb_ld_out = (int)out->stride(-2);
+  }
+  a.cmb_counters = cmb_counters.data_ptr<int32_t>();
+  p.w = w.data_ptr();
+  p.w_rows_total = w.numel() / K;
+  p.ld_w = w.stride(-2);
+  p.x = x.data_ptr();
+  p.x_rows = x.numel() / K;
+  p.ld_x = x.stride(-2);
+  p.swiglu = false;
+  p.block_n = (int)block_n;
+  p.units_hint = (int)units_hint;
+  p.num_sms = num_sms();
+  check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_down_combine");
 }
 
 void sum_rmsnorm(std::vector<at::Tensor> parts, const at::Tensor& weight,
@@ -505,6 +582,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_route", &moe_route);
   m.def("moe_gate", &moe_gate);
+  m.def("gemm_down_combine", &gemm_down_combine);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("argmax", &argmax);

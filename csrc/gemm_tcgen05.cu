@@ -90,6 +90,56 @@ __device__ __forceinline__ void epi_bar() {  // the 4 epilogue warps only
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// Fused MoE combine of output-feature tile ft (see GemmArgs::cmb_*), run by
+// the 128 epilogue threads: 16 threads x 8 features cover the tile's 128
+// features of one token; 8 tokens at a time. Same summation order and
+// roundings as moe_combine_kernel.
+__device__ void combine_feature_tile(const GemmArgs& a, int ft) {
+  const int et = threadIdx.x - 64;
+  const int col = ft * 128 + (et & 15) * 8;
+  const int Hf = a.f_tiles * 128;
+  for (int t = et >> 4; t < a.cmb_T; t += 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < a.cmb_topk; ++j) {
+      const int r = a.cmb_inv[(size_t)t * a.cmb_topk + j];
+      if (r < 0) continue;
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.out + (size_t)r * a.ld_out + col));
+      const uint32_t* pv = &v.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x0, x1;
+        unpack_bf16x2(pv[e], x0, x1);
+        acc[2 * e] += x0;
+        acc[2 * e + 1] += x1;
+      }
+    }
+    if (a.cmb_residual != nullptr) {
+      const uint4 rv =
+          *reinterpret_cast<const uint4*>(a.cmb_residual + (size_t)t * a.cmb_ld_res + col);
+      const uint32_t* pr = &rv.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float r0, r1;
+        unpack_bf16x2(pr[e], r0, r1);
+        acc[2 * e] = round_bf16(acc[2 * e]) + r0;
+        acc[2 * e + 1] = round_bf16(acc[2 * e + 1]) + r1;
+      }
+    }
+    uint4 u;
+    u.x = pack_bf16x2(acc[0], acc[1]);
+    u.y = pack_bf16x2(acc[2], acc[3]);
+    u.z = pack_bf16x2(acc[4], acc[5]);
+    u.w = pack_bf16x2(acc[6], acc[7]);
+    if (a.cmb_out != nullptr)
+      *reinterpret_cast<uint4*>(a.cmb_out + (size_t)t * a.cmb_ld_out + col) = u;
+    for (int sg = 0; sg < a.n_peers; ++sg)
+      if (t >= a.cmb_seg_offsets[sg] && t < a.cmb_seg_offsets[sg + 1])
+        *reinterpret_cast<uint4*>(
+            a.peer_out[sg] + (size_t)(t - a.cmb_seg_offsets[sg] + a.peer_row_offset) * Hf + col) =
+            u;
+  }
+}
+
 template <bool SWIGLU, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -368,7 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               v = make_uint4(o[0], o[1], o[2], o[3]);
             }
             *reinterpret_cast<uint4*>(args.out + (size_t)row * args.ld_out + col) = v;
-            for (int p = 0; p < args.n_peers; ++p)
+            if (args.cmb_inv == nullptr)
+              for (int p = 0; p < args.n_peers; ++p)
               *reinterpret_cast<uint4*>(
                   args.peer_out[p] + (size_t)(row + args.peer_row_offset) * args.ld_out + col) = v;
           }
@@ -382,7 +433,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[slot]);
+      if (args.cmb_inv != nullptr) {
+        // the CTA that stores the last row block of feature tile ft combines it
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64)
+          *last_flag = (atomicAdd(&args.cmb_counters[ft], 1) == tiles / args.f_tiles - 1);
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          combine_feature_tile(args, ft);
+          if (threadIdx.x == 64) args.cmb_counters[ft] = 0;
+        }
+      }
     }
+    // no local rows at all: the combine is residual-only (or zeros)
+    if (args.cmb_inv != nullptr && tiles == 0 && !*abort_flag && blockIdx.x < args.f_tiles)
+      combine_feature_tile(args, blockIdx.x);
   }
 
   tc_fence_before();

@@ -48,6 +48,23 @@ struct GemmArgs {
   // (TMA tile::gather4); nullptr: rows are contiguous in x
   const int* row_ids;
   int max_units;                   // upper bound on work units (set by the launcher)
+  // fused MoE combine (grouped, non-SwiGLU, e.g. the down projection): once
+  // every row block of output-feature tile ft is stored in `out`, the CTA that
+  // stored the last one sums, for each of cmb_T tokens, the token's top-k rows
+  // of `out` (cmb_inv[t * k + j], -1 = expert not local) in j order, adds the
+  // residual, and stores the tile's 128 features to cmb_out and to the peer
+  // buffer of the token's segment (peer_out[s] for cmb_seg_offsets[s] <= t <
+  // cmb_seg_offsets[s + 1], row t - cmb_seg_offsets[s] + peer_row_offset,
+  // row stride f_tiles * 128). In this mode peer_out/n_peers apply only to the
+  // combined rows. cmb_counters[f_tiles] start zeroed and are reset after use.
+  const int* cmb_inv;              // nullptr: no fused combine
+  int cmb_T, cmb_topk;
+  const __nv_bfloat16* cmb_residual;
+  int cmb_ld_res;
+  __nv_bfloat16* cmb_out;          // optional [cmb_T, cmb_ld_out]
+  int cmb_ld_out;
+  int cmb_seg_offsets[kMaxPeers + 1];
+  int* cmb_counters;
 };
 
 struct GemmLaunch {

@@ -219,3 +219,19 @@ def test_flags_roundtrip_and_timeout():
     C.wait_flags([base + 8], 1, status, 50_000_000, None)
     torch.cuda.synchronize()
     assert int(status[0]) == 2
+
+
+@pytest.mark.parametrize("with_residual", [True, False])
+def test_moe_experts_no_local_rows(with_residual):
+    """Every routed expert lives on another rank: the output is the residual
+    (or zeros) and the fused combine still writes every token."""
+    T, H, I = 3, 2048, 768
+    xn = _randn(T, H, seed=80)
+    h = _randn(T, H, seed=81)
+    wgu = _randn(32, 2 * I, H, scale=0.02, seed=82)
+    wd = _randn(32, H, I, scale=0.02, seed=83)
+    ids = torch.arange(64, 72, device=DEV, dtype=torch.int32).repeat(T, 1)
+    w = torch.full((T, 8), 0.125, device=DEV)
+    out = ops.moe_experts(xn, ids, w, wgu, wd, 0, residual=h if with_residual else None)
+    want = h if with_residual else torch.zeros_like(h)
+    assert torch.equal(out, want)
