@@ -59,14 +59,17 @@ class AttentionWorker:
 
     def forward_attention_layer(self, layer_idx: int, x_parts: Sequence[torch.Tensor],
                                 batch_offset: int, q_len: int, start_pos: Optional[int] = None,
-                                sink=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                                sink=None, out: Optional[torch.Tensor] = None,
+                                wait=None) -> torch.Tensor:
         """One attention block for the micro-batch whose sequences occupy cache
         rows [batch_offset, batch_offset + T // q_len). `x_parts` are the
-        layer inputs (the F2A partials); returns h = x + o_proj(attn)."""
+        layer inputs (the F2A partials); returns h = x + o_proj(attn). `wait`
+        (an ``ops.FlagWait``): the parts arrive from peers and the first kernel
+        waits for their flags."""
         cfg = self.cfg
         lw = self.w.layers[layer_idx]
         start = self.cache.seq_len if start_pos is None else start_pos
-        x, xn = ops.sum_rmsnorm(list(x_parts), lw.in_norm, cfg.rms_norm_eps)
+        x, xn = ops.sum_rmsnorm(list(x_parts), lw.in_norm, cfg.rms_norm_eps, wait=wait)
         qkv = ops.linear(xn, lw.w_qkv)
         k_l, v_l = self.cache.layer(layer_idx)
         if q_len == 1:  # decode: norm + RoPE + append folded into the attention kernel
@@ -85,10 +88,12 @@ class AttentionWorker:
         return ops.linear(o, lw.w_o, residual=x, out=out)
 
     def forward_lm_head(self, x_parts: Sequence[torch.Tensor], q_len: int = 1,
-                        last_only: bool = True) -> torch.Tensor:
+                        last_only: bool = True, wait=None) -> torch.Tensor:
         """Final RMSNorm + LM head. With `last_only`, only the last position of
         each sequence is projected (that is all sampling needs); returns
         [B, V] (or [T, V])."""
+        if wait is not None:
+            ops.wait_flags(wait)  # the parts are read by torch copies below
         H = self.cfg.hidden_size
         parts = [p.reshape(-1, H) for p in x_parts]
         if last_only and q_len > 1:

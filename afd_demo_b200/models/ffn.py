@@ -48,9 +48,10 @@ class FFNWorker:
 
     def forward_ffn_layer(self, layer_idx: int, hidden_states: torch.Tensor,
                           add_residual: bool = True, sink=None, out: Optional[torch.Tensor] = None,
-                          mb_idx: int = 0) -> torch.Tensor:
+                          mb_idx: int = 0, wait=None) -> torch.Tensor:
         """h [T, H] (= attn_out + residual) -> h + moe(norm(h)) [T, H], or only
-        the local experts' partial sum when `add_residual` is False."""
+        the local experts' partial sum when `add_residual` is False. `wait`
+        (an ``ops.FlagWait``): h arrives from peers; the first kernel waits."""
         cfg = self.cfg
         lw = self.w.layers[layer_idx]
         H = cfg.hidden_size
@@ -62,7 +63,7 @@ class FFNWorker:
                 raise NotImplementedError("the fused F2A store covers MoE layers only; "
                                           "use --comm-impl nccl for models with dense layers")
             self._mark(True, EventType.MOE_SHARED_OR_DENSE, layer_idx, mb_idx)
-            xn = ops.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps)
+            xn = ops.sum_rmsnorm([h], lw.post_norm, cfg.rms_norm_eps, wait=wait)[1]
             y = ops.dense_mlp(xn, lw.w_dense_gate_up, lw.w_dense_down, residual=residual)
             self._mark(False, EventType.MOE_SHARED_OR_DENSE, layer_idx, mb_idx)
             return y
@@ -72,4 +73,4 @@ class FFNWorker:
                            lw.expert_start, add_residual=residual is not None, out=out,
                            tracker_marks=lambda start, name: self._mark(start, stage[name],
                                                                         layer_idx, mb_idx),
-                           **kw)
+                           wait=wait, **kw)

@@ -9,7 +9,7 @@ missing raises. The extension is ``afd_demo_b200/_C*.so`` built in place by
 from __future__ import annotations
 
 import math
-from typing import List, Optional, Sequence, Tuple
+from typing import List, NamedTuple, Optional, Sequence, Tuple
 
 import torch
 
@@ -92,11 +92,36 @@ def num_sms() -> int:
 
 
 # ------------------------------------------------------------------ norms --
+class FlagWait(NamedTuple):
+    """A receive folded into the consuming kernel: the kernel waits (bounded
+    by `timeout_ns`) until every flag reaches *epoch + value before reading
+    its input; a timeout is recorded in `status`."""
+    flags: Sequence[int]
+    value: int
+    status: torch.Tensor
+    timeout_ns: int
+    epoch: Optional[torch.Tensor]
+
+
+def _wait_args(wait: Optional[FlagWait]) -> tuple:
+    if wait is None:
+        return [], 0, None, 0, None
+    return list(wait.flags), int(wait.value), wait.status, int(wait.timeout_ns), wait.epoch
+
+
+def wait_flags(wait: Optional[FlagWait]) -> None:
+    """Stand-alone form of a folded wait (a one-CTA kernel)."""
+    if wait is not None:
+        ext().wait_flags(list(wait.flags), int(wait.value), wait.status, int(wait.timeout_ns),
+                         wait.epoch)
+
+
 def sum_rmsnorm(parts: Sequence[torch.Tensor], w: torch.Tensor, eps: float,
-                want_sum: bool = True, out: Optional[torch.Tensor] = None
-                ) -> Tuple[torch.Tensor, torch.Tensor]:
+                want_sum: bool = True, out: Optional[torch.Tensor] = None,
+                wait: Optional[FlagWait] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """x = sum(parts), y = RMSNorm(x). Returns (x, y); x is parts[0] itself
-    when there is a single part."""
+    when there is a single part. `wait`: the parts arrive from peers; the
+    kernel waits for their flags first."""
     if not _cuda(parts[0]):
         return torch_ref.sum_rmsnorm(parts, w, eps)
     p0 = parts[0]
@@ -106,7 +131,8 @@ def sum_rmsnorm(parts: Sequence[torch.Tensor], w: torch.Tensor, eps: float,
     x = None
     if len(parts) > 1 and want_sum:
         x = torch.empty(rows, H, device=p0.device, dtype=p0.dtype)
-    ext().sum_rmsnorm([p.reshape(rows, H) for p in parts], w, x, y, float(eps))
+    ext().sum_rmsnorm([p.reshape(rows, H) for p in parts], w, x, y, float(eps),
+                      *_wait_args(wait))
     return (x if x is not None else p0.reshape(rows, H)), y
 
 
@@ -417,7 +443,8 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
             out: Optional[torch.Tensor] = None, peers: Sequence[int] = (),
             seg_offsets: Sequence[int] = (), peer_row_offset: int = 0, flags: Sequence[int] = (),
             signal_value: int = 0, done_counter: Optional[torch.Tensor] = None,
-            epoch: Optional[torch.Tensor] = None, tracker_marks=None) -> torch.Tensor:
+            epoch: Optional[torch.Tensor] = None, tracker_marks=None,
+            wait: Optional[FlagWait] = None) -> torch.Tensor:
     """The whole sparse-MoE block on h = attn_out + residual: post-attention
     RMSNorm, router GEMM, softmax/top-k/renormalise + routing (one kernel for
     up to 4096 routed pairs), grouped expert GEMMs, combine. Returns
@@ -445,7 +472,8 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
         C.moe_gate(h, post_norm_w, w_router, xn, logits, ws.ids, ws.weights,
                    _GateCounters.get(h.device, T), top_k, bool(norm_topk_prob), float(eps),
                    _gate_groups(T, E), expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
-                   ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+                   ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows,
+                   *_wait_args(wait))
         mark(False, "router")
         mark(True, "experts")
         y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T,
@@ -453,7 +481,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
                                done_counter, epoch)
         mark(False, "experts")
         return y
-    xn = rmsnorm(h, post_norm_w, eps)
+    xn = sum_rmsnorm([h], post_norm_w, eps, wait=wait)[1]
     logits = linear(xn, w_router) if E % 128 == 0 else torch.nn.functional.linear(xn, w_router)
     if T * top_k <= 4096 and E <= 256:
         C.moe_route(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob), expert_start, E_loc,

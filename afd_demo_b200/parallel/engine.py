@@ -80,6 +80,10 @@ class PipelineEngine:
         colocated = has_attn and has_ffn
         with _on(s_attn):
             tr.begin(plan)
+        # fold each receive's wait into the consuming kernel, except when
+        # timing: then the receive wait is its own (measured) span
+        if tr.fused:
+            tr.defer_waits = not (ta or tf)
         if has_ffn:
             m_.ffn_worker.tracker = tf
 
@@ -88,11 +92,13 @@ class PipelineEngine:
                 if tf:
                     tf.mark_start(EventType.RECV_WAIT, l, m)
                 h = tr.a2f_recv(l, m)
+                wait = tr.take_wait()
                 if tf:
                     tf.mark_end(EventType.RECV_WAIT, l, m)
                     tf.mark_start(EventType.FFN_COMPUTE, l, m)
                 out = m_.ffn_worker.forward_ffn_layer(
-                    l, h, add_residual=(ctx.ffn_index == 0), sink=tr.f2a_sink(l, m), mb_idx=m)
+                    l, h, add_residual=(ctx.ffn_index == 0), sink=tr.f2a_sink(l, m), mb_idx=m,
+                    wait=wait)
                 if tf:
                     tf.mark_end(EventType.FFN_COMPUTE, l, m)
                 t0 = time.perf_counter()
@@ -119,6 +125,7 @@ class PipelineEngine:
                 r0 = s.batch_offset * s.q_len
                 xs[s.idx] = [x0[r0:r0 + s.tokens]]
         have = {(s.idx, -1) for s in slots}  # (m, l): layer-l output of m received
+        waits: Dict[int, object] = {}  # m -> wait left to the consumer of xs[m]
 
         def recv(l: int, m: int):
             if (m, l) in have:
@@ -126,6 +133,9 @@ class PipelineEngine:
             if ta:
                 ta.mark_start(EventType.RECV_WAIT, l, m)
             xs[m] = tr.f2a_recv(l, m)
+            w = tr.take_wait()
+            if w is not None:
+                waits[m] = w
             if ta:
                 ta.mark_end(EventType.RECV_WAIT, l, m)
             have.add((m, l))
@@ -142,7 +152,8 @@ class PipelineEngine:
                     if ta:
                         ta.mark_start(EventType.ATTN_COMPUTE, l, m)
                     h = attn.forward_attention_layer(l, xs[m], s.batch_offset, s.q_len,
-                                                     start_pos=start, sink=tr.a2f_sink(l, m))
+                                                     start_pos=start, sink=tr.a2f_sink(l, m),
+                                                     wait=waits.pop(m, None))
                     if ta:
                         ta.mark_end(EventType.ATTN_COMPUTE, l, m)
                     t0 = time.perf_counter()
@@ -158,7 +169,8 @@ class PipelineEngine:
         with _on(s_attn):
             for s in slots:
                 recv(L - 1, s.idx)
-                logits.append(attn.forward_lm_head(xs[s.idx], s.q_len, last_only=last_only))
+                logits.append(attn.forward_lm_head(xs[s.idx], s.q_len, last_only=last_only,
+                                                   wait=waits.pop(s.idx, None)))
             out = torch.cat(logits, 0) if len(logits) > 1 else logits[0]
             if advance_cache:
                 cache.advance(plan.q_len)

@@ -35,6 +35,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
+from .. import ops
 from . import faults
 from .micro_batch import ForwardPlan
 
@@ -73,6 +74,13 @@ class Transport:
 
     def f2a_send(self, l: int, m: int, out: torch.Tensor) -> None:
         raise NotImplementedError
+
+    # A transport may leave the receive's wait to the consuming kernel: after
+    # a2f_recv / f2a_recv, take_wait() hands over the pending wait (or None).
+    defer_waits = False
+
+    def take_wait(self):
+        return None
 
     def check(self) -> None:
         pass
@@ -294,6 +302,8 @@ class PeerTransport(Transport):
         self.status = torch.zeros(2, device=device, dtype=torch.int32)
         self.counters = torch.zeros(num_mb, device=device, dtype=torch.int32)
         self._dropbox = torch.zeros(16, device=device, dtype=torch.int32)  # injected drops
+        self._pending = None
+        self.defer_waits = True
         # exchange IPC handles (collective over all ranks)
         handle = bytes(self.C.ipc_handle(self.region))
         allh: List[Optional[bytes]] = [None] * ctx.world_size
@@ -337,6 +347,17 @@ class PeerTransport(Transport):
                     raise ValueError(f"{s.tokens} tokens exceed attention buffer {self.Ta}")
         self.C.add_i32(self.epoch, self.L)
 
+    def _recv_wait(self, flags: List[int], value: int) -> None:
+        w = ops.FlagWait(flags, value, self.status, self.timeout_ns, self.epoch)
+        if self.defer_waits:
+            self._pending = w
+        else:
+            ops.wait_flags(w)
+
+    def take_wait(self):
+        w, self._pending = self._pending, None
+        return w
+
     def check(self) -> None:
         st = self.status.cpu()
         if int(st[0]) != 0:
@@ -364,14 +385,14 @@ class PeerTransport(Transport):
 
     def f2a_recv(self, l, m):
         flags = [self._attn_flag(self.base, m, f) for f in range(self.n_ffn)]
-        self.C.wait_flags(flags, l + 1 - self.L, self.status, self.timeout_ns, self.epoch)
+        self._recv_wait(flags, l + 1 - self.L)
         T = self.plan.slots_of(self.ctx.attn_index)[m].tokens
         return [self._view(self._attn_data(self.base, m, f), T) for f in range(self.n_ffn)]
 
     # FFN side ----------------------------------------------------------------
     def a2f_recv(self, l, m):
         flags = [self._ffn_flag(self.base, m, a) for a in range(self.n_attn)]
-        self.C.wait_flags(flags, l + 1 - self.L, self.status, self.timeout_ns, self.epoch)
+        self._recv_wait(flags, l + 1 - self.L)
         return self._view(self._ffn_data(self.base, m), self.plan.ffn_slots[m].tokens)
 
     def f2a_sink(self, l, m):

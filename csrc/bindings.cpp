@@ -195,8 +195,26 @@ void gemm_down_combine(const at::Tensor& w, const at::Tensor& x, at::Tensor& y, 
   check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_down_combine");
 }
 
+// bounded flag wait folded into a consuming kernel (empty list: none)
+static afd::FlagWait make_wait(const std::vector<int64_t>& flags, int64_t value,
+                               const c10::optional<at::Tensor>& status, int64_t timeout_ns,
+                               const c10::optional<at::Tensor>& epoch) {
+  TORCH_CHECK(flags.size() <= (size_t)afd::kMaxFlagPeers, "too many wait flags");
+  afd::FlagWait w{};
+  for (size_t i = 0; i < flags.size(); ++i) w.flags[i] = reinterpret_cast<int*>(flags[i]);
+  w.n = (int)flags.size();
+  w.value = (int)value;
+  w.epoch = opt_ptr<const int>(epoch);
+  w.status = opt_ptr<int>(status);
+  w.timeout_ns = (unsigned long long)timeout_ns;
+  return w;
+}
+
 void sum_rmsnorm(std::vector<at::Tensor> parts, const at::Tensor& weight,
-                 const c10::optional<at::Tensor>& x_out, at::Tensor& y_out, double eps) {
+                 const c10::optional<at::Tensor>& x_out, at::Tensor& y_out, double eps,
+                 std::vector<int64_t> wait_flags, int64_t wait_value,
+                 const c10::optional<at::Tensor>& status, int64_t timeout_ns,
+                 const c10::optional<at::Tensor>& epoch) {
   TORCH_CHECK(!parts.empty() && parts.size() <= (size_t)afd::kMaxParts, "1..8 parts");
   afd::SumNormArgs a{};
   const int64_t H = parts[0].size(-1);
@@ -214,6 +232,7 @@ void sum_rmsnorm(std::vector<at::Tensor> parts, const at::Tensor& weight,
   a.ld_out = (int)(y_out.dim() > 1 ? y_out.stride(-2) : H);
   a.H = (int)H;
   a.eps = (float)eps;
+  a.wait = make_wait(wait_flags, wait_value, status, timeout_ns, epoch);
   check_rc(afd::launch_sum_rmsnorm(a, (int)rows, cur_stream()), "sum_rmsnorm");
 }
 
@@ -386,7 +405,10 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
               at::Tensor& counters, int64_t top_k, bool renorm, double eps, int64_t groups,
               int64_t expert_start, int64_t n_local, int64_t block_n, at::Tensor& inv,
               at::Tensor& row_token, at::Tensor& row_weight, at::Tensor& expert_offsets,
-              at::Tensor& blocks, at::Tensor& num_blocks, at::Tensor& num_rows) {
+              at::Tensor& blocks, at::Tensor& num_blocks, at::Tensor& num_rows,
+              std::vector<int64_t> wait_flags, int64_t wait_value,
+              const c10::optional<at::Tensor>& status, int64_t timeout_ns,
+              const c10::optional<at::Tensor>& epoch) {
   TORCH_CHECK(h.stride(1) == 1 && xn.is_contiguous() && logits.is_contiguous() &&
                   w_router.is_contiguous(),
               "moe_gate: contiguous rows expected");
@@ -410,6 +432,7 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
   g.top_k = (int)top_k;
   g.renorm = renorm ? 1 : 0;
   g.eps = (float)eps;
+  g.wait = make_wait(wait_flags, wait_value, status, timeout_ns, epoch);
   afd::MoeAlignArgs a{};
   a.T = T;
   a.top_k = g.top_k;

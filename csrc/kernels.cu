@@ -67,10 +67,25 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
 // One CTA (256 threads) per row; H % 8 == 0, H <= 256 * 8 * 4.
 constexpr int kNormThreads = 256;
 
+// Every CTA: thread 0 waits (bounded) for the flags, then the CTA proceeds.
+// The acquire load plus the barrier order the peers' data stores before this
+// CTA's reads. On a timeout the status word records it and the CTA proceeds
+// (the host turns the status into an error after the step).
+__device__ __forceinline__ void block_wait(const FlagWait& w, int where) {
+  if (w.n == 0) return;
+  if (threadIdx.x == 0) {
+    const int v = w.value + (w.epoch != nullptr ? *w.epoch : 0);
+    for (int i = 0; i < w.n; ++i)
+      if (!wait_flag_geq(w.flags[i], v, w.status, where + i, w.timeout_ns)) break;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kNormThreads) sum_rmsnorm_kernel(SumNormArgs a) {
   __shared__ float red[kNormThreads / 32];
   pdl_wait();
   pdl_trigger();
+  block_wait(a.wait, 120);
   const int row = blockIdx.x;
   const int H = a.H;
   constexpr int kMaxChunks = 4;
@@ -390,6 +405,7 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   __shared__ int s_flag;
   pdl_wait();
   pdl_trigger();
+  block_wait(g.wait, 140);
   const int t = blockIdx.x / g.G;
   const int grp = blockIdx.x % g.G;
   const int H = g.H;

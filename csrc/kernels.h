@@ -11,6 +11,17 @@ namespace afd {
 constexpr int kMaxParts = 8;
 constexpr int kMaxFlagPeers = 9;
 
+// A receive folded into the consuming kernel: before reading its inputs every
+// CTA waits (bounded) until each flag reaches *epoch + value. n == 0: no wait.
+struct FlagWait {
+  int* flags[kMaxFlagPeers];
+  int n;
+  int value;
+  const int* epoch;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
 struct SumNormArgs {
   const __nv_bfloat16* parts[kMaxParts];  // each [rows, ld_in]
   int n_parts;
@@ -21,6 +32,7 @@ struct SumNormArgs {
   int ld_out;
   int H;
   float eps;
+  FlagWait wait;                          // inputs produced by peers (optional)
 };
 
 struct QKRopeArgs {
@@ -111,6 +123,7 @@ struct MoeGateArgs {
   int* done_cnt;                 // [1] zeroed, self-cleaning
   int T, H, E, G, top_k, renorm;
   float eps;
+  FlagWait wait;                 // h produced by peers (optional)
 };
 
 struct MoeGatherArgs {
