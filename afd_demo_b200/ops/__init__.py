@@ -9,6 +9,7 @@ missing raises. The extension is ``afd_demo_b200/_C*.so`` built in place by
 from __future__ import annotations
 
 import math
+import os
 from typing import List, NamedTuple, Optional, Sequence, Tuple
 
 import torch
@@ -352,7 +353,7 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
            1, None, None, row_ids)
     if out is None and not peers:
         out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
-    if T <= _FUSED_COMBINE_MAX_TOKENS:
+    if _FUSED_COMBINE and T <= _FUSED_COMBINE_MAX_TOKENS:
         # combine (+ residual, + F2A stores, + flags) in the down GEMM's epilogue
         C.gemm_down_combine(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, ws.blocks,
                             ws.num_blocks, ws.row_weight, bn, ws.max_blocks * (H // 128), ws.inv,
@@ -397,8 +398,14 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
 _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate kernel
 
 
+# AFD_FUSED_GATE=0 / AFD_FUSED_COMBINE=0 select the unfused kernel sequences
+# (A/B measurements)
+_FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
+_FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "1") != "0"
+
+
 def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
-    return (T * top_k <= _GATE_MAX_ENTRIES and H <= 4096 and H % 8 == 0 and E <= 256
+    return (_FUSED_GATE and T * top_k <= _GATE_MAX_ENTRIES and H <= 4096 and H % 8 == 0 and E <= 256
             and E % 8 == 0 and top_k <= 16 and _gate_groups(T, E) > 0)
 
 

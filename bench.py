@@ -250,8 +250,10 @@ def main():
                            use_cuda_graph=True, host_io=True)
             return model._last_generation_metrics
 
-        gen()  # warm (graphs for this batch)
+        met0 = gen()  # warm (graphs for this batch)
         met = gen()
+        if os.environ.get("AFD_BENCH_DEBUG"):
+            print(f"[rank {rank}] e2e warm {met0} timed {met}", file=sys.stderr, flush=True)
         tp = torch.tensor([met["decode_tpot_ms"], met["prefill_ms"]], device=f"cuda:{local}")
         if world > 1:
             dist.all_reduce(tp, op=dist.ReduceOp.MAX)
