@@ -1,0 +1,159 @@
+#!/usr/bin/env python3
+"""Per-kernel timings on Qwen3-30B-A3B shapes with roofline fractions.
+
+Each op is timed with CUDA events over `--iters` back-to-back launches after
+`--warmup` launches, on the launching stream, with a device synchronize on
+both sides. Weights rotate over enough distinct copies that every launch
+reads them from HBM (the set of copies is larger than the 126 MB L2), as the
+48 distinct layers of the model do. Achieved bandwidth = algorithmic bytes /
+time; achieved FLOP rate = algorithmic FLOPs / time; fractions are of the
+measured peaks in MEASURED_PEAKS.json when present (HBM copy bandwidth and
+cuBLAS bf16 burst throughput), else of the pool's fallback figures (6.65 TB/s,
+1.59 PFLOP/s).
+
+    python -m afd_demo_b200.scripts.bench_kernels [--tokens 16,32,64,128] [--json out.json]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+if __package__ in (None, ""):
+    sys.path.insert(0, REPO)
+
+from afd_demo_b200 import ops  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]) * 1e9, float(d["bf16_tflops"]) * 1e12, "of measured"
+    return 6.65e12, 1.59e15, "of fallback"
+
+
+def copies_for(nbytes: int) -> int:
+    return max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
+
+
+def timeit(fn, iters: int, warmup: int) -> float:
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1e3 / iters  # us
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--tokens", default="16,32,64,128")
+    ap.add_argument("--kv-len", type=int, default=276)
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--json", default="")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    bw, fl, tag = peaks()
+    H, I, E, k, nq, nkv, D = 2048, 768, 128, 8, 32, 4, 128
+    QKV = (nq + 2 * nkv) * D
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*s, scale=0.02):
+        return (torch.randn(*s, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    rows = []
+
+    def report(name, T, us, nbytes, flops):
+        r = {"op": name, "tokens": T, "us": round(us, 2),
+             "GB/s": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e-6 / bw, 3),
+             "TFLOP/s": round(flops / us / 1e6, 1), "tc_frac": round(flops / us / 1e-6 / fl, 3)}
+        rows.append(r)
+        print(f"{name:28s} T={T:5d} {us:9.2f} us  {r['GB/s']:8.1f} GB/s ({r['hbm_frac']:.2f} {tag})"
+              f"  {r['TFLOP/s']:7.1f} TFLOP/s ({r['tc_frac']:.3f} {tag})", flush=True)
+
+    n_qkv = copies_for(QKV * H * 2)
+    w_qkv = [rnd(QKV, H) for _ in range(n_qkv)]
+    n_o = copies_for(H * nq * D * 2)
+    w_o = [rnd(H, nq * D) for _ in range(n_o)]
+    n_e = 2  # one layer of experts is 1.2 GB: two copies alternate
+    w_gu = [rnd(E, 2 * I, H) for _ in range(n_e)]
+    w_dn = [rnd(E, H, I) for _ in range(n_e)]
+    w_r = [rnd(E, H) for _ in range(n_qkv)]
+    pn = (1 + 0.1 * torch.randn(H, device=dev)).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+    rope = ops.rope_table(4096, D, 1e6, dev)
+
+    for T in [int(t) for t in a.tokens.split(",")]:
+        x = rnd(T, H, scale=1.0)
+        o_in = rnd(T, nq * D, scale=1.0)
+        report("sum_rmsnorm (2 parts)", T,
+               timeit(lambda i: ops.sum_rmsnorm([x, x], pn, 1e-6), a.iters, a.warmup),
+               3 * T * H * 2, 0)
+        report("linear qkv", T,
+               timeit(lambda i: ops.linear(x, w_qkv[i % n_qkv]), a.iters, a.warmup),
+               QKV * H * 2 + T * (H + QKV) * 2, 2 * T * H * QKV)
+        report("linear o_proj + residual", T,
+               timeit(lambda i: ops.linear(o_in, w_o[i % n_o], residual=x), a.iters, a.warmup),
+               H * nq * D * 2 + T * (nq * D + 2 * H) * 2, 2 * T * H * nq * D)
+        kc = rnd(T, nkv, a.kv_len + 8, D, scale=1.0)
+        vc = rnd(T, nkv, a.kv_len + 8, D, scale=1.0)
+        qkv = rnd(T, QKV, scale=1.0)
+        start = a.kv_len - 1
+        pos = torch.tensor([start], device=dev, dtype=torch.int32)
+        report("decode attention (fused)", T,
+               timeit(lambda i: ops.decode_attention_fused(qkv, qn, qn, rope, kc, vc, start, pos, 0,
+                                                           nq, nkv, 1e-6), a.iters, a.warmup),
+               2 * T * nkv * a.kv_len * D * 2, 4 * T * nq * a.kv_len * D)
+        h = rnd(T, H, scale=1.0)
+        ids = torch.stack([torch.randperm(E, device=dev)[:k] for _ in range(T)]).to(torch.int32)
+        distinct = int(torch.unique(ids).numel())
+        wts = torch.full((T, k), 1.0 / k, device=dev)
+        eb = distinct * 3 * I * H * 2
+        report(f"moe experts ({distinct} hit)", T,
+               timeit(lambda i: ops.moe_experts(x, ids, wts, w_gu[i % n_e], w_dn[i % n_e], 0,
+                                                residual=h), a.iters, a.warmup),
+               eb, 2 * T * k * 3 * I * H)
+        report("moe block (gate+experts)", T,
+               timeit(lambda i: ops.moe_ffn(h, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
+                                            1e-6), a.iters, a.warmup),
+               eb + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
+
+    # prefill-sized dense GEMM and attention
+    T = a.prefill_tokens
+    xp = rnd(T, H, scale=1.0)
+    report("linear qkv (prefill)", T,
+           timeit(lambda i: ops.linear(xp, w_qkv[i % n_qkv]), max(5, a.iters // 5), 2),
+           QKV * H * 2 + T * (H + QKV) * 2, 2 * T * H * QKV)
+    S = 256
+    B = T // S
+    q = rnd(T, nq, D, scale=1.0)
+    kc = rnd(B, nkv, S, D, scale=1.0)
+    vc = rnd(B, nkv, S, D, scale=1.0)
+    pos0 = torch.zeros(1, device=dev, dtype=torch.int32)
+    report(f"prefill attention S={S}", T,
+           timeit(lambda i: ops.attention(q, kc, vc, 0, S, 0, pos0), max(5, a.iters // 5), 2),
+           (T * nq * D * 2) * 2 + 2 * B * nkv * S * D * 2, 2 * 2 * B * nq * S * S * D / 2)
+    if a.json:
+        os.makedirs(os.path.dirname(os.path.abspath(a.json)), exist_ok=True)
+        json.dump({"peaks": {"hbm_Bps": bw, "bf16_flops": fl, "basis": tag}, "rows": rows},
+                  open(a.json, "w"), indent=1)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

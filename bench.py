@@ -162,13 +162,17 @@ def main():
     torch.cuda.synchronize()
 
     if args.profile:
-        model.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
+        # greedy tokens from the model, so the routing is that of real decoding
+        logits = model.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
         tok = torch.zeros(B, 1, dtype=torch.long, device=f"cuda:{local}")
+        r = model.local_batch(B)
         for i in range(args.profile):
+            if model.ctx.is_attention_node:
+                tok[r.start:r.stop, 0] = ops.argmax(logits)
             if i == args.profile - 1:
                 torch.cuda.synchronize()
                 torch.cuda.nvtx.range_push("profile_step")
-            model.run_forward(tok, "dbo", 2, crosslayer=True)
+            logits = model.run_forward(tok, "dbo", 2, crosslayer=True)
             if i == args.profile - 1:
                 torch.cuda.synchronize()
                 torch.cuda.nvtx.range_pop()

@@ -100,11 +100,20 @@ __device__ void combine_feature_tile(const GemmArgs& a, int ft) {
   const int Hf = a.f_tiles * 128;
   for (int t = et >> 4; t < a.cmb_T; t += 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < a.cmb_topk; ++j) {
-      const int r = a.cmb_inv[(size_t)t * a.cmb_topk + j];
-      if (r < 0) continue;
-      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.out + (size_t)r * a.ld_out + col));
-      const uint32_t* pv = &v.x;
+    // all row indices, then all rows, then the sums in j order (loads in flight)
+    int r[16];
+    uint4 v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      r[j] = j < a.cmb_topk ? a.cmb_inv[(size_t)t * a.cmb_topk + j] : -1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      v[j] = r[j] >= 0 ? __ldcg(reinterpret_cast<const uint4*>(a.out + (size_t)r[j] * a.ld_out + col))
+                       : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (r[j] < 0) continue;
+      const uint32_t* pv = &v[j].x;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float x0, x1;
@@ -362,14 +371,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < blk.y && emit; c += 16) {
         float acc[16];
         if (wsp != nullptr) {
-          // last split: sum the partial slices in split order
+          // last split: sum the partial slices in split order; four slices'
+          // 16 values are loaded before any is added, so 64 loads are in
+          // flight instead of one dependent load at a time
           const size_t split_stride = (size_t)tiles * BN * kBM;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            acc[j] = 0.f;
-            if (c + j < blk.y)
-              for (int sp = 0; sp < k_splits; ++sp)
-                acc[j] += __ldcg(wsp + sp * split_stride + (c + j) * kBM);
+          for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+          for (int sp0 = 0; sp0 < k_splits; sp0 += 4) {
+            float v[4][16];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                v[u][j] = (sp0 + u < k_splits && c + j < blk.y)
+                              ? __ldcg(wsp + (sp0 + u) * split_stride + (c + j) * kBM)
+                              : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[j] += v[u][j];
           }
         } else {
           tmem_ld16(t_row + c, acc);

@@ -95,13 +95,25 @@ __global__ void __launch_bounds__(kNormThreads) sum_rmsnorm_kernel(SumNormArgs a
   for (int c = 0; c < kMaxChunks; ++c) {
     const int col = (c * kNormThreads + threadIdx.x) * 8;
     if (col < H) {
-      float acc[8];
-      load8(a.parts[0] + (size_t)row * a.ld_in + col, acc);
-      for (int p = 1; p < a.n_parts; ++p) {
-        float t[8];
-        load8(a.parts[p] + (size_t)row * a.ld_in + col, t);
+      // every part's vector is requested before the sum (loads in flight)
+      uint4 pv[kMaxParts];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      for (int p = 0; p < kMaxParts; ++p)
+        pv[p] = p < a.n_parts
+                    ? *reinterpret_cast<const uint4*>(a.parts[p] + (size_t)row * a.ld_in + col)
+                    : make_uint4(0, 0, 0, 0);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kMaxParts; ++p) {
+        if (p >= a.n_parts) break;
+        const uint32_t* q = &pv[p].x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float u0, u1;
+          unpack_bf16x2(q[e], u0, u1);
+          acc[2 * e] += u0;
+          acc[2 * e + 1] += u1;
+        }
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -447,12 +459,28 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   for (int j = warp; j < per_grp; j += kGateThreads / 32) {
     const int e = grp * per_grp + j;
     const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
-    float acc = 0.f;
-    for (int col = lane * 8; col < H; col += 32 * 8) {
-      float w[8];
-      load8(wr + col, w);
+    // the row's vectors (H <= 4096: at most 16 per lane) are all requested
+    // before the dot product
+    constexpr int kVec = kGateMaxH / (32 * 8);
+    uint4 wv[kVec];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc += w[i] * xn_s[col + i];
+    for (int c = 0; c < kVec; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      wv[c] = col < H ? *reinterpret_cast<const uint4*>(wr + col) : make_uint4(0, 0, 0, 0);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kVec; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col >= H) break;
+      const uint32_t* pw = &wv[c].x;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float w0, w1;
+        unpack_bf16x2(pw[i], w0, w1);
+        acc += w0 * xn_s[col + 2 * i];
+        acc += w1 * xn_s[col + 2 * i + 1];
+      }
     }
     acc = warp_sum(acc);
     if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
@@ -519,18 +547,30 @@ __global__ void __launch_bounds__(kNormThreads) moe_combine_kernel(MoeCombineArg
   const int t = blockIdx.x;
   const int H = a.H;
   int rows[16];
-  for (int j = 0; j < a.top_k; ++j) rows[j] = a.inv[(size_t)t * a.top_k + j];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) rows[j] = j < a.top_k ? a.inv[(size_t)t * a.top_k + j] : -1;
   int seg = -1;
   for (int s = 0; s < a.n_peers; ++s)
     if (t >= a.seg_offsets[s] && t < a.seg_offsets[s + 1]) seg = s;
   for (int col = threadIdx.x * 8; col < H; col += kNormThreads * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < a.top_k; ++j) {
-      if (rows[j] < 0) continue;
-      float y[8];
-      load8(a.y + (size_t)rows[j] * H + col, y);
+    // every row's vector is requested before the sums (loads in flight)
+    uint4 v[16];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += y[i];
+    for (int j = 0; j < 16; ++j)
+      v[j] = rows[j] >= 0 ? *reinterpret_cast<const uint4*>(a.y + (size_t)rows[j] * H + col)
+                          : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (rows[j] < 0) continue;
+      const uint32_t* pv = &v[j].x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float y0, y1;
+        unpack_bf16x2(pv[e], y0, y1);
+        acc[2 * e] += y0;
+        acc[2 * e + 1] += y1;
+      }
     }
     if (a.residual != nullptr) {
       float r[8];
