@@ -302,8 +302,10 @@ class DisaggregatedQwenModel:
         devmod.synchronize()
         ctx.barrier()
         t_pf0 = ev()
+        # prefill DBO pipelines micro-batches across layers, as the reference's
+        # AsyncPipelineScheduler does (src/pipeline/async_scheduler.py:281-456)
         logits = self.run_forward(input_ids, prefill_mode, num_prefill_micro_batches,
-                                  reset_cache=True)
+                                  crosslayer=(prefill_mode == "dbo"), reset_cache=True)
         t_pf1 = ev()
         generated = [local] if is_attn else []
         next_tok = None

@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Per-kernel timings on Qwen3-30B-A3B shapes with roofline fractions.
 
-Each op is timed with CUDA events over `--iters` back-to-back launches after
-`--warmup` launches, on the launching stream, with a device synchronize on
-both sides. Weights rotate over enough distinct copies that every launch
+Each op is timed with CUDA events around one replay of a CUDA graph holding
+`--iters` back-to-back calls (after `--warmup` eager calls), on the launching
+stream, with a device synchronize on both sides: device time per call, as in
+the captured decode step. Weights rotate over enough distinct copies that every launch
 reads them from HBM (the set of copies is larger than the 126 MB L2), as the
 48 distinct layers of the model do. Achieved bandwidth = algorithmic bytes /
 time; achieved FLOP rate = algorithmic FLOPs / time; fractions are of the
@@ -45,15 +46,36 @@ def copies_for(nbytes: int) -> int:
     return max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
 
 
-def timeit(fn, iters: int, warmup: int) -> float:
+def timeit(fn, iters: int, warmup: int, graph: bool = True) -> float:
+    """Device time per call. With `graph`, the `iters` calls are captured in
+    one CUDA graph and the replay is timed, as the decode step replays them;
+    otherwise host launch time is included."""
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for i in range(iters):
-        fn(i)
-    e.record()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            for i in range(warmup):  # allocations of the capture stream
+                fn(i)
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for i in range(iters):
+                fn(i)
+        g.replay()  # first replay uploads the graph
+        torch.cuda.synchronize()
+        s.record()
+        g.replay()
+        e.record()
+    else:
+        s.record()
+        for i in range(iters):
+            fn(i)
+        e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) * 1e3 / iters  # us
 

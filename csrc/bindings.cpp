@@ -6,6 +6,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -327,7 +328,16 @@ void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at:
   a.D = (int)q.size(2);
   a.s_max = (int)k_cache.size(2);
   const int B = (int)(q.size(0) / q_len);
-  check_rc(afd::launch_prefill_attention(a, B, cur_stream()), "prefill_attention");
+  // tcgen05 kernel for head_dim 128; AFD_PREFILL_ATTN=mma selects the
+  // mma.sync kernel (A/B measurements)
+  static const bool use_mma = [] {
+    const char* e = std::getenv("AFD_PREFILL_ATTN");
+    return e != nullptr && std::string(e) == "mma";
+  }();
+  if (a.D == 128 && !use_mma)
+    check_rc(afd::launch_prefill_attention_tc(a, B, cur_stream()), "prefill_attention_tc");
+  else
+    check_rc(afd::launch_prefill_attention(a, B, cur_stream()), "prefill_attention");
 }
 
 void router_topk(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, int64_t top_k,

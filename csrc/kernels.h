@@ -194,5 +194,7 @@ int launch_wait_flags(const FlagArgs& a, cudaStream_t s);
 int launch_add_i32(int* p, int by, cudaStream_t s);
 int launch_decode_attention(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s);
 int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s);
+// tcgen05/TMEM/TMA version (attention_tc.cu), head_dim 128
+int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s);
 
 }  // namespace afd

@@ -172,16 +172,19 @@ def test_decode_attention_fused(B, kv_len, G, D):
     assert torch.equal(vc[1:1 + B, :, start], vc2[1:1 + B, :, start])
 
 
-@pytest.mark.parametrize("B,q_len,start", [(1, 16, 0), (2, 128, 0), (3, 100, 0), (2, 64, 40),
-                                           (1, 512, 0)])
-def test_prefill_attention(B, q_len, start):
+@pytest.mark.parametrize("B,q_len,start,off", [(1, 16, 0, 0), (2, 128, 0, 0), (3, 100, 0, 0),
+                                               (2, 64, 40, 0), (1, 512, 0, 0), (2, 300, 0, 1),
+                                               (1, 257, 100, 0), (2, 129, 383, 1)])
+def test_prefill_attention(B, q_len, start, off):
+    """Causal prefill over a cache holding `start` earlier keys; sequences
+    sit at cache rows off .. off + B - 1."""
     nq, nkv, D, S = 32, 4, 128, 1024
-    kc = _randn(B, nkv, S, D, seed=50)
-    vc = _randn(B, nkv, S, D, seed=51)
+    kc = _randn(B + off, nkv, S, D, seed=50)
+    vc = _randn(B + off, nkv, S, D, seed=51)
     q = _randn(B * q_len, nq, D, seed=52)
     pos = torch.tensor([start], device=DEV, dtype=torch.int32)
-    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, q_len, start)
-    out = ops.attention(q, kc, vc, 0, q_len, start, pos)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), off, q_len, start)
+    out = ops.attention(q, kc, vc, off, q_len, start, pos)
     assert _rel(out, ref) < 1e-2
 
 
