@@ -201,8 +201,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const float scale = rsqrtf((float)kTcD);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    // TMEM loads/stores are warp-collective (.sync.aligned): every branch
+    // around them is taken by the whole warp (warp-uniform predicates), or
+    // the warp would wait for lanes that never arrive.
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(s_full, j & 1, abort_flag, nullptr, 70)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, abort_flag, nullptr, 70))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float s[kTcBN];
 #pragma unroll
@@ -226,10 +232,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float m_new = fmaxf(m, rmax);
       if (j > 0) {
         // P_{j-1} V_{j-1} must be done before O is rescaled or P overwritten
-        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, nullptr, 71)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, nullptr, 71))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        if (m_new > m) {
-          const float alpha = __expf(m - m_new);
+        // rows whose max grew scale O by alpha; the others by 1 (same warp pass)
+        const bool grow = m_new > m;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float alpha = grow ? __expf(m - m_new) : 1.f;
           l *= alpha;
 #pragma unroll
           for (int c = 0; c < kTcD / 16; ++c) {
@@ -267,7 +278,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && n_tiles > 0 && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, nullptr, 72)) {
+    const bool done = ok && n_tiles > 0 &&
+                      __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag,
+                                                        nullptr, 72));
+    if (done) {
       tc_fence_after();
       const float inv = 1.f / l;
       const bool valid = q0 + row < a.q_len;

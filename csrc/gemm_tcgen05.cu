@@ -337,7 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ft = un.tile % args.f_tiles;
       const int slot = t % L::kSlots;
       const uint32_t tpar = (uint32_t)((t / L::kSlots) & 1);
-      if (!mbar_wait(&tfull_bar[slot], tpar, abort_flag, args.status, 30)) break;
+      // warp-uniform: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[slot], tpar, abort_flag, args.status, 30)))
+        break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + slot * L::kSlotCols;
       const int f_base = ft * kBM + q * 32;
