@@ -410,12 +410,22 @@ class _StepGraph:
             cache.pos_dev.fill_(pos0)
         self.graph = torch.cuda.CUDAGraph()
         before = ops.LAUNCHES.count
-        with torch.cuda.graph(self.graph):
-            self.out = model.engine.forward(model.plan(B, 1, num_mb), model._local_ids(self.tokens),
-                                            mode=mode, crosslayer=crosslayer,
-                                            advance_cache=False)
-            if cache is not None:
-                cache.pos_dev.add_(1)
+        # capture_begin/end on a side stream instead of the torch.cuda.graph
+        # context manager, which empties the allocator cache: the next prefill
+        # would then cudaMalloc all of its buffers again
+        cs = torch.cuda.Stream(model.device)
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cs):
+            self.graph.capture_begin()
+            try:
+                self.out = model.engine.forward(model.plan(B, 1, num_mb),
+                                                model._local_ids(self.tokens), mode=mode,
+                                                crosslayer=crosslayer, advance_cache=False)
+                if cache is not None:
+                    cache.pos_dev.add_(1)
+            finally:
+                self.graph.capture_end()
+        torch.cuda.current_stream().wait_stream(cs)
         # this package's kernels inside one replay
         self.launches = ops.LAUNCHES.count - before
 

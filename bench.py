@@ -255,9 +255,16 @@ def main():
             return model._last_generation_metrics
 
         met0 = gen()  # warm (graphs for this batch)
+        dbg = os.environ.get("AFD_BENCH_DEBUG")
+        keys = ("num_device_alloc", "num_device_free", "num_alloc_retries", "num_sync_all_streams")
+        st0 = torch.cuda.memory_stats() if dbg else {}
+        t0 = time.perf_counter()
         met = gen()
-        if os.environ.get("AFD_BENCH_DEBUG"):
-            print(f"[rank {rank}] e2e warm {met0} timed {met}", file=sys.stderr, flush=True)
+        if dbg:
+            st1 = torch.cuda.memory_stats()
+            print(f"[rank {rank}] e2e warm {met0} timed {met} wall {1e3 * (time.perf_counter() - t0):.0f} ms "
+                  f"alloc-stats {[(k, st1.get(k, 0) - st0.get(k, 0)) for k in keys]}",
+                  file=sys.stderr, flush=True)
         tp = torch.tensor([met["decode_tpot_ms"], met["prefill_ms"]], device=f"cuda:{local}")
         if world > 1:
             dist.all_reduce(tp, op=dist.ReduceOp.MAX)
