@@ -210,7 +210,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         raise ValueError(f"linear: output features {N} must be a multiple of 128")
     bn = _block_n(T)
     tiles = ((T + bn - 1) // bn) * (N // 128)
-    splits = _k_splits(tiles, K // 64) if T <= 256 else 1
+    splits = _k_splits(tiles, K // 64)  # 1 unless the tiles leave most SMs idle
     ws = cnt = None
     if splits > 1:
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)

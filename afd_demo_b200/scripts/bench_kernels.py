@@ -161,6 +161,15 @@ def main(argv=None) -> int:
     report("linear qkv (prefill)", T,
            timeit(lambda i: ops.linear(xp, w_qkv[i % n_qkv]), max(5, a.iters // 5), 2),
            QKV * H * 2 + T * (H + QKV) * 2, 2 * T * H * QKV)
+    op = rnd(T, nq * D, scale=1.0)
+    report("linear o_proj + residual (prefill)", T,
+           timeit(lambda i: ops.linear(op, w_o[i % n_o], residual=xp), max(5, a.iters // 5), 2),
+           H * nq * D * 2 + T * (nq * D + 2 * H) * 2, 2 * T * H * nq * D)
+    hp = rnd(T, H, scale=1.0)
+    report("moe block (prefill)", T,
+           timeit(lambda i: ops.moe_ffn(hp, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
+                                        1e-6), max(5, a.iters // 5), 2),
+           E * 3 * I * H * 2 + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
     S = 256
     B = T // S
     q = rnd(T, nq, D, scale=1.0)

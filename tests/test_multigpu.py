@@ -49,6 +49,7 @@ def _run(rank, world, port, impl, out_dir):
                      "xl": dict(use_decode_dbo=True, decode_use_crosslayer=True,
                                 prefill_mode="dbo", num_prefill_micro_batches=2),
                      "graph": dict(use_decode_dbo=True, decode_use_crosslayer=True,
+                                   prefill_mode="dbo", num_prefill_micro_batches=2,
                                    use_cuda_graph=True, host_io=True)}.items():
         res[name] = m.generate(ids, max_new_tokens=6, do_sample=False, **kw)
     torch.cuda.synchronize()
