@@ -162,8 +162,14 @@ def main():
     torch.cuda.synchronize()
 
     if args.profile:
-        # greedy tokens from the model, so the routing is that of real decoding
+        # greedy tokens from the model, so the routing is that of real decoding;
+        # the prefill of the second pass is NVTX range 'profile_prefill'
+        model.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("profile_prefill")
         logits = model.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         tok = torch.zeros(B, 1, dtype=torch.long, device=f"cuda:{local}")
         r = model.local_batch(B)
         for i in range(args.profile):

@@ -433,8 +433,7 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
   g.logits = bf(logits);
   g.ids = ids.data_ptr<int32_t>();
   g.weights = weights.data_ptr<float>();
-  g.tok_cnt = counters.data_ptr<int32_t>();
-  g.done_cnt = counters.data_ptr<int32_t>() + T;
+  g.done_cnt = counters.data_ptr<int32_t>();
   g.T = T;
   g.H = (int)h.size(1);
   g.E = (int)w_router.size(0);

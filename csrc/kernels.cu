@@ -397,10 +397,10 @@ int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s)
 // in one launch for small token counts. CTA (t, g) normalises token t (same
 // roundings as sum_rmsnorm_kernel; group 0 stores xn), then computes the
 // router logits of experts [g * E/G, (g+1) * E/G) with CUDA-core dot products
-// (fp32 accumulation, one bf16 rounding). The last of a token's G CTAs (per-
-// token counter) runs that token's top-k; the last token to finish (global
-// counter) runs the routing of moe_align_kernel. Counters are reset by the
-// CTAs that consume them, so the buffer stays zeroed between launches.
+// (fp32 accumulation, one bf16 rounding). The last CTA of the grid (one
+// global counter) runs every token's top-k and then the routing of
+// moe_align_kernel, and resets the counter, so it stays zeroed between
+// launches.
 constexpr int kGateThreads = 256;
 constexpr int kGateMaxH = 4096;
 constexpr int kGateMaxEntries = 2048;
@@ -408,7 +408,7 @@ constexpr int kGateMaxEntries = 2048;
 __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, MoeAlignArgs a) {
   __shared__ float xn_s[kGateMaxH];
   __shared__ float red[kGateThreads / 32];
-  __shared__ __nv_bfloat16 lg_s[256];
+  __shared__ __nv_bfloat16 lg_s[kGateThreads / 32][256];
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int off[kMaxLocalExperts + 1];
   __shared__ int boff[kMaxLocalExperts + 1];
@@ -486,35 +486,29 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
     if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
   }
 
-  // 3. the token's last CTA: softmax / top-k / renormalise
+  // 3. the last CTA of the grid: softmax / top-k / renormalise of every
+  // token (warp w takes tokens w, w + 8, ...), then the routing
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[t], 1) == g.G - 1);
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == (int)gridDim.x - 1);
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  for (int e = threadIdx.x; e < g.E; e += kGateThreads)
-    lg_s[e] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
-                                          (size_t)t * g.E + e));
-  __syncthreads();
-  if (warp == 0)
-    topk_token(lg_s, g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
-               g.weights + (size_t)t * g.top_k);
-  if (threadIdx.x == 0) g.tok_cnt[t] = 0;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == g.T - 1);
-  __syncthreads();
-  if (!s_flag) return;
-
-  // 4. the last token: routing over all T tokens
-  __threadfence();
-  const int n = g.T * g.top_k;
-  for (int i = threadIdx.x; i < n; i += kGateThreads) {
-    s_ids[i] = __ldcg(g.ids + i);
-    s_w[i] = __ldcg(g.weights + i);
+  for (int tt = warp; tt < g.T; tt += kGateThreads / 32) {
+    for (int e = lane; e < g.E; e += 32)
+      lg_s[warp][e] = __ushort_as_bfloat16(
+          __ldcg(reinterpret_cast<const unsigned short*>(g.logits) + (size_t)tt * g.E + e));
+    __syncwarp();
+    topk_token(lg_s[warp], g.E, g.top_k, g.renorm, lane, s_ids + tt * g.top_k,
+               s_w + tt * g.top_k);
+    __syncwarp();
   }
   __syncthreads();
+  const int n = g.T * g.top_k;
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    g.ids[i] = s_ids[i];
+    g.weights[i] = s_w[i];
+  }
   align_body(s_ids, s_w, a, cnt, off, boff);
   if (threadIdx.x == 0) *g.done_cnt = 0;
 }

@@ -119,7 +119,6 @@ struct MoeGateArgs {
   __nv_bfloat16* logits;         // [T, E] scratch
   int32_t* ids;                  // [T, top_k] (out)
   float* weights;                // [T, top_k] (out)
-  int* tok_cnt;                  // [T] zeroed, self-cleaning
   int* done_cnt;                 // [1] zeroed, self-cleaning
   int T, H, E, G, top_k, renorm;
   float eps;
