@@ -23,7 +23,8 @@ _C = None
 _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention",
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
                  "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
-                 "decode_attention_fused", "moe_route", "moe_gate", "gemm_down_combine"}
+                 "decode_attention_fused", "moe_route", "moe_gate", "gemm_down_combine",
+                 "moe_align_mt"}
 
 
 class LaunchCounter:
@@ -148,10 +149,17 @@ def _block_n(rows: int) -> int:
     return 64 if rows <= 64 else (128 if rows <= 128 else 256)
 
 
+# row-block size of prefill-sized grouped GEMMs (AFD_MOE_BN_LARGE=128 for A/B)
+_MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "256"))
+
+
 def _moe_block_n(rows: int) -> int:
     """Row-block size of the grouped expert GEMMs: 64 for decode-sized
-    batches, 128 otherwise (keeps two TMEM accumulators for SwiGLU)."""
-    return 64 if rows <= 64 else 128
+    batches; 128 for mid-sized ones (two TMEM accumulators per SwiGLU tile,
+    double-buffered); 256 for prefill-sized ones, where 128-row tiles leave
+    the MMA waiting on shared-memory bandwidth. The MMA width follows each
+    block's actual row count, so a short last block costs little."""
+    return 64 if rows <= 64 else (128 if rows < 2048 else _MOE_BN_LARGE)
 
 
 def _k_splits(tiles: int, k_iters: int) -> int:
@@ -210,7 +218,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         raise ValueError(f"linear: output features {N} must be a multiple of 128")
     bn = _block_n(T)
     tiles = ((T + bn - 1) // bn) * (N // 128)
-    splits = _k_splits(tiles, K // 64)  # 1 unless the tiles leave most SMs idle
+    if T > 256 and 2 * tiles <= num_sms():
+        # few output features (e.g. the router) over many tokens: narrower
+        # token tiles spread the work over more SMs than split-K would
+        bn = 64
+        tiles = ((T + bn - 1) // bn) * (N // 128)
+    # split-K only at decode sizes (small partial tiles), when tiles leave SMs idle
+    splits = _k_splits(tiles, K // 64) if T <= 256 else 1
     ws = cnt = None
     if splits > 1:
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)
@@ -369,6 +383,26 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     return out
 
 
+_ALIGN_CHUNK = 2048  # routed entries per CTA of the multi-CTA routing
+
+
+def _align(ids: torch.Tensor, weights: torch.Tensor, expert_start: int, E_loc: int,
+           ws: "MoEWorkspace") -> None:
+    """Expert-sorted rows and row blocks from top-k ids: one CTA up to two
+    chunks of entries, the two-kernel multi-CTA routing above that."""
+    C = ext()
+    n = ids.numel()
+    if n <= 2 * _ALIGN_CHUNK:
+        C.moe_align(ids, weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+        return
+    chunks = (n + _ALIGN_CHUNK - 1) // _ALIGN_CHUNK
+    part = torch.empty(chunks * E_loc, device=ids.device, dtype=torch.int32)
+    C.moe_align_mt(ids, weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                   ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows, part,
+                   _AlignCounters.get(ids.device, 0))
+
+
 def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                 w_gate_up: torch.Tensor, w_down: torch.Tensor, expert_start: int = 0,
                 residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
@@ -389,8 +423,7 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     k = ids.shape[1]
     if ws is None:
         ws = MoEWorkspace(T, k, E_loc, H, I2 // 2, _moe_block_n(T), xn.device, xn.dtype)
-    ext().moe_align(ids, weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
-                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+    _align(ids, weights, expert_start, E_loc, ws)
     return _moe_gemms_combine(xn, ws, w_gate_up, w_down, residual, out, T, k, peers, seg_offsets,
                               peer_row_offset, flags, signal_value, done_counter, epoch)
 
@@ -439,6 +472,13 @@ class _GateCounters:
 
 class _CombineCounters(_GateCounters):
     """Zeroed per-feature-tile counters of the fused combine."""
+
+    _pool: dict = {}
+    _retired: list = []
+
+
+class _AlignCounters(_GateCounters):
+    """Zeroed completion counter of the multi-CTA routing."""
 
     _pool: dict = {}
     _retired: list = []
@@ -496,8 +536,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
                     ws.blocks, ws.num_blocks, ws.num_rows)
     else:
         C.router_topk(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob))
-        C.moe_align(ws.ids, ws.weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
-                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows)
+        _align(ws.ids, ws.weights, expert_start, E_loc, ws)
     mark(False, "router")
     mark(True, "experts")
     y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T, top_k,

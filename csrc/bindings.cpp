@@ -376,6 +376,34 @@ void moe_align(const at::Tensor& ids, const at::Tensor& weights, int64_t expert_
   check_rc(afd::launch_moe_align(a, cur_stream()), "moe_align");
 }
 
+// multi-CTA routing (large T); part / counter are int32 scratch
+void moe_align_mt(const at::Tensor& ids, const at::Tensor& weights, int64_t expert_start,
+               int64_t n_local, int64_t block_n, at::Tensor& inv, at::Tensor& row_token,
+               at::Tensor& row_weight, at::Tensor& expert_offsets, at::Tensor& blocks,
+               at::Tensor& num_blocks, at::Tensor& num_rows, at::Tensor& part,
+               at::Tensor& counter) {
+  afd::MoeAlignArgs a{};
+  a.ids = ids.data_ptr<int32_t>();
+  a.weights = weights.data_ptr<float>();
+  a.T = (int)ids.size(0);
+  a.top_k = (int)ids.size(1);
+  a.expert_start = (int)expert_start;
+  a.n_local = (int)n_local;
+  a.block_n = (int)block_n;
+  a.inv = inv.data_ptr<int32_t>();
+  a.row_token = row_token.data_ptr<int32_t>();
+  a.row_weight = row_weight.data_ptr<float>();
+  a.expert_offsets = expert_offsets.data_ptr<int32_t>();
+  a.blocks = reinterpret_cast<int4*>(blocks.data_ptr<int32_t>());
+  a.num_blocks = num_blocks.data_ptr<int32_t>();
+  a.num_rows = num_rows.data_ptr<int32_t>();
+  TORCH_CHECK(part.numel() >= ((ids.numel() + 2047) / 2048) * n_local && counter.numel() >= 1,
+              "moe_align_mt: scratch too small");
+  check_rc(afd::launch_moe_align_mt(a, part.data_ptr<int32_t>(), counter.data_ptr<int32_t>(),
+                                    cur_stream()),
+           "moe_align_mt");
+}
+
 // router softmax/top-k from logits + routing, one launch; ids / weights are
 // written too (for callers that want them)
 void moe_route(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, int64_t top_k,
@@ -433,7 +461,8 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
   g.logits = bf(logits);
   g.ids = ids.data_ptr<int32_t>();
   g.weights = weights.data_ptr<float>();
-  g.done_cnt = counters.data_ptr<int32_t>();
+  g.tok_cnt = counters.data_ptr<int32_t>();
+  g.done_cnt = counters.data_ptr<int32_t>() + T;
   g.T = T;
   g.H = (int)h.size(1);
   g.E = (int)w_router.size(0);
@@ -614,6 +643,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_route", &moe_route);
   m.def("moe_gate", &moe_gate);
+  m.def("moe_align_mt", &moe_align_mt);
   m.def("gemm_down_combine", &gemm_down_combine);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);

@@ -281,20 +281,10 @@ __global__ void router_topk_kernel(RouterArgs a) {
 constexpr int kAlignThreads = 1024;
 constexpr int kMaxLocalExperts = 256;
 
-// Body shared by moe_align_kernel and moe_route_kernel; every thread of the
-// (single) CTA calls it. `ids` / `weights` may live in global or shared memory.
-__device__ void align_body(const int32_t* ids, const float* weights, const MoeAlignArgs& a,
-                           int* cnt, int* off, int* boff) {
-  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
-  __syncthreads();
-  const int n = a.T * a.top_k;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i] - a.expert_start;
-    int slot = -1;
-    if (e >= 0 && e < a.n_local) slot = atomicAdd(&cnt[e], 1);
-    a.inv[i] = slot;  // provisional: slot within the expert
-  }
-  __syncthreads();
+// Row and block offsets of every local expert from its row count `cnt`
+// (warp-wide exclusive scans), the expert offsets, the row-block list and its
+// size. Every thread of the CTA calls it after `cnt` is complete.
+__device__ void scan_and_blocks(const int* cnt, int* off, int* boff, const MoeAlignArgs& a) {
   if (threadIdx.x < 32) {
     // warp-wide exclusive scans of row counts and block counts; lane l owns
     // experts [l * per, (l + 1) * per)
@@ -339,6 +329,23 @@ __device__ void align_body(const int32_t* ids, const float* weights, const MoeAl
     for (int r = 0; r < cnt[e]; r += a.block_n, ++b)
       a.blocks[b] = make_int4(off[e] + r, min(a.block_n, cnt[e] - r), e, 0);
   }
+}
+
+// Body shared by moe_align_kernel and moe_route_kernel; every thread of the
+// (single) CTA calls it. `ids` / `weights` may live in global or shared memory.
+__device__ void align_body(const int32_t* ids, const float* weights, const MoeAlignArgs& a,
+                           int* cnt, int* off, int* boff) {
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int n = a.T * a.top_k;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = ids[i] - a.expert_start;
+    int slot = -1;
+    if (e >= 0 && e < a.n_local) slot = atomicAdd(&cnt[e], 1);
+    a.inv[i] = slot;  // provisional: slot within the expert
+  }
+  __syncthreads();
+  scan_and_blocks(cnt, off, boff, a);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int slot = a.inv[i];
     if (slot < 0) continue;
@@ -357,6 +364,89 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
   pdl_wait();
   pdl_trigger();
   align_body(a.ids, a.weights, a, cnt, off, boff);
+}
+
+// Multi-CTA routing for large token counts (prefill): chunk c of kAlignChunk
+// (token, k) entries gets its per-expert counts and provisional slots in one
+// CTA (moe_align_hist_kernel); the last of those CTAs turns the counts into
+// per-chunk row bases and the expert offsets / row blocks (scan_and_blocks);
+// moe_align_assign_kernel then places every entry. part[c * n_local + e]
+// holds chunk c's count, then its base row. `counter` starts and ends zero.
+constexpr int kAlignChunk = 2048;
+constexpr int kAlignMTThreads = 512;
+
+__global__ void __launch_bounds__(kAlignMTThreads)
+    moe_align_hist_kernel(MoeAlignArgs a, int* part, int* counter) {
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int n = a.T * a.top_k;
+  const int c = blockIdx.x;
+  const int i0 = c * kAlignChunk, i1 = min(n, i0 + kAlignChunk);
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int e = a.ids[i] - a.expert_start;
+    int slot = -1;
+    if (e >= 0 && e < a.n_local) slot = atomicAdd(&cnt[e], 1);
+    a.inv[i] = slot;  // provisional: slot within (chunk, expert)
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) part[c * a.n_local + e] = cnt[e];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int C = gridDim.x;
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x) {
+    int run = 0;
+    for (int cc = 0; cc < C; ++cc) {
+      const int v = __ldcg(part + cc * a.n_local + e);
+      part[cc * a.n_local + e] = run;  // exclusive prefix within the expert
+      run += v;
+    }
+    cnt[e] = run;
+  }
+  __syncthreads();
+  scan_and_blocks(cnt, off, boff, a);
+  for (int e = threadIdx.x; e < a.n_local; e += blockDim.x)
+    for (int cc = 0; cc < C; ++cc) part[cc * a.n_local + e] += off[e];
+  if (threadIdx.x == 0) *counter = 0;
+}
+
+__global__ void __launch_bounds__(kAlignMTThreads)
+    moe_align_assign_kernel(MoeAlignArgs a, const int* part) {
+  pdl_wait();
+  pdl_trigger();
+  const int n = a.T * a.top_k;
+  const int c = blockIdx.x;
+  const int i0 = c * kAlignChunk, i1 = min(n, i0 + kAlignChunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int slot = a.inv[i];
+    if (slot < 0) continue;
+    const int e = a.ids[i] - a.expert_start;
+    const int row = part[c * a.n_local + e] + slot;
+    a.inv[i] = row;
+    a.row_token[row] = i / a.top_k;
+    a.row_weight[row] = a.weights[i];
+  }
+}
+
+int launch_moe_align_mt(const MoeAlignArgs& a, int* part, int* counter, cudaStream_t s) {
+  if (a.n_local > kMaxLocalExperts || a.block_n <= 0) return 1;
+  const int n = a.T * a.top_k;
+  if (n == 0) return 0;
+  const int C = (n + kAlignChunk - 1) / kAlignChunk;
+  int e = (int)launch_k(moe_align_hist_kernel, dim3(C), dim3(kAlignMTThreads), 0, s, a, part,
+                        counter);
+  if (e) return e;
+  return (int)launch_k(moe_align_assign_kernel, dim3(C), dim3(kAlignMTThreads), 0, s, a,
+                       (const int*)part);
 }
 
 // Router softmax/top-k for all T tokens (one warp per token) followed by the
@@ -397,10 +487,10 @@ int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s)
 // in one launch for small token counts. CTA (t, g) normalises token t (same
 // roundings as sum_rmsnorm_kernel; group 0 stores xn), then computes the
 // router logits of experts [g * E/G, (g+1) * E/G) with CUDA-core dot products
-// (fp32 accumulation, one bf16 rounding). The last CTA of the grid (one
-// global counter) runs every token's top-k and then the routing of
-// moe_align_kernel, and resets the counter, so it stays zeroed between
-// launches.
+// (fp32 accumulation, one bf16 rounding). The last of a token's G CTAs (per-
+// token counter) runs that token's top-k; the last token to finish (global
+// counter) runs the routing of moe_align_kernel. Counters are reset by the
+// CTAs that consume them, so the buffer stays zeroed between launches.
 constexpr int kGateThreads = 256;
 constexpr int kGateMaxH = 4096;
 constexpr int kGateMaxEntries = 2048;
@@ -408,7 +498,7 @@ constexpr int kGateMaxEntries = 2048;
 __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, MoeAlignArgs a) {
   __shared__ float xn_s[kGateMaxH];
   __shared__ float red[kGateThreads / 32];
-  __shared__ __nv_bfloat16 lg_s[kGateThreads / 32][256];
+  __shared__ __nv_bfloat16 lg_s[256];
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int off[kMaxLocalExperts + 1];
   __shared__ int boff[kMaxLocalExperts + 1];
@@ -486,29 +576,35 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
     if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
   }
 
-  // 3. the last CTA of the grid: softmax / top-k / renormalise of every
-  // token (warp w takes tokens w, w + 8, ...), then the routing
+  // 3. the token's last CTA: softmax / top-k / renormalise
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == (int)gridDim.x - 1);
+  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[t], 1) == g.G - 1);
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  for (int tt = warp; tt < g.T; tt += kGateThreads / 32) {
-    for (int e = lane; e < g.E; e += 32)
-      lg_s[warp][e] = __ushort_as_bfloat16(
-          __ldcg(reinterpret_cast<const unsigned short*>(g.logits) + (size_t)tt * g.E + e));
-    __syncwarp();
-    topk_token(lg_s[warp], g.E, g.top_k, g.renorm, lane, s_ids + tt * g.top_k,
-               s_w + tt * g.top_k);
-    __syncwarp();
-  }
+  for (int e = threadIdx.x; e < g.E; e += kGateThreads)
+    lg_s[e] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
+                                          (size_t)t * g.E + e));
   __syncthreads();
+  if (warp == 0)
+    topk_token(lg_s, g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
+               g.weights + (size_t)t * g.top_k);
+  if (threadIdx.x == 0) g.tok_cnt[t] = 0;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == g.T - 1);
+  __syncthreads();
+  if (!s_flag) return;
+
+  // 4. the last token: routing over all T tokens
+  __threadfence();
   const int n = g.T * g.top_k;
   for (int i = threadIdx.x; i < n; i += kGateThreads) {
-    g.ids[i] = s_ids[i];
-    g.weights[i] = s_w[i];
+    s_ids[i] = __ldcg(g.ids + i);
+    s_w[i] = __ldcg(g.weights + i);
   }
+  __syncthreads();
   align_body(s_ids, s_w, a, cnt, off, boff);
   if (threadIdx.x == 0) *g.done_cnt = 0;
 }
@@ -698,18 +794,166 @@ __global__ void add_i32_kernel(int* p, int by) {
 }
 
 // ============================================================== launchers ===
+// Many rows: one warp per row (8 rows per CTA), warp-shuffle reduction only.
+// Same roundings as sum_rmsnorm_kernel. H <= 32 * 8 * kRowVec.
+constexpr int kRowVec = 16;
+
+__global__ void __launch_bounds__(256) sum_rmsnorm_rows_kernel(SumNormArgs a, int rows) {
+  pdl_wait();
+  pdl_trigger();
+  block_wait(a.wait, 130);
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const int H = a.H;
+  float xv[kRowVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowVec; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < H) {
+      uint4 pv[kMaxParts];
+#pragma unroll
+      for (int p = 0; p < kMaxParts; ++p)
+        pv[p] = p < a.n_parts
+                    ? *reinterpret_cast<const uint4*>(a.parts[p] + (size_t)row * a.ld_in + col)
+                    : make_uint4(0, 0, 0, 0);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kMaxParts; ++p) {
+        if (p >= a.n_parts) break;
+        const uint32_t* q = &pv[p].x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float u0, u1;
+          unpack_bf16x2(q[e], u0, u1);
+          acc[2 * e] += u0;
+          acc[2 * e + 1] += u1;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xv[c][i] = round_bf16(acc[i]);
+        ss += xv[c][i] * xv[c][i];
+      }
+      if (a.x_out != nullptr) store8(a.x_out + (size_t)row * H + col, xv[c]);
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)H + a.eps);
+#pragma unroll
+  for (int c = 0; c < kRowVec; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < H) {
+      float w[8], y[8];
+      load8(a.weight + col, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(xv[c][i] * rstd);
+      store8(a.y_out + (size_t)row * a.ld_out + col, y);
+    }
+  }
+}
+
 int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s) {
   if (a.H % 8 != 0 || a.H > kNormThreads * 8 * 4 || a.n_parts < 1 || a.n_parts > kMaxParts)
     return 1;
   if (rows == 0) return 0;
+  if (rows >= 256 && a.H <= 32 * 8 * kRowVec)
+    return (int)launch_k(sum_rmsnorm_rows_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, a,
+                         rows);
   return (int)launch_k(sum_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s, a);
+}
+
+// D = 128 variant for many tokens: a warp takes kQKHeads consecutive heads of
+// one token and lane l the rotation pairs (j, j + 64) for j = 2l, 2l + 1, so
+// every load is a 4-byte vector and the loads of all its heads are issued
+// before any reduction. Same roundings as qk_norm_rope_cache_kernel.
+constexpr int kQKHeads = 8;
+
+__global__ void __launch_bounds__(256) qk_norm_rope_cache_d128_kernel(QKRopeArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int n_heads = a.nq + 2 * a.nkv;
+  const int groups = (n_heads + kQKHeads - 1) / kQKHeads;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= a.T * groups) return;
+  const int t = gw / groups;
+  const int h0 = (gw % groups) * kQKHeads;
+  constexpr int D = 128, half = 64;
+  const int j = 2 * lane;
+  const int start = *a.start_pos;
+  const int pos = start + t % a.q_len;
+  const int b = a.batch_offset + t / a.q_len;
+  const __nv_bfloat16* src = a.qkv + (size_t)t * a.ld_qkv;
+  uint32_t lo[kQKHeads], hi[kQKHeads];
+#pragma unroll
+  for (int i = 0; i < kQKHeads; ++i) {
+    const int h = h0 + i;
+    lo[i] = h < n_heads ? *reinterpret_cast<const uint32_t*>(src + h * D + j) : 0u;
+    hi[i] = h < n_heads ? *reinterpret_cast<const uint32_t*>(src + h * D + half + j) : 0u;
+  }
+  const float2 cs = *reinterpret_cast<const float2*>(a.rope + (size_t)pos * D + j);
+  const float2 sn = *reinterpret_cast<const float2*>(a.rope + (size_t)pos * D + half + j);
+  float qw[4], kw[4];
+  {
+    const uint32_t q0 = *reinterpret_cast<const uint32_t*>(a.q_norm + j);
+    const uint32_t q1 = *reinterpret_cast<const uint32_t*>(a.q_norm + half + j);
+    const uint32_t k0 = *reinterpret_cast<const uint32_t*>(a.k_norm + j);
+    const uint32_t k1 = *reinterpret_cast<const uint32_t*>(a.k_norm + half + j);
+    unpack_bf16x2(q0, qw[0], qw[1]);
+    unpack_bf16x2(q1, qw[2], qw[3]);
+    unpack_bf16x2(k0, kw[0], kw[1]);
+    unpack_bf16x2(k1, kw[2], kw[3]);
+  }
+  const float c[2] = {cs.x, cs.y}, sv[2] = {sn.x, sn.y};
+#pragma unroll
+  for (int i = 0; i < kQKHeads; ++i) {
+    const int h = h0 + i;
+    if (h >= n_heads) break;  // warp-uniform
+    float x[4];
+    unpack_bf16x2(lo[i], x[0], x[1]);
+    unpack_bf16x2(hi[i], x[2], x[3]);
+    __nv_bfloat16* dst;
+    if (h >= a.nq + a.nkv) {  // value head: straight copy into the cache
+      dst = a.v_cache + (((size_t)b * a.nkv + (h - a.nq - a.nkv)) * a.s_max + pos) * D;
+      *reinterpret_cast<uint32_t*>(dst + j) = lo[i];
+      *reinterpret_cast<uint32_t*>(dst + half + j) = hi[i];
+      continue;
+    }
+    const bool is_q = h < a.nq;
+    const float* nw = is_q ? qw : kw;
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)D + a.eps);
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float xl = round_bf16(nw[e] * round_bf16(x[e] * rstd));
+      const float xh = round_bf16(nw[2 + e] * round_bf16(x[2 + e] * rstd));
+      // HF: x * cos + rotate_half(x) * sin, each product and the sum in bf16
+      y[e] = round_bf16(round_bf16(xl * c[e]) + round_bf16(-xh * sv[e]));
+      y[2 + e] = round_bf16(round_bf16(xh * c[e]) + round_bf16(xl * sv[e]));
+    }
+    dst = is_q ? a.q_out + ((size_t)t * a.nq + h) * D
+               : a.k_cache + (((size_t)b * a.nkv + (h - a.nq)) * a.s_max + pos) * D;
+    *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(y[0], y[1]);
+    *reinterpret_cast<uint32_t*>(dst + half + j) = pack_bf16x2(y[2], y[3]);
+  }
 }
 
 int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s) {
   if (a.D % 64 != 0 || a.D > 128) return 1;
-  const int warps = a.T * (a.nq + 2 * a.nkv);
-  if (warps == 0) return 0;
+  const int n_heads = a.nq + 2 * a.nkv;
   const int wpb = 8;
+  if (a.D == 128 && a.ld_qkv % 2 == 0) {
+    const int warps = a.T * ((n_heads + kQKHeads - 1) / kQKHeads);
+    if (warps == 0) return 0;
+    return (int)launch_k(qk_norm_rope_cache_d128_kernel, dim3((warps + wpb - 1) / wpb),
+                         dim3(wpb * 32), 0, s, a);
+  }
+  const int warps = a.T * n_heads;
+  if (warps == 0) return 0;
   return (int)launch_k(qk_norm_rope_cache_kernel, dim3((warps + wpb - 1) / wpb), dim3(wpb * 32), 0, s, a);
 }
 

@@ -119,6 +119,7 @@ struct MoeGateArgs {
   __nv_bfloat16* logits;         // [T, E] scratch
   int32_t* ids;                  // [T, top_k] (out)
   float* weights;                // [T, top_k] (out)
+  int* tok_cnt;                  // [T] zeroed, self-cleaning
   int* done_cnt;                 // [1] zeroed, self-cleaning
   int T, H, E, G, top_k, renorm;
   float eps;
@@ -180,6 +181,9 @@ int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s);
 int launch_qk_norm_rope_cache(const QKRopeArgs& a, cudaStream_t s);
 int launch_router_topk(const RouterArgs& a, cudaStream_t s);
 int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s);
+// multi-CTA routing for large T: part int32 [ceil(T*top_k / 2048) * n_local],
+// counter int32 [1] zeroed (left zeroed)
+int launch_moe_align_mt(const MoeAlignArgs& a, int* part, int* counter, cudaStream_t s);
 // router top-k + moe_align in one launch (T * top_k <= 4096)
 int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s);
 int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s);
