@@ -150,7 +150,7 @@ def _block_n(rows: int) -> int:
 
 
 # row-block size of prefill-sized grouped GEMMs (AFD_MOE_BN_LARGE=128 for A/B)
-_MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "256"))
+_MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "128"))
 
 
 def _moe_block_n(rows: int) -> int:

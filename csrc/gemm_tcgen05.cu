@@ -63,8 +63,9 @@ struct GemmSmem {
   // epilogue staging: per warp 16 rows x 32 features bf16
   static constexpr int kStageOutBytes = kEpiWarps * 16 * 32 * 2;
   static constexpr int kRowIdBytes = BN * 4;                 // gathered rows of one block
-  static constexpr int kTotal =
-      kDataBytes + kStageOutBytes + kRowIdBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kScaleBytes = kEpiWarps * BN * 4;     // warp-private row scales
+  static constexpr int kTotal = kDataBytes + kStageOutBytes + kRowIdBytes + kScaleBytes +
+                                1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ int4 unit_block(const GemmArgs& a, int b) {
@@ -165,6 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* rows_s = reinterpret_cast<int*>(smem + L::kDataBytes + L::kStageOutBytes + 256);
+  float* scale_s = reinterpret_cast<float*>(smem + L::kDataBytes + L::kStageOutBytes + 256 +
+                                            L::kRowIdBytes);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -329,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();  // residual / row scale / outputs belong to earlier kernels
     const int q = warp & 3;
     __nv_bfloat16* st = stage_out + (warp - 2) * 16 * 32;
+    float* sc = scale_s + (warp - 2) * BN;  // this warp's copy of the tile's row scales
     volatile int* last_flag = abort_flag + 1;
     int t = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
@@ -370,7 +374,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         emit = *last_flag != 0;
         if (emit) __threadfence();
       }
-      for (int c = 0; c < blk.y && emit; c += 16) {
+      if (!SWIGLU && args.row_scale != nullptr) {
+        // all of the tile's row scales in flight at once, kept in smem
+        for (int r = lane; r < blk.y; r += 32) sc[r] = args.row_scale[blk.x + r];
+        __syncwarp();
+      }
+      // 32 accumulator columns (rows of the output) per TMEM load, handled as
+      // two 16-row halves through the staging tile
+      for (int c0 = 0; c0 < blk.y && emit; c0 += 32) {
+      float a32[32], u32[32];
+      if (wsp == nullptr) {
+        tmem_ld32(t_row + c0, a32);
+        if constexpr (SWIGLU) tmem_ld32(t_row + L::kAccCols + c0, u32);
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c = c0 + 16 * hh;
+        if (c >= blk.y) break;
         float acc[16];
         if (wsp != nullptr) {
           // last split: sum the partial slices in split order; four slices'
@@ -394,11 +414,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) acc[j] += v[u][j];
           }
         } else {
-          tmem_ld16(t_row + c, acc);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = a32[16 * hh + j];
         }
         if (SWIGLU) {
           float up[16];
-          tmem_ld16(t_row + L::kAccCols + c, up);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) up[j] = u32[16 * hh + j];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             // HF rounds gate/up to bf16 before the activation and the product
@@ -408,10 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (args.row_scale != nullptr) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int r = min(c + j, blk.y - 1);
-            acc[j] = round_bf16(acc[j]) * args.row_scale[blk.x + r];
-          }
+          for (int j = 0; j < 16; ++j) acc[j] = round_bf16(acc[j]) * sc[min(c + j, blk.y - 1)];
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) st[j * 32 + lane] = f_to_bf16(acc[j]);
@@ -447,6 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
+      }
       }
       if (wsp != nullptr) {
         if (emit && threadIdx.x == 64) args.tile_counters[un.tile] = 0;

@@ -794,10 +794,10 @@ __global__ void add_i32_kernel(int* p, int by) {
 }
 
 // ============================================================== launchers ===
-// Many rows: one warp per row (8 rows per CTA), warp-shuffle reduction only.
-// Same roundings as sum_rmsnorm_kernel. H <= 32 * 8 * kRowVec.
-constexpr int kRowVec = 16;
-
+// Many rows: one warp per row (8 rows per CTA), warp-shuffle reduction only;
+// H = 256 * VPL, each lane owns VPL 8-wide vectors and requests all of a
+// part's vectors before adding them. Same roundings as sum_rmsnorm_kernel.
+template <int VPL>
 __global__ void __launch_bounds__(256) sum_rmsnorm_rows_kernel(SumNormArgs a, int rows) {
   pdl_wait();
   pdl_trigger();
@@ -805,52 +805,49 @@ __global__ void __launch_bounds__(256) sum_rmsnorm_rows_kernel(SumNormArgs a, in
   const int row = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;
-  const int H = a.H;
-  float xv[kRowVec][8];
-  float ss = 0.f;
+  float xv[VPL][8];
 #pragma unroll
-  for (int c = 0; c < kRowVec; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < H) {
-      uint4 pv[kMaxParts];
+  for (int c = 0; c < VPL; ++c)
 #pragma unroll
-      for (int p = 0; p < kMaxParts; ++p)
-        pv[p] = p < a.n_parts
-                    ? *reinterpret_cast<const uint4*>(a.parts[p] + (size_t)row * a.ld_in + col)
-                    : make_uint4(0, 0, 0, 0);
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < 8; ++i) xv[c][i] = 0.f;
+  for (int p = 0; p < a.n_parts; ++p) {
+    uint4 v[VPL];
 #pragma unroll
-      for (int p = 0; p < kMaxParts; ++p) {
-        if (p >= a.n_parts) break;
-        const uint32_t* q = &pv[p].x;
+    for (int c = 0; c < VPL; ++c)
+      v[c] = *reinterpret_cast<const uint4*>(a.parts[p] + (size_t)row * a.ld_in +
+                                             (c * 32 + lane) * 8);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float u0, u1;
-          unpack_bf16x2(q[e], u0, u1);
-          acc[2 * e] += u0;
-          acc[2 * e + 1] += u1;
-        }
+    for (int c = 0; c < VPL; ++c) {
+      const uint32_t* q = &v[c].x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u0, u1;
+        unpack_bf16x2(q[e], u0, u1);
+        xv[c][2 * e] += u0;
+        xv[c][2 * e + 1] += u1;
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xv[c][i] = round_bf16(acc[i]);
-        ss += xv[c][i] * xv[c][i];
-      }
-      if (a.x_out != nullptr) store8(a.x_out + (size_t)row * H + col, xv[c]);
     }
   }
-  ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / (float)H + a.eps);
+  float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowVec; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < H) {
-      float w[8], y[8];
-      load8(a.weight + col, w);
+  for (int c = 0; c < VPL; ++c) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(xv[c][i] * rstd);
-      store8(a.y_out + (size_t)row * a.ld_out + col, y);
+    for (int i = 0; i < 8; ++i) {
+      xv[c][i] = round_bf16(xv[c][i]);
+      ss += xv[c][i] * xv[c][i];
     }
+    if (a.x_out != nullptr) store8(a.x_out + (size_t)row * a.H + (c * 32 + lane) * 8, xv[c]);
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)a.H + a.eps);
+#pragma unroll
+  for (int c = 0; c < VPL; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    float w[8], y[8];
+    load8(a.weight + col, w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(xv[c][i] * rstd);
+    store8(a.y_out + (size_t)row * a.ld_out + col, y);
   }
 }
 
@@ -858,9 +855,12 @@ int launch_sum_rmsnorm(const SumNormArgs& a, int rows, cudaStream_t s) {
   if (a.H % 8 != 0 || a.H > kNormThreads * 8 * 4 || a.n_parts < 1 || a.n_parts > kMaxParts)
     return 1;
   if (rows == 0) return 0;
-  if (rows >= 256 && a.H <= 32 * 8 * kRowVec)
-    return (int)launch_k(sum_rmsnorm_rows_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, a,
-                         rows);
+  if (rows >= 256) {
+    const dim3 grid((rows + 7) / 8), block(256);
+    if (a.H == 1024) return (int)launch_k(sum_rmsnorm_rows_kernel<4>, grid, block, 0, s, a, rows);
+    if (a.H == 2048) return (int)launch_k(sum_rmsnorm_rows_kernel<8>, grid, block, 0, s, a, rows);
+    if (a.H == 4096) return (int)launch_k(sum_rmsnorm_rows_kernel<16>, grid, block, 0, s, a, rows);
+  }
   return (int)launch_k(sum_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, s, a);
 }
 
