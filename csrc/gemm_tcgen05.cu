@@ -341,6 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ft = un.tile % args.f_tiles;
       const int slot = t % L::kSlots;
       const uint32_t tpar = (uint32_t)((t / L::kSlots) & 1);
+      if (!SWIGLU && args.row_scale != nullptr) {
+        // the tile's row scales, requested while its MMAs still run
+        for (int r = lane; r < blk.y; r += 32) sc[r] = args.row_scale[blk.x + r];
+        __syncwarp();
+      }
       // warp-uniform: the TMEM loads below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[slot], tpar, abort_flag, args.status, 30)))
         break;
@@ -373,11 +378,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         epi_bar();
         emit = *last_flag != 0;
         if (emit) __threadfence();
-      }
-      if (!SWIGLU && args.row_scale != nullptr) {
-        // all of the tile's row scales in flight at once, kept in smem
-        for (int r = lane; r < blk.y; r += 32) sc[r] = args.row_scale[blk.x + r];
-        __syncwarp();
       }
       // 32 accumulator columns (rows of the output) per TMEM load, handled as
       // two 16-row halves through the staging tile
