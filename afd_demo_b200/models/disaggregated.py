@@ -74,6 +74,10 @@ class DisaggregatedQwenModel:
         self._last_generation_metrics: Dict[str, Any] = {}
         self._last_decode_timing = None
         self._graphs: Dict[Any, Any] = {}
+        # SMs left to the FFN's persistent GEMMs when both roles share a GPU
+        # in a DBO schedule (0: all); AFD_COLOCATED_FFN_SMS overrides
+        import os
+        self.colocated_ffn_sms = int(os.environ.get("AFD_COLOCATED_FFN_SMS", "0"))
 
     # ------------------------------------------------------------ set-up
     @property

@@ -93,6 +93,26 @@ def num_sms() -> int:
     return _NUM_SMS
 
 
+class sm_budget:
+    """Caps the grid of the persistent GEMMs launched inside the block at `n`
+    SMs (None or 0: no cap), leaving the rest to kernels of a concurrent
+    stream. Launch parameters are fixed at launch, so a captured CUDA graph
+    keeps the cap that was active during capture."""
+
+    def __init__(self, n: Optional[int]):
+        self.n = int(n or 0)
+
+    def __enter__(self):
+        if self.n:
+            ext().set_gemm_sm_cap(self.n)
+        return self
+
+    def __exit__(self, *exc):
+        if self.n:
+            ext().set_gemm_sm_cap(0)
+        return False
+
+
 # ------------------------------------------------------------------ norms --
 class FlagWait(NamedTuple):
     """A receive folded into the consuming kernel: the kernel waits (bounded

@@ -25,6 +25,7 @@ from typing import Dict, List, Optional
 
 import torch
 
+from .. import ops
 from ..utils.timing import EventType, TimingTracker
 from .micro_batch import ForwardPlan
 
@@ -87,8 +88,12 @@ class PipelineEngine:
         if has_ffn:
             m_.ffn_worker.tracker = tf
 
+        # co-located DBO: the FFN's persistent GEMMs leave SMs to the attention
+        # stream so the two micro-batches really run side by side
+        ffn_sms = m_.colocated_ffn_sms if (colocated and not serial) else 0
+
         def ffn_block(l: int, m: int):
-            with _on(s_ffn):
+            with _on(s_ffn), ops.sm_budget(ffn_sms):
                 if tf:
                     tf.mark_start(EventType.RECV_WAIT, l, m)
                 h = tr.a2f_recv(l, m)

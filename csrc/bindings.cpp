@@ -41,6 +41,12 @@ inline T* opt_ptr(const c10::optional<at::Tensor>& t) {
 }
 
 int g_num_sms = 0;
+// Upper bound on the persistent GEMM grid (0: all SMs). Set around work that
+// should leave SMs to a concurrent stream (co-located attention + FFN).
+static int g_sm_cap = 0;
+
+void set_gemm_sm_cap(int64_t cap) { g_sm_cap = (int)cap; }
+
 int num_sms() {
   if (g_num_sms == 0) {
     int dev = 0;
@@ -115,7 +121,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   p.swiglu = swiglu;
   p.block_n = (int)block_n;
   p.units_hint = (int)units_hint;
-  p.num_sms = num_sms();
+  p.num_sms = g_sm_cap > 0 ? std::min(num_sms(), g_sm_cap) : num_sms();
   if (a.blocks == nullptr && dense_rows == 0) return;
   check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_swapab");
 }
@@ -192,7 +198,7 @@ void gemm_down_combine(const at::Tensor& w, const at::Tensor& x, at::Tensor& y, 
   p.swiglu = false;
   p.block_n = (int)block_n;
   p.units_hint = (int)units_hint;
-  p.num_sms = num_sms();
+  p.num_sms = g_sm_cap > 0 ? std::min(num_sms(), g_sm_cap) : num_sms();
   check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_down_combine");
 }
 
@@ -643,6 +649,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_route", &moe_route);
   m.def("moe_gate", &moe_gate);
+  m.def("set_gemm_sm_cap", &set_gemm_sm_cap);
   m.def("moe_align_mt", &moe_align_mt);
   m.def("gemm_down_combine", &gemm_down_combine);
   m.def("moe_gather", &moe_gather);
