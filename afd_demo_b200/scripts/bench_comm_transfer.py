@@ -22,7 +22,14 @@ Implementations:
 * gemm (a2f only): the real fused path -- the o_proj tcgen05 GEMM
   ([tokens, 4096] x [4096, 2048] + residual) whose epilogue stores the output
   tile into every FFN GPU -- against the same GEMM stored locally followed by
-  NCCL isends.
+  NCCL isends;
+* moe (f2a only): the real fused return -- every FFN rank runs its slice of
+  the Qwen3-30B-A3B expert layer (128 / n_ffn experts, top-8 routing) whose
+  combine stores each token's partial sum (FFN rank 0 adds the residual)
+  straight into the attention GPU's slot for that rank -- against the same
+  layer stored locally followed by NCCL isends. Its roofline is the slowest
+  of the local expert weights over HBM, the FLOPs over the GEMM peak and the
+  returned rows over NVLink.
 
 Roofline of a transfer: bytes crossing the busiest GPU's NVLink ports
 (tokens * row bytes * peers) / 770 GB/s (measured peer copy bandwidth per
@@ -51,7 +58,19 @@ if __package__ in (None, ""):
 H = 2048
 TOPK = 8
 LINK_GBS = 770.0
-GEMM_TFLOPS = 1656.5
+
+
+def _peaks():
+    """HBM bytes/s and bf16 FLOP/s: MEASURED_PEAKS.json when present."""
+    p = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]) * 1e9, float(d["bf16_tflops"]) * 1e12
+    return 6.65e12, 1.59e15
+
+
+HBM_BPS, GEMM_FLOPS = _peaks()
+GEMM_TFLOPS = GEMM_FLOPS / 1e12
 
 
 def parse():
@@ -59,7 +78,7 @@ def parse():
     ap.add_argument("--sizes-mib", default="0.004,0.031,1,16,32")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--iters", type=int, default=50)
-    ap.add_argument("--impls", default="nccl,fused,gemm")
+    ap.add_argument("--impls", default="nccl,fused,gemm,moe")
     ap.add_argument("--directions", default="a2f,f2a")
     ap.add_argument("--output", default="results/comm_bench/comm_transfer.json")
     ap.add_argument("--csv-output", default="")
@@ -203,6 +222,60 @@ def main() -> int:
                 row["gemm_roofline_ms"] = max(flops / (GEMM_TFLOPS * 1e12),
                                               tokens * H * 2 * n_ffn / (LINK_GBS * 1e9)) * 1e3
                 row["gemm_fused_roofline_frac"] = row["gemm_roofline_ms"] / row["gemm_fused_ms"]
+            if "moe" in a.impls and direction == "f2a":
+                E, I, Ek = 128, 768, 128 // n_ffn
+                fi = rank - 1
+                if rank > 0:
+                    w_gu = (torch.randn(Ek, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                    w_dn = (torch.randn(Ek, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                gl = torch.Generator(device=dev).manual_seed(7)  # same routing on every rank
+                rid = torch.stack([torch.randperm(E, device=dev, generator=gl)[:TOPK]
+                                   for _ in range(min(tokens, 4096))])
+                rid = rid.repeat((tokens + rid.shape[0] - 1) // rid.shape[0], 1)[:tokens]
+                rid = rid.to(torch.int32).contiguous()
+                rw = torch.full((tokens, TOPK), 1.0 / TOPK, device=dev)
+                xn = hidden
+                res = hidden if rank == 1 else None
+                out_loc = torch.empty(tokens, H, device=dev, dtype=torch.bfloat16)
+
+                def moe_fused(i):
+                    flag_value[0] += 1
+                    v = flag_value[0]
+                    if rank > 0:
+                        ops.moe_experts(xn, rid, rw, w_gu, w_dn, fi * Ek, residual=res,
+                                        peers=[dst_addr(0, rank)], seg_offsets=[0, tokens],
+                                        flags=[flag_addr(peer[0], rank)], signal_value=v,
+                                        done_counter=counter)
+                    else:
+                        C.wait_flags([flag_addr(base, r) for r in senders], v, status,
+                                     int(a.timeout_ms * 1e6), None)
+
+                def moe_nccl(i):
+                    works = []
+                    if rank > 0:
+                        ops.moe_experts(xn, rid, rw, w_gu, w_dn, fi * Ek, residual=res,
+                                        out=out_loc)
+                        works = [dist.isend(out_loc, dst=0)]
+                    else:
+                        works = [dist.irecv(recv[:tokens * H * 2].view(torch.bfloat16), src=r)
+                                 for r in senders]
+                    for wk in works:
+                        wk.wait()
+
+                for i in range(a.warmup):
+                    moe_fused(i)
+                    moe_nccl(i)
+                row["moe_fused_ms"] = timed(moe_fused, a.iters)
+                row["moe_nccl_ms"] = timed(moe_nccl, a.iters)
+                hit = torch.zeros(E, dtype=torch.bool, device=dev)
+                hit[rid.view(-1).long()] = True
+                loc_hit = max(int(hit[r * Ek:(r + 1) * Ek].sum()) for r in range(n_ffn))
+                wbytes = loc_hit * 3 * I * H * 2
+                flops = 2.0 * tokens * TOPK * 3 * I * H / n_ffn
+                row["moe_local_experts_hit"] = loc_hit
+                row["moe_roofline_ms"] = max(wbytes / HBM_BPS, flops / GEMM_FLOPS,
+                                             tokens * H * 2 * n_ffn / (LINK_GBS * 1e9)) * 1e3
+                row["moe_fused_roofline_frac"] = row["moe_roofline_ms"] / row["moe_fused_ms"]
             for k in ("nccl_ms", "fused_ms"):
                 if k in row:
                     row[k.replace("_ms", "_gbs")] = link_bytes / (row[k] * 1e-3) / 1e9
