@@ -609,11 +609,173 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   if (threadIdx.x == 0) *g.done_cnt = 0;
 }
 
+// Tiled variant (E % 16 == 0): CTA (token group tg of 16, expert group eg of
+// 16) normalises its 16 tokens into shared memory (expert group 0 also stores
+// xn), then thread (t, e) = (tid / 16, tid % 16) computes one router logit
+// from the shared-memory row and the router row, so each router row is read
+// once per token group instead of once per token. The last expert group of a
+// token group (per-group counter) runs its 16 tokens' top-k (a warp per two
+// tokens); the last token group (global counter) runs the routing.
+constexpr int kGateTile = 16;
+
+__global__ void __launch_bounds__(kGateThreads) moe_gate_tiled_kernel(MoeGateArgs g,
+                                                                      MoeAlignArgs a) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(gsm);           // [16][H]
+  __shared__ __nv_bfloat16 lg_s[kGateThreads / 32][256];
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  __shared__ int32_t s_ids[kGateMaxEntries];
+  __shared__ float s_w[kGateMaxEntries];
+  __shared__ int s_flag;
+  pdl_wait();
+  pdl_trigger();
+  block_wait(g.wait, 150);
+  const int n_eg = g.E / kGateTile;
+  const int tg = blockIdx.x / n_eg, eg = blockIdx.x % n_eg;
+  const int t0 = tg * kGateTile;
+  const int nt = min(kGateTile, g.T - t0);
+  const int H = g.H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // 1. RMSNorm of the group's tokens: warp w takes tokens 2w, 2w + 1
+  for (int tl = warp; tl < kGateTile; tl += kGateThreads / 32) {
+    __nv_bfloat16* xr = xs + (size_t)tl * H;
+    if (tl >= nt) {  // padding rows: zeros (their logits are never used)
+      for (int col = lane * 8; col < H; col += 256)
+        *reinterpret_cast<uint4*>(xr + col) = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const __nv_bfloat16* hr = g.h + (size_t)(t0 + tl) * g.ld_h;
+    constexpr int kV = kGateMaxH / 256;
+    uint4 hv[kV];
+#pragma unroll
+    for (int c = 0; c < kV; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      hv[c] = col < H ? *reinterpret_cast<const uint4*>(hr + col) : make_uint4(0, 0, 0, 0);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kV; ++c) {
+      const uint32_t* q = &hv[c].x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u0, u1;
+        unpack_bf16x2(q[e], u0, u1);
+        ss += u0 * u0 + u1 * u1;
+      }
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)H + g.eps);
+#pragma unroll
+    for (int c = 0; c < kV; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col >= H) break;
+      float x[8], w[8], y[8];
+      const uint32_t* q = &hv[c].x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) unpack_bf16x2(q[e], x[2 * e], x[2 * e + 1]);
+      load8(g.norm_w + col, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(x[i] * rstd);
+      store8(xr + col, y);
+      if (eg == 0) store8(g.xn + (size_t)(t0 + tl) * H + col, y);
+    }
+  }
+  __syncthreads();
+
+  // 2. logits: thread (tl, el) = (tid / 16, tid % 16)
+  {
+    const int tl = threadIdx.x / kGateTile, el = threadIdx.x % kGateTile;
+    const int e = eg * kGateTile + el;
+    const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
+    const __nv_bfloat16* xr = xs + (size_t)tl * H;
+    float acc = 0.f;
+    for (int col = 0; col < H; col += 16) {
+      const uint4 w0 = *reinterpret_cast<const uint4*>(wr + col);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(wr + col + 8);
+      const uint4 x0 = *reinterpret_cast<const uint4*>(xr + col);
+      const uint4 x1 = *reinterpret_cast<const uint4*>(xr + col + 8);
+      const uint32_t* pw0 = &w0.x;
+      const uint32_t* pw1 = &w1.x;
+      const uint32_t* px0 = &x0.x;
+      const uint32_t* px1 = &x1.x;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a0, a1, b0, b1;
+        unpack_bf16x2(pw0[i], a0, a1);
+        unpack_bf16x2(px0[i], b0, b1);
+        acc += a0 * b0;
+        acc += a1 * b1;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a0, a1, b0, b1;
+        unpack_bf16x2(pw1[i], a0, a1);
+        unpack_bf16x2(px1[i], b0, b1);
+        acc += a0 * b0;
+        acc += a1 * b1;
+      }
+    }
+    if (tl < nt) g.logits[(size_t)(t0 + tl) * g.E + e] = __float2bfloat16_rn(acc);
+  }
+
+  // 3. the token group's last CTA: top-k of its tokens
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[tg], 1) == n_eg - 1);
+  __syncthreads();
+  if (!s_flag) return;
+  __threadfence();
+  for (int tl = warp; tl < nt; tl += kGateThreads / 32) {
+    const int t = t0 + tl;
+    for (int e = lane; e < g.E; e += 32)
+      lg_s[warp][e] = __ushort_as_bfloat16(
+          __ldcg(reinterpret_cast<const unsigned short*>(g.logits) + (size_t)t * g.E + e));
+    __syncwarp();
+    topk_token(lg_s[warp], g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
+               g.weights + (size_t)t * g.top_k);
+    __syncwarp();
+  }
+  if (threadIdx.x == 0) g.tok_cnt[tg] = 0;
+  __threadfence();
+  __syncthreads();
+  const int n_tg = (g.T + kGateTile - 1) / kGateTile;
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == n_tg - 1);
+  __syncthreads();
+  if (!s_flag) return;
+
+  // 4. the last token group: routing over all T tokens
+  __threadfence();
+  const int n = g.T * g.top_k;
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    s_ids[i] = __ldcg(g.ids + i);
+    s_w[i] = __ldcg(g.weights + i);
+  }
+  __syncthreads();
+  align_body(s_ids, s_w, a, cnt, off, boff);
+  if (threadIdx.x == 0) *g.done_cnt = 0;
+}
+
 int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
   if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % g.G != 0 ||
       g.top_k > 16 || g.H > kGateMaxH || g.H % 8 != 0 || a.n_local > kMaxLocalExperts ||
       a.block_n <= 0)
     return 1;
+  if (g.E % kGateTile == 0) {
+    const int smem = kGateTile * g.H * 2;
+    static int attr = 0;
+    if (smem > attr) {
+      cudaError_t e = cudaFuncSetAttribute(moe_gate_tiled_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kGateTile * kGateMaxH * 2);
+      if (e != cudaSuccess) return (int)e;
+      attr = kGateTile * kGateMaxH * 2;
+    }
+    const int grid = ((g.T + kGateTile - 1) / kGateTile) * (g.E / kGateTile);
+    return (int)launch_k(moe_gate_tiled_kernel, dim3(grid), dim3(kGateThreads), smem, s, g, a);
+  }
   return (int)launch_k(moe_gate_kernel, dim3(g.T * g.G), dim3(kGateThreads), 0, s, g, a);
 }
 
