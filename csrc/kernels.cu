@@ -685,40 +685,50 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_tiled_kernel(MoeGateArg
   }
   __syncthreads();
 
-  // 2. logits: thread (tl, el) = (tid / 16, tid % 16)
+  // 2. logits: warp w takes tokens 2w, 2w + 1 and all 16 experts of the
+  // group; lanes split the hidden dimension (8 elements per lane per 256-wide
+  // chunk), every router vector feeds both tokens, warp sums at the end
   {
-    const int tl = threadIdx.x / kGateTile, el = threadIdx.x % kGateTile;
-    const int e = eg * kGateTile + el;
-    const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
-    const __nv_bfloat16* xr = xs + (size_t)tl * H;
-    float acc = 0.f;
-    for (int col = 0; col < H; col += 16) {
-      const uint4 w0 = *reinterpret_cast<const uint4*>(wr + col);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(wr + col + 8);
-      const uint4 x0 = *reinterpret_cast<const uint4*>(xr + col);
-      const uint4 x1 = *reinterpret_cast<const uint4*>(xr + col + 8);
-      const uint32_t* pw0 = &w0.x;
-      const uint32_t* pw1 = &w1.x;
-      const uint32_t* px0 = &x0.x;
-      const uint32_t* px1 = &x1.x;
+    const int ta = 2 * warp, tb = 2 * warp + 1;
+    const __nv_bfloat16* xa = xs + (size_t)ta * H;
+    const __nv_bfloat16* xb = xs + (size_t)tb * H;
+    const __nv_bfloat16* wr0 = g.w_router + (size_t)(eg * kGateTile) * H;
+    float acc[2][kGateTile];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float a0, a1, b0, b1;
-        unpack_bf16x2(pw0[i], a0, a1);
-        unpack_bf16x2(px0[i], b0, b1);
-        acc += a0 * b0;
-        acc += a1 * b1;
-      }
+    for (int e = 0; e < kGateTile; ++e) acc[0][e] = acc[1][e] = 0.f;
+    for (int col = lane * 8; col < H; col += 256) {
+      float fa[8], fb[8];
+      load8(xa + col, fa);
+      load8(xb + col, fb);
+      uint4 wv[kGateTile];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float a0, a1, b0, b1;
-        unpack_bf16x2(pw1[i], a0, a1);
-        unpack_bf16x2(px1[i], b0, b1);
-        acc += a0 * b0;
-        acc += a1 * b1;
+      for (int e = 0; e < kGateTile; ++e)
+        wv[e] = *reinterpret_cast<const uint4*>(wr0 + (size_t)e * H + col);
+#pragma unroll
+      for (int e = 0; e < kGateTile; ++e) {
+        const uint32_t* q = &wv[e].x;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float w0, w1;
+          unpack_bf16x2(q[i], w0, w1);
+          acc[0][e] += w0 * fa[2 * i] + w1 * fa[2 * i + 1];
+          acc[1][e] += w0 * fb[2 * i] + w1 * fb[2 * i + 1];
+        }
       }
     }
-    if (tl < nt) g.logits[(size_t)(t0 + tl) * g.E + e] = __float2bfloat16_rn(acc);
+#pragma unroll
+    for (int e = 0; e < kGateTile; ++e) {
+      acc[0][e] = warp_sum(acc[0][e]);
+      acc[1][e] = warp_sum(acc[1][e]);
+    }
+    // lane e writes (ta, e), lane 16 + e writes (tb, e)
+    const int e = lane % kGateTile;
+    const int tl = lane < kGateTile ? ta : tb;
+    float v = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGateTile; ++k)
+      if (k == e) v = lane < kGateTile ? acc[0][k] : acc[1][k];
+    if (tl < nt) g.logits[(size_t)(t0 + tl) * g.E + eg * kGateTile + e] = __float2bfloat16_rn(v);
   }
 
   // 3. the token group's last CTA: top-k of its tokens
