@@ -504,6 +504,27 @@ class _AlignCounters(_GateCounters):
     _retired: list = []
 
 
+def moe_gate(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor, top_k: int,
+             eps: float, norm_topk_prob: bool = True, expert_start: int = 0,
+             n_local: Optional[int] = None) -> Tuple[torch.Tensor, "MoEWorkspace"]:
+    """The fused decode gate alone (RMSNorm, router, top-k, routing): returns
+    the normalised input and the routing workspace (ids, weights, row blocks)."""
+    T, H = h.shape
+    E = w_router.shape[0]
+    n_local = E if n_local is None else n_local
+    if not _gate_fusable(T, H, E, top_k):
+        raise ValueError("moe_gate: shape outside the fused gate's limits")
+    ws = MoEWorkspace(T, top_k, n_local, H, 768, _moe_block_n(T), h.device, h.dtype)
+    xn = torch.empty_like(h)
+    logits = torch.empty(T, E, device=h.device, dtype=h.dtype)
+    ext().moe_gate(h, post_norm_w, w_router, xn, logits, ws.ids, ws.weights,
+                   _GateCounters.get(h.device, T), top_k, bool(norm_topk_prob), float(eps),
+                   _gate_groups(T, E), expert_start, n_local, ws.block_n, ws.inv, ws.row_token,
+                   ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows,
+                   *_wait_args(None))
+    return xn, ws
+
+
 def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
             w_gate_up: torch.Tensor, w_down: torch.Tensor, top_k: int, eps: float,
             norm_topk_prob: bool = True, expert_start: int = 0, add_residual: bool = True,

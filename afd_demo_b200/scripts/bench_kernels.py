@@ -150,6 +150,9 @@ def main(argv=None) -> int:
                timeit(lambda i: ops.moe_experts(x, ids, wts, w_gu[i % n_e], w_dn[i % n_e], 0,
                                                 residual=h), a.iters, a.warmup),
                eb, 2 * T * k * 3 * I * H)
+        report("moe gate (norm+router+top-k+routing)", T,
+               timeit(lambda i: ops.moe_gate(h, pn, w_r[i % n_qkv], k, 1e-6), a.iters, a.warmup),
+               E * H * 2 + 2 * T * H * 2, 2 * T * E * H)
         report("moe block (gate+experts)", T,
                timeit(lambda i: ops.moe_ffn(h, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
                                             1e-6), a.iters, a.warmup),

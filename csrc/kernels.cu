@@ -7,6 +7,8 @@
 // Numerics follow HF Qwen3-MoE: fp32 math with a bf16 rounding at every point
 // where the eager PyTorch code materialises a bf16 tensor.
 
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -773,7 +775,14 @@ int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s)
       g.top_k > 16 || g.H > kGateMaxH || g.H % 8 != 0 || a.n_local > kMaxLocalExperts ||
       a.block_n <= 0)
     return 1;
-  if (g.E % kGateTile == 0) {
+  // per-token CTAs parallelise best for a few tokens; the tiled kernel reads
+  // each router row once per 16 tokens, which wins from a few dozen tokens
+  // (AFD_GATE_TILED_MIN_T moves the switch point for A/B measurements)
+  static const int tiled_min_t = [] {
+    const char* e = std::getenv("AFD_GATE_TILED_MIN_T");
+    return e != nullptr ? std::atoi(e) : 48;
+  }();
+  if (g.E % kGateTile == 0 && g.T >= tiled_min_t) {
     const int smem = kGateTile * g.H * 2;
     static int attr = 0;
     if (smem > attr) {
