@@ -497,6 +497,7 @@ constexpr int kGateThreads = 256;
 constexpr int kGateMaxH = 4096;
 constexpr int kGateMaxEntries = 2048;
 
+template <int kVec>  // router vectors per lane = H / 256
 __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, MoeAlignArgs a) {
   __shared__ float xn_s[kGateMaxH];
   __shared__ float red[kGateThreads / 32];
@@ -507,16 +508,34 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   __shared__ int32_t s_ids[kGateMaxEntries];
   __shared__ float s_w[kGateMaxEntries];
   __shared__ int s_flag;
-  pdl_wait();
-  pdl_trigger();
-  block_wait(g.wait, 140);
   const int t = blockIdx.x / g.G;
   const int grp = blockIdx.x % g.G;
   const int H = g.H;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int kChunks = (kVec + kGateThreads / 32 - 1) / (kGateThreads / 32);
+  // Static weights first, before waiting on the previous kernel: this warp's
+  // first router row and this thread's slice of the norm weight.
+  const int per_grp = g.E / g.G;
+  uint4 wv0[kVec];
+#pragma unroll
+  for (int c = 0; c < kVec; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    wv0[c] = (warp < per_grp && col < H)
+                 ? *reinterpret_cast<const uint4*>(g.w_router +
+                                                   (size_t)(grp * per_grp + warp) * H + col)
+                 : make_uint4(0, 0, 0, 0);
+  }
+  float nwt[kChunks][8];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) load8(g.norm_w + col, nwt[c]);
+  }
+  pdl_wait();
+  pdl_trigger();
+  block_wait(g.wait, 140);
 
   // 1. RMSNorm of token t
-  constexpr int kChunks = kGateMaxH / (kGateThreads * 8);
   float xv[kChunks][8];
   float ss = 0.f;
 #pragma unroll
@@ -534,11 +553,10 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   for (int c = 0; c < kChunks; ++c) {
     const int col = (c * kGateThreads + threadIdx.x) * 8;
     if (col < H) {
-      float w[8], y[8];
-      load8(g.norm_w + col, w);
+      float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        y[i] = round_bf16(w[i] * round_bf16(xv[c][i] * rstd));
+        y[i] = round_bf16(nwt[c][i] * round_bf16(xv[c][i] * rstd));
         xn_s[col + i] = y[i];
       }
       if (grp == 0) store8(g.xn + (size_t)t * H + col, y);
@@ -547,18 +565,18 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   __syncthreads();
 
   // 2. router logits of this CTA's experts: warp w takes experts w, w + 8, ...
-  const int per_grp = g.E / g.G;
   for (int j = warp; j < per_grp; j += kGateThreads / 32) {
     const int e = grp * per_grp + j;
     const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
     // the row's vectors (H <= 4096: at most 16 per lane) are all requested
-    // before the dot product
-    constexpr int kVec = kGateMaxH / (32 * 8);
+    // before the dot product (the first row was requested before the wait)
     uint4 wv[kVec];
 #pragma unroll
     for (int c = 0; c < kVec; ++c) {
       const int col = (c * 32 + lane) * 8;
-      wv[c] = col < H ? *reinterpret_cast<const uint4*>(wr + col) : make_uint4(0, 0, 0, 0);
+      wv[c] = j == warp ? wv0[c]
+                        : (col < H ? *reinterpret_cast<const uint4*>(wr + col)
+                                   : make_uint4(0, 0, 0, 0));
     }
     float acc = 0.f;
 #pragma unroll
@@ -611,191 +629,15 @@ __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, M
   if (threadIdx.x == 0) *g.done_cnt = 0;
 }
 
-// Tiled variant (E % 16 == 0): CTA (token group tg of 16, expert group eg of
-// 16) normalises its 16 tokens into shared memory (expert group 0 also stores
-// xn), then thread (t, e) = (tid / 16, tid % 16) computes one router logit
-// from the shared-memory row and the router row, so each router row is read
-// once per token group instead of once per token. The last expert group of a
-// token group (per-group counter) runs its 16 tokens' top-k (a warp per two
-// tokens); the last token group (global counter) runs the routing.
-constexpr int kGateTile = 16;
-
-__global__ void __launch_bounds__(kGateThreads) moe_gate_tiled_kernel(MoeGateArgs g,
-                                                                      MoeAlignArgs a) {
-  extern __shared__ __align__(16) uint8_t gsm[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(gsm);           // [16][H]
-  __shared__ __nv_bfloat16 lg_s[kGateThreads / 32][256];
-  __shared__ int cnt[kMaxLocalExperts];
-  __shared__ int off[kMaxLocalExperts + 1];
-  __shared__ int boff[kMaxLocalExperts + 1];
-  __shared__ int32_t s_ids[kGateMaxEntries];
-  __shared__ float s_w[kGateMaxEntries];
-  __shared__ int s_flag;
-  pdl_wait();
-  pdl_trigger();
-  block_wait(g.wait, 150);
-  const int n_eg = g.E / kGateTile;
-  const int tg = blockIdx.x / n_eg, eg = blockIdx.x % n_eg;
-  const int t0 = tg * kGateTile;
-  const int nt = min(kGateTile, g.T - t0);
-  const int H = g.H;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-  // 1. RMSNorm of the group's tokens: warp w takes tokens 2w, 2w + 1
-  for (int tl = warp; tl < kGateTile; tl += kGateThreads / 32) {
-    __nv_bfloat16* xr = xs + (size_t)tl * H;
-    if (tl >= nt) {  // padding rows: zeros (their logits are never used)
-      for (int col = lane * 8; col < H; col += 256)
-        *reinterpret_cast<uint4*>(xr + col) = make_uint4(0, 0, 0, 0);
-      continue;
-    }
-    const __nv_bfloat16* hr = g.h + (size_t)(t0 + tl) * g.ld_h;
-    constexpr int kV = kGateMaxH / 256;
-    uint4 hv[kV];
-#pragma unroll
-    for (int c = 0; c < kV; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      hv[c] = col < H ? *reinterpret_cast<const uint4*>(hr + col) : make_uint4(0, 0, 0, 0);
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < kV; ++c) {
-      const uint32_t* q = &hv[c].x;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float u0, u1;
-        unpack_bf16x2(q[e], u0, u1);
-        ss += u0 * u0 + u1 * u1;
-      }
-    }
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / (float)H + g.eps);
-#pragma unroll
-    for (int c = 0; c < kV; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col >= H) break;
-      float x[8], w[8], y[8];
-      const uint32_t* q = &hv[c].x;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) unpack_bf16x2(q[e], x[2 * e], x[2 * e + 1]);
-      load8(g.norm_w + col, w);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = w[i] * round_bf16(x[i] * rstd);
-      store8(xr + col, y);
-      if (eg == 0) store8(g.xn + (size_t)(t0 + tl) * H + col, y);
-    }
-  }
-  __syncthreads();
-
-  // 2. logits: warp w takes tokens 2w, 2w + 1 and all 16 experts of the
-  // group; lanes split the hidden dimension (8 elements per lane per 256-wide
-  // chunk), every router vector feeds both tokens, warp sums at the end
-  {
-    const int ta = 2 * warp, tb = 2 * warp + 1;
-    const __nv_bfloat16* xa = xs + (size_t)ta * H;
-    const __nv_bfloat16* xb = xs + (size_t)tb * H;
-    const __nv_bfloat16* wr0 = g.w_router + (size_t)(eg * kGateTile) * H;
-    float acc[2][kGateTile];
-#pragma unroll
-    for (int e = 0; e < kGateTile; ++e) acc[0][e] = acc[1][e] = 0.f;
-    for (int col = lane * 8; col < H; col += 256) {
-      float fa[8], fb[8];
-      load8(xa + col, fa);
-      load8(xb + col, fb);
-      uint4 wv[kGateTile];
-#pragma unroll
-      for (int e = 0; e < kGateTile; ++e)
-        wv[e] = *reinterpret_cast<const uint4*>(wr0 + (size_t)e * H + col);
-#pragma unroll
-      for (int e = 0; e < kGateTile; ++e) {
-        const uint32_t* q = &wv[e].x;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float w0, w1;
-          unpack_bf16x2(q[i], w0, w1);
-          acc[0][e] += w0 * fa[2 * i] + w1 * fa[2 * i + 1];
-          acc[1][e] += w0 * fb[2 * i] + w1 * fb[2 * i + 1];
-        }
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < kGateTile; ++e) {
-      acc[0][e] = warp_sum(acc[0][e]);
-      acc[1][e] = warp_sum(acc[1][e]);
-    }
-    // lane e writes (ta, e), lane 16 + e writes (tb, e)
-    const int e = lane % kGateTile;
-    const int tl = lane < kGateTile ? ta : tb;
-    float v = 0.f;
-#pragma unroll
-    for (int k = 0; k < kGateTile; ++k)
-      if (k == e) v = lane < kGateTile ? acc[0][k] : acc[1][k];
-    if (tl < nt) g.logits[(size_t)(t0 + tl) * g.E + eg * kGateTile + e] = __float2bfloat16_rn(v);
-  }
-
-  // 3. the token group's last CTA: top-k of its tokens
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[tg], 1) == n_eg - 1);
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  for (int tl = warp; tl < nt; tl += kGateThreads / 32) {
-    const int t = t0 + tl;
-    for (int e = lane; e < g.E; e += 32)
-      lg_s[warp][e] = __ushort_as_bfloat16(
-          __ldcg(reinterpret_cast<const unsigned short*>(g.logits) + (size_t)t * g.E + e));
-    __syncwarp();
-    topk_token(lg_s[warp], g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
-               g.weights + (size_t)t * g.top_k);
-    __syncwarp();
-  }
-  if (threadIdx.x == 0) g.tok_cnt[tg] = 0;
-  __threadfence();
-  __syncthreads();
-  const int n_tg = (g.T + kGateTile - 1) / kGateTile;
-  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == n_tg - 1);
-  __syncthreads();
-  if (!s_flag) return;
-
-  // 4. the last token group: routing over all T tokens
-  __threadfence();
-  const int n = g.T * g.top_k;
-  for (int i = threadIdx.x; i < n; i += kGateThreads) {
-    s_ids[i] = __ldcg(g.ids + i);
-    s_w[i] = __ldcg(g.weights + i);
-  }
-  __syncthreads();
-  align_body(s_ids, s_w, a, cnt, off, boff);
-  if (threadIdx.x == 0) *g.done_cnt = 0;
-}
-
 int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
   if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % g.G != 0 ||
       g.top_k > 16 || g.H > kGateMaxH || g.H % 8 != 0 || a.n_local > kMaxLocalExperts ||
       a.block_n <= 0)
     return 1;
-  // per-token CTAs parallelise best for a few tokens; the tiled kernel reads
-  // each router row once per 16 tokens, which wins from a few dozen tokens
-  // (AFD_GATE_TILED_MIN_T moves the switch point for A/B measurements)
-  static const int tiled_min_t = [] {
-    const char* e = std::getenv("AFD_GATE_TILED_MIN_T");
-    return e != nullptr ? std::atoi(e) : 48;
-  }();
-  if (g.E % kGateTile == 0 && g.T >= tiled_min_t) {
-    const int smem = kGateTile * g.H * 2;
-    static int attr = 0;
-    if (smem > attr) {
-      cudaError_t e = cudaFuncSetAttribute(moe_gate_tiled_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kGateTile * kGateMaxH * 2);
-      if (e != cudaSuccess) return (int)e;
-      attr = kGateTile * kGateMaxH * 2;
-    }
-    const int grid = ((g.T + kGateTile - 1) / kGateTile) * (g.E / kGateTile);
-    return (int)launch_k(moe_gate_tiled_kernel, dim3(grid), dim3(kGateThreads), smem, s, g, a);
-  }
-  return (int)launch_k(moe_gate_kernel, dim3(g.T * g.G), dim3(kGateThreads), 0, s, g, a);
+  const dim3 grid(g.T * g.G), block(kGateThreads);
+  if (g.H <= 1024) return (int)launch_k(moe_gate_kernel<4>, grid, block, 0, s, g, a);
+  if (g.H <= 2048) return (int)launch_k(moe_gate_kernel<8>, grid, block, 0, s, g, a);
+  return (int)launch_k(moe_gate_kernel<16>, grid, block, 0, s, g, a);
 }
 
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
