@@ -382,9 +382,18 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
         x = torch.empty(R, H, device=xn.device, dtype=xn.dtype)
         C.moe_gather(xn, ws.row_token, ws.num_rows, x, R)
         row_ids = None
+    # decode sizes: ~one row block per hit expert, I/128 feature tiles each --
+    # a few tiles per SM, so splitting K in two evens out the last wave
+    max_tiles = ws.max_blocks * (I // 128)
+    est_tiles = min(E_loc, T * k) * (I // 128)
+    gu_splits = 2 if (_GU_SPLIT and T <= 64 and est_tiles < 6 * num_sms()
+                      and (H // 64) % 2 == 0) else 1
+    gws = gcnt = None
+    if gu_splits > 1:
+        gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, gu_splits)
     C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
-           0, None, None, True, bn, ws.max_blocks * (I // 128), [], 0, [], 0, None, None, None,
-           1, None, None, row_ids)
+           0, None, None, True, bn, max_tiles * gu_splits, [], 0, [], 0, None, None, None,
+           gu_splits, gws, gcnt, row_ids)
     if out is None and not peers:
         out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
     if _FUSED_COMBINE and T <= _FUSED_COMBINE_MAX_TOKENS:
@@ -454,6 +463,7 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 # AFD_FUSED_GATE=0 / AFD_FUSED_COMBINE=0 select the unfused kernel sequences
 # (A/B measurements)
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
+_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "1") != "0"  # split-K of the decode gate_up GEMM
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "1") != "0"
 
 

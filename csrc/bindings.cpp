@@ -106,8 +106,11 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   a.ws = opt_ptr<float>(ws);
   a.tile_counters = opt_ptr<int>(tile_counters);
   if (k_splits > 1) {
-    const int64_t tiles = ((dense_rows + block_n - 1) / block_n) * f_tiles;
-    TORCH_CHECK(a.ws != nullptr && ws->numel() >= k_splits * tiles * block_n * 128,
+    // dense: exact tile count; grouped: the caller's bound (units_hint / k_splits)
+    const int64_t tiles = a.blocks == nullptr ? ((dense_rows + block_n - 1) / block_n) * f_tiles
+                                              : units_hint / k_splits;
+    TORCH_CHECK(a.ws != nullptr &&
+                    ws->numel() >= k_splits * tiles * block_n * 128 * (swiglu ? 2 : 1),
                 "split-K workspace too small");
     TORCH_CHECK(a.tile_counters != nullptr && tile_counters->numel() >= tiles,
                 "split-K tile counters too small");

@@ -354,11 +354,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int f_base = ft * kBM + q * 32;
       bool emit = true;
       float* wsp = nullptr;
-      if (!SWIGLU && k_splits > 1) {
-        // split-K: store this split's partial tile into its own fp32 slice;
-        // the last split to finish sums the slices in split order, so the
-        // result does not depend on which split finished first
-        const size_t tile_elems = (size_t)BN * kBM;
+      if (k_splits > 1) {
+        // split-K: store this split's partial tile (SwiGLU: gate and up) into
+        // its own fp32 slice; the last split to finish sums the slices in split
+        // order, so the result does not depend on which split finished first
+        const size_t tile_elems = (size_t)BN * kBM * (SWIGLU ? 2 : 1);
         wsp = args.ws + (size_t)un.tile * tile_elems + q * 32 + lane;
         float* own = wsp + (size_t)un.split * tiles * tile_elems;
         for (int c = 0; c < blk.y; c += 16) {
@@ -367,6 +367,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             if (c + j < blk.y) __stcg(own + (c + j) * kBM, acc[j]);
+          if constexpr (SWIGLU) {
+            tmem_ld16(t_row + L::kAccCols + c, acc);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c + j < blk.y) __stcg(own + (size_t)BN * kBM + (c + j) * kBM, acc[j]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -392,35 +398,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c = c0 + 16 * hh;
         if (c >= blk.y) break;
         float acc[16];
+        float up[16];
         if (wsp != nullptr) {
           // last split: sum the partial slices in split order; four slices'
           // 16 values are loaded before any is added, so 64 loads are in
           // flight instead of one dependent load at a time
-          const size_t split_stride = (size_t)tiles * BN * kBM;
+          const size_t split_stride = (size_t)tiles * BN * kBM * (SWIGLU ? 2 : 1);
+          auto reduce = [&](float (&out)[16], const float* src) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-          for (int sp0 = 0; sp0 < k_splits; sp0 += 4) {
-            float v[4][16];
+            for (int j = 0; j < 16; ++j) out[j] = 0.f;
+            for (int sp0 = 0; sp0 < k_splits; sp0 += 4) {
+              float v[4][16];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+              for (int u = 0; u < 4; ++u)
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
-                v[u][j] = (sp0 + u < k_splits && c + j < blk.y)
-                              ? __ldcg(wsp + (sp0 + u) * split_stride + (c + j) * kBM)
-                              : 0.f;
+                for (int j = 0; j < 16; ++j)
+                  v[u][j] = (sp0 + u < k_splits && c + j < blk.y)
+                                ? __ldcg(src + (sp0 + u) * split_stride + (c + j) * kBM)
+                                : 0.f;
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+              for (int u = 0; u < 4; ++u)
 #pragma unroll
-              for (int j = 0; j < 16; ++j) acc[j] += v[u][j];
-          }
+                for (int j = 0; j < 16; ++j) out[j] += v[u][j];
+            }
+          };
+          reduce(acc, wsp);
+          if constexpr (SWIGLU) reduce(up, wsp + (size_t)BN * kBM);
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[j] = a32[16 * hh + j];
+          if constexpr (SWIGLU) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) up[j] = u32[16 * hh + j];
+          }
         }
         if (SWIGLU) {
-          float up[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) up[j] = u32[16 * hh + j];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             // HF rounds gate/up to bf16 before the activation and the product
