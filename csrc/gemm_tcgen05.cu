@@ -595,7 +595,6 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   GemmArgs a = p.args;
   a.block_n = p.block_n;
   if (a.k_splits > 1) {
-    if (p.swiglu || a.blocks != nullptr) return 1006;  // dense, non-SwiGLU only
     if ((p.args.K / kBK) % a.k_splits != 0) return 1007;
     if (a.ws == nullptr || a.tile_counters == nullptr) return 1008;
   }
