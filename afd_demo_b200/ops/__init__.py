@@ -463,7 +463,7 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 # AFD_FUSED_GATE=0 / AFD_FUSED_COMBINE=0 select the unfused kernel sequences
 # (A/B measurements)
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
-_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "1") != "0"  # split-K of the decode gate_up GEMM
+_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"  # split-K of the decode gate_up GEMM (measured slower)
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "1") != "0"
 
 
