@@ -239,3 +239,42 @@ def test_moe_experts_no_local_rows(with_residual):
     out = ops.moe_experts(xn, ids, w, wgu, wd, 0, residual=h if with_residual else None)
     want = h if with_residual else torch.zeros_like(h)
     assert torch.equal(out, want)
+
+
+def test_prefill_attention_long_sequence():
+    """A 2048-token causal prefill (16 key tiles per query tile)."""
+    nq, nkv, D, S, q_len = 32, 4, 128, 2048, 2048
+    kc = _randn(1, nkv, S, D, seed=90)
+    vc = _randn(1, nkv, S, D, seed=91)
+    q = _randn(q_len, nq, D, seed=92)
+    pos = torch.zeros(1, device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, q_len, 0)
+    out = ops.attention(q, kc, vc, 0, q_len, 0, pos)
+    assert _rel(out, ref) < 1e-2
+
+
+def test_gemm_sm_budget_same_result():
+    """Capping the persistent grid changes the schedule, not the result."""
+    x = _randn(200, 2048, seed=93)
+    w = _randn(1024, 2048, scale=0.02, seed=94)
+    full = ops.linear(x, w)
+    with ops.sm_budget(40):
+        capped = ops.linear(x, w)
+    assert torch.equal(full, capped)
+
+
+@pytest.mark.parametrize("T", [1, 16, 100])
+def test_moe_gate_alone(T):
+    """The fused gate's ids / weights equal the router top-k of the fp32
+    reference (as expert -> weight maps; near-ties may swap order)."""
+    H, E = 2048, 128
+    h = _randn(T, H, seed=95)
+    pw = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    wr = _randn(E, H, scale=0.02, seed=96)
+    xn_r, ids_r, w_r = torch_ref.router_topk(h, pw, wr, 8, 1e-6)
+    xn, ws = ops.moe_gate(h, pw, wr, 8, 1e-6)
+    assert _rel(xn, xn_r) < 1e-2
+    dense = torch.zeros(T, E, device=DEV).scatter_(1, ws.ids.long(), ws.weights)
+    dense_r = torch.zeros(T, E, device=DEV).scatter_(1, ids_r.long(), w_r)
+    assert (dense - dense_r).abs().max() < 2e-2
+    assert int(ws.num_rows) == T * 8
