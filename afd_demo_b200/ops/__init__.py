@@ -407,6 +407,21 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
            None, ws.row_weight, False, bn, ws.max_blocks * (H // 128), [], 0, [], 0, None, None,
            None, 1, None, None, None)
+    if peers and _SPLIT_F2A:
+        # prefill sizes: combine locally, then one bulk peer copy per attention
+        # rank's segment (the combine kernel's scattered NVLink stores run at
+        # about half the link bandwidth; the copy kernel reaches ~0.7 of it)
+        local = out if out is not None else torch.empty(T, H, device=xn.device, dtype=xn.dtype)
+        C.moe_combine(ws.y, ws.inv, T, k, residual, local, [], [], 0, [], 0, None, None)
+        row_bytes = H * local.element_size()
+        for i, (dst, flag) in enumerate(zip(peers, flags)):
+            lo, hi = int(seg_offsets[i]), int(seg_offsets[i + 1])
+            if hi <= lo:
+                continue
+            grid = max(1, min(4 * num_sms(), (hi - lo) * row_bytes // (16 * 512)))
+            C.peer_copy(local[lo:hi], [int(dst) + int(peer_row_offset) * row_bytes], [int(flag)],
+                        int(signal_value), done_counter, epoch, grid)
+        return out
     C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
                   int(peer_row_offset), list(flags), int(signal_value), done_counter, epoch)
     return out
@@ -463,6 +478,7 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 # AFD_FUSED_GATE=0 / AFD_FUSED_COMBINE=0 select the unfused kernel sequences
 # (A/B measurements)
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
+_SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine, then bulk copy
 _GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"  # split-K of the decode gate_up GEMM (measured slower)
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "1") != "0"
 

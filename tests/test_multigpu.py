@@ -39,11 +39,13 @@ def _run(rank, world, port, impl, out_dir):
     ctx.initialize(DistributedConfig(world_size=world, rank=rank, local_rank=rank,
                                      backend="nccl", master_addr="127.0.0.1",
                                      master_port=str(port), timeout_s=120))
-    m = DisaggregatedQwenModel.from_pretrained("mini", device=f"cuda:{rank}", max_seq_len=64,
+    m = DisaggregatedQwenModel.from_pretrained("mini", device=f"cuda:{rank}", max_seq_len=96,
                                                max_batch_size=8, comm_impl=impl,
                                                timeout_ms=20000)
     res = {}
     ids = _ids()
+    # 320 tokens per micro-batch: the prefill-sized F2A path (combine, then bulk copy)
+    res["prefill_long"] = m.run_forward(_ids(S=80), "dbo", 2, True, reset_cache=True)
     res["prefill_logits"] = m.run_forward(ids, "dbo", 2, True, reset_cache=True)
     for name, kw in {"serial": dict(use_decode_dbo=False),
                      "xl": dict(use_decode_dbo=True, decode_use_crosslayer=True,
@@ -69,10 +71,11 @@ def _single(out_dir):
     from afd_demo_b200.utils import device as devmod
 
     devmod.init_backend("cuda")
-    m = DisaggregatedQwenModel.from_pretrained("mini", device="cuda:0", max_seq_len=64,
+    m = DisaggregatedQwenModel.from_pretrained("mini", device="cuda:0", max_seq_len=96,
                                                max_batch_size=8)
     ids = _ids()
-    res = {"prefill_logits": m.run_forward(ids, "dbo", 2, True, reset_cache=True),
+    res = {"prefill_long": m.run_forward(_ids(S=80), "dbo", 2, True, reset_cache=True),
+           "prefill_logits": m.run_forward(ids, "dbo", 2, True, reset_cache=True),
            "serial": m.generate(ids, max_new_tokens=6, do_sample=False, use_decode_dbo=False)}
     torch.save({k: v.cpu() for k, v in res.items()}, os.path.join(out_dir, "single.pt"))
 
@@ -107,6 +110,9 @@ def test_multi_gpu_matches_single(single, impl, world):
     ref = want["prefill_logits"].float()
     rel = float((logits - ref).norm() / ref.norm())
     assert rel < 2e-2, rel
+    long = torch.cat([g["prefill_long"] for g in got]).float()
+    ref_long = want["prefill_long"].float()
+    assert float((long - ref_long).norm() / ref_long.norm()) < 2e-2
     if world == 2:  # no expert split: bitwise the single-GPU computation
         assert torch.equal(torch.cat([g["serial"] for g in got]), want["serial"])
     for g in got:
