@@ -20,6 +20,7 @@ the waits:
 
 from __future__ import annotations
 
+import os
 import time
 from typing import Dict, List, Optional
 
@@ -28,6 +29,10 @@ import torch
 from .. import ops
 from ..utils.timing import EventType, TimingTracker
 from .micro_batch import ForwardPlan
+
+
+# AFD_DEFER_WAITS=0: a stand-alone wait kernel per receive (A/B measurements)
+_DEFER_WAITS = os.environ.get("AFD_DEFER_WAITS", "1") != "0"
 
 
 class _Null:
@@ -84,7 +89,7 @@ class PipelineEngine:
         # fold each receive's wait into the consuming kernel, except when
         # timing: then the receive wait is its own (measured) span
         if tr.fused:
-            tr.defer_waits = not (ta or tf)
+            tr.defer_waits = _DEFER_WAITS and not (ta or tf)
         if has_ffn:
             m_.ffn_worker.tracker = tf
 
