@@ -480,7 +480,7 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
 _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine, then bulk copy
 _GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"  # split-K of the decode gate_up GEMM (measured slower)
-_FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "1") != "0"
+_FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slower (esp. with peers)
 
 
 def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
