@@ -213,32 +213,38 @@ __global__ void qk_norm_rope_cache_kernel(QKRopeArgs a) {
 __device__ __forceinline__ void topk_token(const __nv_bfloat16* logits, int E, int top_k,
                                            int renorm, int lane, int32_t* ids_out,
                                            float* w_out) {
+  // Register-resident: the loops run over the compile-time bound with a guard,
+  // and lane k keeps the k-th pick (top_k <= 16 < 32), so nothing is indexed
+  // at run time and nothing goes to local memory.
   constexpr int kMaxPer = 8;  // E <= 256
-  const int per = (E + 31) / 32;
   float v[kMaxPer];
   float m = -INFINITY;
-  for (int i = 0; i < per; ++i) {
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
     const int e = lane + 32 * i;
     v[i] = e < E ? bf16_to_f(logits[e]) : -INFINITY;
     m = fmaxf(m, v[i]);
   }
   m = warp_max(m);
   float s = 0.f;
-  for (int i = 0; i < per; ++i) {
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
     const int e = lane + 32 * i;
     v[i] = e < E ? __expf(v[i] - m) : 0.f;
     s += v[i];
   }
   s = warp_sum(s);
   const float inv = 1.f / s;
-  for (int i = 0; i < per; ++i) v[i] *= inv;
-  float sel_w[16];
-  int sel_e[16];
-  float wsum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) v[i] *= inv;
+  float my_w = 0.f;
+  int my_e = 0;
+  float wsum = 0.f;  // the same on every lane: the butterfly leaves every lane the same pick
   for (int k = 0; k < top_k; ++k) {
     float best = -1.f;
     int be = 0x7fffffff;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
       const int e = lane + 32 * i;
       if (e < E && (v[i] > best || (v[i] == best && e < be))) { best = v[i]; be = e; }
     }
@@ -248,18 +254,15 @@ __device__ __forceinline__ void topk_token(const __nv_bfloat16* logits, int E, i
       const int oe = __shfl_xor_sync(0xffffffff, be, o);
       if (ob > best || (ob == best && oe < be)) { best = ob; be = oe; }
     }
-    sel_w[k] = best;
-    sel_e[k] = be;
+    if (lane == k) { my_w = best; my_e = be; }
     wsum += best;
-    for (int i = 0; i < per; ++i)
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
       if (lane + 32 * i == be) v[i] = -2.f;  // remove from further rounds
   }
-  if (lane == 0) {
-    const float r = renorm ? 1.f / wsum : 1.f;
-    for (int k = 0; k < top_k; ++k) {
-      ids_out[k] = sel_e[k];
-      w_out[k] = sel_w[k] * r;
-    }
+  if (lane < top_k) {
+    ids_out[lane] = my_e;
+    w_out[lane] = my_w * (renorm ? 1.f / wsum : 1.f);
   }
 }
 
