@@ -475,8 +475,8 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
 _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate kernel
 
 
-# AFD_FUSED_GATE=0 / AFD_FUSED_COMBINE=0 select the unfused kernel sequences
-# (A/B measurements)
+# Switches for A/B measurements: AFD_FUSED_GATE=0 selects the unfused gate kernel
+# sequence, AFD_FUSED_COMBINE=1 the combine inside the down GEMM's epilogue.
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
 _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine, then bulk copy
 _GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"  # split-K of the decode gate_up GEMM (measured slower)

@@ -87,6 +87,23 @@ def test_moe_ffn_block(T, E_loc, start):
     assert _rel(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("T,E_loc,start", [(1, 128, 0), (16, 128, 0), (200, 128, 0), (24, 32, 32)])
+def test_moe_ffn_block_fused_combine(T, E_loc, start, monkeypatch):
+    """The A/B variant that runs the top-k combine inside the down GEMM's
+    epilogue (off by default) against the same fp32 statement."""
+    monkeypatch.setattr(ops, "_FUSED_COMBINE", True)
+    H, I, E = 2048, 768, 128
+    h = _randn(T, H, seed=17)
+    pw = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    wr = _randn(E, H, scale=0.02, seed=18)
+    wgu = _randn(E_loc, 2 * I, H, scale=0.02, seed=19)
+    wd = _randn(E_loc, H, I, scale=0.02, seed=20)
+    ref = torch_ref.ffn_layer(h, pw, wr, wgu, wd, 8, 1e-6, expert_start=start,
+                              add_residual=(start == 0))
+    out = ops.moe_ffn(h, pw, wr, wgu, wd, 8, 1e-6, True, start, add_residual=(start == 0))
+    assert _rel(out, ref) < 2e-2
+
+
 def test_moe_residual_and_ep_partials_sum():
     T, H, I, E = 48, 2048, 768, 128
     xn = _randn(T, H, seed=9)
