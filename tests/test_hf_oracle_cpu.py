@@ -1,0 +1,56 @@
+"""Independent oracle: HF transformers' own Qwen3-MoE, the model code the
+reference's workers call (src/model/attention_worker.py:127,
+src/model/ffn_worker.py:98-107), loads a checkpoint that this framework's writer
+produced in the Qwen3-MoE safetensors layout (per-expert
+`mlp.experts.{e}.{gate,up,down}_proj.weight`, sharded index). Its logits and
+greedy tokens must match this framework's CPU path in every schedule."""
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from afd_demo_b200.config import tiny_qwen3_moe  # noqa: E402
+from afd_demo_b200.models import DisaggregatedQwenModel  # noqa: E402
+from afd_demo_b200.models.weights import write_random_checkpoint  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def models(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("ckpt"))
+    cfg = tiny_qwen3_moe()
+    write_random_checkpoint(path, cfg, seed=0, dtype=torch.float32)
+    hf = transformers.AutoModelForCausalLM.from_pretrained(path, dtype=torch.float32)
+    hf.eval()
+    ours = DisaggregatedQwenModel.from_pretrained(path, device="cpu", dtype=torch.float32,
+                                                  max_seq_len=64, max_batch_size=4)
+    ids = torch.randint(0, cfg.vocab_size, (4, 16), generator=torch.Generator().manual_seed(0))
+    return hf, ours, ids
+
+
+def test_hf_reads_the_checkpoint_layout(models):
+    hf, ours, _ = models
+    assert type(hf).__name__ == "Qwen3MoeForCausalLM"
+    assert hf.config.num_experts == ours.config.num_experts
+    assert hf.config.norm_topk_prob is True
+
+
+@pytest.mark.parametrize("mode,nmb", [("serial", 1), ("dbo", 2)])
+def test_last_position_logits_match_hf(models, mode, nmb):
+    hf, ours, ids = models
+    with torch.no_grad():
+        ref = hf(ids).logits[:, -1].float()
+    out = ours.run_forward(ids, mode, nmb, reset_cache=True).float()
+    assert out.shape == ref.shape
+    assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("dbo,crosslayer", [(False, False), (True, False), (True, True)])
+def test_greedy_tokens_match_hf(models, dbo, crosslayer):
+    hf, ours, ids = models
+    with torch.no_grad():
+        ref = hf.generate(ids, max_new_tokens=8, do_sample=False, pad_token_id=0,
+                          eos_token_id=None)
+    out = ours.generate(ids, max_new_tokens=8, do_sample=False, use_decode_dbo=dbo,
+                        decode_use_crosslayer=crosslayer)
+    assert torch.equal(out[:, ids.shape[1]:].cpu(), ref[:, ids.shape[1]:])
