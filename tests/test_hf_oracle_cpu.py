@@ -54,3 +54,18 @@ def test_greedy_tokens_match_hf(models, dbo, crosslayer):
     out = ours.generate(ids, max_new_tokens=8, do_sample=False, use_decode_dbo=dbo,
                         decode_use_crosslayer=crosslayer)
     assert torch.equal(out[:, ids.shape[1]:].cpu(), ref[:, ids.shape[1]:])
+
+
+def test_reads_a_checkpoint_saved_by_transformers(models, tmp_path):
+    """The other direction: transformers 5 saves a single `model.safetensors`
+    and names the expert count `num_local_experts`; the loader reads both."""
+    hf, _, ids = models
+    hf.save_pretrained(str(tmp_path))
+    again = DisaggregatedQwenModel.from_pretrained(str(tmp_path), device="cpu",
+                                                   dtype=torch.float32, max_seq_len=64,
+                                                   max_batch_size=4)
+    assert again.config.num_experts == hf.config.num_experts
+    with torch.no_grad():
+        ref = hf(ids).logits[:, -1].float()
+    out = again.run_forward(ids, "serial", 1, reset_cache=True).float()
+    assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())

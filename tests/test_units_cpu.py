@@ -122,6 +122,16 @@ def test_config_hf_roundtrip(tmp_path):
     assert back.to_hf_dict() == cfg.to_hf_dict()
 
 
+def test_config_reads_transformers5_names():
+    d = PRESETS["qwen3-30b-a3b"]().to_hf_dict()
+    d.pop("num_experts")
+    d.pop("rope_theta", None)
+    d["num_local_experts"] = 64
+    d["rope_parameters"] = {"rope_type": "default", "rope_theta": 5e5}
+    cfg = ModelConfig.from_dict(d)
+    assert cfg.num_experts == 64 and cfg.rope_theta == 5e5
+
+
 def test_sparse_layer_rule():
     cfg = tiny_qwen3_moe()
     cfg.mlp_only_layers = [1]
