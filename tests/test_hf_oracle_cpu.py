@@ -69,3 +69,20 @@ def test_reads_a_checkpoint_saved_by_transformers(models, tmp_path):
         ref = hf(ids).logits[:, -1].float()
     out = again.run_forward(ids, "serial", 1, reset_cache=True).float()
     assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_dense_mlp_layers_match_hf(tmp_path):
+    """`mlp_only_layers` layers are a dense SwiGLU MLP (HF `Qwen3MoeMLP`)."""
+    cfg = tiny_qwen3_moe()
+    cfg.mlp_only_layers = [1]
+    write_random_checkpoint(str(tmp_path), cfg, seed=1, dtype=torch.float32)
+    hf = transformers.AutoModelForCausalLM.from_pretrained(str(tmp_path), dtype=torch.float32)
+    assert type(hf.model.layers[1].mlp).__name__ == "Qwen3MoeMLP"
+    ours = DisaggregatedQwenModel.from_pretrained(str(tmp_path), device="cpu",
+                                                  dtype=torch.float32, max_seq_len=64,
+                                                  max_batch_size=2)
+    ids = torch.randint(0, cfg.vocab_size, (2, 16), generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        ref = hf(ids).logits[:, -1].float()
+    out = ours.run_forward(ids, "dbo", 2, reset_cache=True).float()
+    assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
