@@ -43,6 +43,9 @@ class AttentionWorker:
         self.cache = KVCache(cfg.num_hidden_layers, max_batch, cfg.num_key_value_heads, max_seq,
                              cfg.head_dim, self.device, dtype)
         self.tracker = None  # optional TimingTracker for sub-stage events
+        # (lo, hi) visible key range per cache row for the current prefill
+        # (padding masks), set by the model around one forward; None = causal only
+        self.key_range = None
 
     # ------------------------------------------------------------------
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -82,7 +85,8 @@ class AttentionWorker:
                                        self.cache.pos_dev, q_len, batch_offset,
                                        cfg.num_attention_heads, cfg.num_key_value_heads,
                                        cfg.rms_norm_eps)
-            o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev)
+            o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev,
+                              self.key_range)
         if sink is not None:
             return ops.linear(o, lw.w_o, residual=x, out=out, **sink.gemm_kwargs())
         return ops.linear(o, lw.w_o, residual=x, out=out)

@@ -33,7 +33,7 @@ from ..parallel.dist import DistributedContext, get_distributed_context
 from ..parallel import faults
 from ..parallel.engine import PipelineEngine
 from ..parallel.health import AFDPeerFailure
-from ..parallel.micro_batch import ForwardPlan, additive_causal_mask, make_plan
+from ..parallel.micro_batch import ForwardPlan, additive_causal_mask, key_ranges_from_mask, make_plan
 from ..parallel.transport import LocalTransport, NcclTransport, PeerTransport, Transport
 from ..utils import device as devmod
 from ..utils.sampling import sample_next_token
@@ -191,13 +191,28 @@ class DisaggregatedQwenModel:
 
     def run_forward(self, input_ids: torch.Tensor, mode: str = "serial", num_micro_batches: int = 1,
                     crosslayer: bool = False, trackers=None, last_only: bool = True,
-                    reset_cache: bool = False) -> Optional[torch.Tensor]:
+                    reset_cache: bool = False, attention_mask: Optional[torch.Tensor] = None
+                    ) -> Optional[torch.Tensor]:
+        """One forward of every layer. `attention_mask` [B, S] (1 = token, 0 =
+        padding; prefill only) hides padded keys as the reference's prefill
+        schedulers do; positions stay 0..S-1."""
         B, S = input_ids.shape
         plan = self.plan(B, S, num_micro_batches)
         if reset_cache and self.kv_cache is not None:
             self.kv_cache.reset(len(self.local_batch(B)))
-        return self.engine.forward(plan, self._local_ids(input_ids), mode=mode,
-                                   crosslayer=crosslayer, trackers=trackers, last_only=last_only)
+        aw = self.attention_worker
+        if attention_mask is not None and aw is not None:
+            if S == 1:
+                raise ValueError("attention_mask applies to prefill (seq_len > 1) only")
+            r = self.local_batch(B)
+            aw.key_range = key_ranges_from_mask(attention_mask[r.start:r.stop].to(self.device))
+        try:
+            return self.engine.forward(plan, self._local_ids(input_ids), mode=mode,
+                                       crosslayer=crosslayer, trackers=trackers,
+                                       last_only=last_only)
+        finally:
+            if aw is not None:
+                aw.key_range = None
 
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
@@ -205,7 +220,8 @@ class DisaggregatedQwenModel:
         """Full-sequence serial forward (validation path); logits for every
         position [B_local, S, V] on attention ranks."""
         B, S = input_ids.shape
-        out = self.run_forward(input_ids, "serial", 1, last_only=False, reset_cache=True)
+        out = self.run_forward(input_ids, "serial", 1, last_only=False, reset_cache=True,
+                               attention_mask=attention_mask)
         if out is None:
             return None
         return out.view(-1, S, out.shape[-1])
@@ -217,7 +233,8 @@ class DisaggregatedQwenModel:
         """Prefill (resets and fills the KV cache); last-position logits
         [B_local, V]. The reference's generate always prefills serially and
         unsplit; `mode="dbo"` runs the micro-batched overlap instead."""
-        return self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True)
+        return self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True,
+                                attention_mask=attention_mask)
 
     @torch.no_grad()
     def forward_decode(self, input_ids: torch.Tensor) -> Optional[torch.Tensor]:

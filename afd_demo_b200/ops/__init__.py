@@ -290,13 +290,19 @@ def decode_attention_fused(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torc
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, batch_offset: int,
-              q_len: int, start_pos: int, start_pos_dev: Optional[torch.Tensor]) -> torch.Tensor:
-    """Causal GQA attention over the cache; returns [T, nq * D]."""
+              q_len: int, start_pos: int, start_pos_dev: Optional[torch.Tensor],
+              key_range: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+    """Causal GQA attention over the cache; returns [T, nq * D]. `key_range`
+    (prefill only) = (lo, hi) int32 tensors indexed by cache row: keys outside
+    [lo, hi) are hidden (padding masks)."""
     if not _cuda(q):
-        return torch_ref.attention(q, k_cache, v_cache, batch_offset, q_len, start_pos)
+        return torch_ref.attention(q, k_cache, v_cache, batch_offset, q_len, start_pos,
+                                   key_range)
     T, nq, D = q.shape
     out = torch.empty(T, nq, D, device=q.device, dtype=q.dtype)
     if q_len == 1:
+        if key_range is not None:
+            raise ValueError("padding key ranges apply to prefill (q_len > 1) only")
         nkv = k_cache.shape[1]
         tiles = (start_pos + 1 + 63) // 64
         nsplit = max(1, min(tiles, (2 * num_sms() + T * nkv - 1) // max(1, T * nkv)))
@@ -307,7 +313,9 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, bat
         ext().decode_attention(q, k_cache, v_cache, out, start_pos_dev, batch_offset, nsplit,
                                o_part, ml_part)
     else:
-        ext().prefill_attention(q, k_cache, v_cache, out, start_pos_dev, q_len, batch_offset)
+        lo, hi = key_range if key_range is not None else (None, None)
+        ext().prefill_attention(q, k_cache, v_cache, out, start_pos_dev, q_len, batch_offset,
+                                lo, hi)
     return out.view(T, nq * D)
 
 

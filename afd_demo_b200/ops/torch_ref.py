@@ -101,10 +101,13 @@ def qk_norm_rope_cache(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torc
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-              batch_offset: int, q_len: int, start_pos: int) -> torch.Tensor:
+              batch_offset: int, q_len: int, start_pos: int,
+              key_range: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
     """Causal GQA attention of q [B*q_len, nq, D] against cache rows
     [batch_offset, batch_offset+B) and positions [0, start_pos+q_len).
     Query i of a sequence sits at position start_pos+i and sees keys <= it.
+    `key_range` = (lo, hi), int tensors indexed by cache row: only keys in
+    [lo, hi) are visible (padding); a query that sees no key outputs zeros.
     Returns [B*q_len, nq*D]."""
     T, nq, D = q.shape
     B = T // q_len
@@ -119,9 +122,14 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     s = torch.matmul(qf, k.transpose(-1, -2)) / math.sqrt(D)
     qpos = start_pos + torch.arange(q_len, device=q.device)
     kpos = torch.arange(kv_len, device=q.device)
-    mask = kpos[None, :] > qpos[:, None]
+    mask = (kpos[None, :] > qpos[:, None])[None, None]  # [1, 1, q_len, kv_len]
+    if key_range is not None:
+        lo = key_range[0][batch_offset:batch_offset + B].to(q.device).long()
+        hi = key_range[1][batch_offset:batch_offset + B].to(q.device).long()
+        out_of_range = (kpos[None, :] < lo[:, None]) | (kpos[None, :] >= hi[:, None])
+        mask = mask | out_of_range[:, None, None, :]
     s = s.masked_fill(mask, float("-inf"))
-    p = torch.softmax(s, dim=-1)
+    p = torch.softmax(s, dim=-1).nan_to_num(0.0)  # rows with no visible key -> 0
     o = torch.matmul(p, v)  # [B, nq, q_len, D]
     return o.transpose(1, 2).reshape(T, nq * D).to(q.dtype)
 

@@ -189,3 +189,28 @@ def make_plan(topology: Topology, global_batch: int, num_micro_batches: int, q_l
         offs = [sum(seg[:a]) for a in range(n_attn)]
         ffn_slots.append(FFNSlot(m, seg, offs))
     return ForwardPlan(topology, global_batch, q_len, num_mb, batches, attn_slots, ffn_slots)
+
+
+def key_ranges_from_mask(attention_mask: Optional[torch.Tensor]
+                         ) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+    """Per-sequence visible key range [lo, hi) from a [B, S] 0/1 padding mask,
+    as the prefill schedulers combine it with the causal mask (reference
+    src/pipeline/async_scheduler.py:177-198, src/pipeline/scheduler.py:169-199).
+    Each row must be one run of ones (left or right padding); an all-ones mask
+    gives None (nothing to hide). Returns int32 tensors on the mask's device."""
+    if attention_mask is None:
+        return None
+    m = attention_mask.to(torch.bool)
+    if bool(m.all()):
+        return None
+    B, S = m.shape
+    pos = torch.arange(S, device=m.device)
+    n = m.sum(1)
+    if bool((n == 0).any()):
+        raise ValueError("attention_mask has a row with no token")
+    lo = torch.where(m, pos, S).min(1).values
+    hi = torch.where(m, pos + 1, 0).max(1).values
+    if bool(((hi - lo) != n).any()):
+        raise ValueError("attention_mask rows must be one contiguous run of ones "
+                         "(left or right padding)")
+    return lo.to(torch.int32), hi.to(torch.int32)

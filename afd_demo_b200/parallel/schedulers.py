@@ -107,7 +107,7 @@ class SimplePipelineScheduler:
     @torch.no_grad()
     def run(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None):
         out = self.model.run_forward(input_ids, "serial", self.num_micro_batches,
-                                     reset_cache=True)
+                                     reset_cache=True, attention_mask=attention_mask)
         if self.model.transport is not None and devmod.is_cuda():
             self.model.transport.check()
         return out
@@ -137,7 +137,7 @@ class AsyncPipelineScheduler:
         nmb = min(self.num_micro_batches, input_ids.shape[0])
         tr = _trackers(m, self.enable_timing, nmb, self.timing_mode, self.comm_timing_mode)
         out = m.run_forward(input_ids, "dbo", self.num_micro_batches, self.crosslayer,
-                            trackers=tr, reset_cache=True)
+                            trackers=tr, reset_cache=True, attention_mask=attention_mask)
         if self.enable_timing:
             devmod.synchronize()
         self._timing_data = _finish(tr, m.ctx)

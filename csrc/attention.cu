@@ -262,6 +262,9 @@ __global__ void __launch_bounds__(128) prefill_attention_kernel(PrefillAttnArgs 
   const int qpos0 = start + q0 + qr0;
   const int qpos1 = qpos0 + 8;
   const int kv_end = start + q0 + nq_rows;  // exclusive
+  // visible key range (padding): [key_lo, key_hi) of this cache row
+  const int key_lo = a.key_lo != nullptr ? a.key_lo[cb] : 0;
+  const int key_hi = a.key_hi != nullptr ? a.key_hi[cb] : kv_end;
   const __nv_bfloat16* kbase = a.k_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
   const __nv_bfloat16* vbase = a.v_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
 
@@ -305,8 +308,9 @@ __global__ void __launch_bounds__(128) prefill_attention_kernel(PrefillAttnArgs 
       for (int e = 0; e < 2; ++e) {
         const int kp = kc + e;
         float v0 = s[nt][e] * sl2, v1 = s[nt][2 + e] * sl2;
-        if (kp > qpos0 || kp >= kv_end) v0 = -INFINITY;
-        if (kp > qpos1 || kp >= kv_end) v1 = -INFINITY;
+        const bool hidden = kp >= kv_end || kp < key_lo || kp >= key_hi;
+        if (kp > qpos0 || hidden) v0 = -INFINITY;
+        if (kp > qpos1 || hidden) v1 = -INFINITY;
         s[nt][e] = v0;
         s[nt][2 + e] = v1;
         mx0 = fmaxf(mx0, v0);

@@ -349,6 +349,7 @@ static int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* 
 }
 
 int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s) {
+  if (a.key_lo != nullptr || a.key_hi != nullptr) return 1;  // padding masks: mma.sync kernel
   if (a.D != kTcD || a.q_len <= 0 || B <= 0 || a.nq % a.nkv != 0) return 1;
   TcMaps mp;
   {  // q [B, q_len, nq, D]

@@ -323,7 +323,8 @@ void decode_attention_fused(const at::Tensor& qkv, const at::Tensor& q_norm,
 
 void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                        at::Tensor& out, const at::Tensor& start_pos, int64_t q_len,
-                       int64_t batch_offset) {
+                       int64_t batch_offset, const c10::optional<at::Tensor>& key_lo,
+                       const c10::optional<at::Tensor>& key_hi) {
   afd::PrefillAttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);
@@ -337,13 +338,23 @@ void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at:
   a.D = (int)q.size(2);
   a.s_max = (int)k_cache.size(2);
   const int B = (int)(q.size(0) / q_len);
-  // tcgen05 kernel for head_dim 128; AFD_PREFILL_ATTN=mma selects the
-  // mma.sync kernel (A/B measurements)
+  const bool masked = key_lo.has_value() && key_hi.has_value();
+  if (masked) {
+    TORCH_CHECK(key_lo->scalar_type() == at::kInt && key_hi->scalar_type() == at::kInt &&
+                    key_lo->is_cuda() && key_hi->is_cuda() && key_lo->is_contiguous() &&
+                    key_hi->is_contiguous() && key_lo->numel() >= batch_offset + B &&
+                    key_hi->numel() >= batch_offset + B,
+                "key_lo / key_hi: contiguous int32 CUDA tensors with a row per cache row");
+    a.key_lo = key_lo->data_ptr<int>();
+    a.key_hi = key_hi->data_ptr<int>();
+  }
+  // tcgen05 kernel for head_dim 128 without a padding mask; AFD_PREFILL_ATTN=mma
+  // selects the mma.sync kernel (A/B measurements), which also takes key ranges
   static const bool use_mma = [] {
     const char* e = std::getenv("AFD_PREFILL_ATTN");
     return e != nullptr && std::string(e) == "mma";
   }();
-  if (a.D == 128 && !use_mma)
+  if (a.D == 128 && !use_mma && !masked)
     check_rc(afd::launch_prefill_attention_tc(a, B, cur_stream()), "prefill_attention_tc");
   else
     check_rc(afd::launch_prefill_attention(a, B, cur_stream()), "prefill_attention");

@@ -86,6 +86,10 @@ struct PrefillAttnArgs {
   __nv_bfloat16* out;         // [B * q_len, nq, D]
   const int* start_pos;
   int q_len, batch_offset, nq, nkv, D, s_max;
+  // optional per-cache-row visible key range [key_lo, key_hi) (padding masks;
+  // only the mma.sync kernel reads them)
+  const int* key_lo = nullptr;
+  const int* key_hi = nullptr;
 };
 
 struct RouterArgs {

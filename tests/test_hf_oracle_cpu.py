@@ -86,3 +86,30 @@ def test_dense_mlp_layers_match_hf(tmp_path):
         ref = hf(ids).logits[:, -1].float()
     out = ours.run_forward(ids, "dbo", 2, reset_cache=True).float()
     assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("side", ["right", "left"])
+def test_padding_mask_matches_hf(models, side):
+    """Prefill with a padding mask (the reference's `--prefill-seq-len`
+    max_length padding): padded keys are hidden, positions stay 0..S-1, as
+    HF computes for `model(ids, attention_mask=mask)`."""
+    hf, ours, ids = models
+    B, S = ids.shape
+    lens = torch.tensor([S, S - 3, S - 7, 5])
+    mask = torch.zeros(B, S, dtype=torch.long)
+    for b in range(B):
+        if side == "right":
+            mask[b, :lens[b]] = 1
+        else:
+            mask[b, S - lens[b]:] = 1
+    with torch.no_grad():
+        ref = hf(ids, attention_mask=mask).logits.float()
+    full = ours.forward(ids, attention_mask=mask).float()
+    for b in range(B):
+        # rows whose query sees at least one key (left padding: the real tokens)
+        rows = slice(0, S) if side == "right" else slice(S - int(lens[b]), S)
+        d = (full[b, rows] - ref[b, rows]).abs().max().item()
+        assert d < 1e-3 * max(1.0, ref[b, rows].abs().max().item()), (b, d)
+    for mode, nmb in (("serial", 1), ("dbo", 2)):
+        last = ours.run_forward(ids, mode, nmb, reset_cache=True, attention_mask=mask).float()
+        assert (last - ref[:, -1]).abs().max().item() < 1e-3 * max(1.0, ref[:, -1].abs().max().item())

@@ -270,6 +270,29 @@ def test_prefill_attention_long_sequence():
     assert _rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("D,q_len,start,off", [(128, 100, 0, 0), (128, 130, 0, 1), (64, 77, 0, 0),
+                                             (128, 40, 24, 0)])
+def test_prefill_attention_padding_mask(D, q_len, start, off):
+    """Key ranges (padding masks): rows fully visible, right-padded,
+    left-padded, and a left-padded row whose first queries see no key
+    (output zeros, as the fp32 statement defines)."""
+    B, nkv, S = 4, 2, 256
+    nq = 8
+    kc = _randn(B + off, nkv, S, D, seed=95)
+    vc = _randn(B + off, nkv, S, D, seed=96)
+    q = _randn(B * q_len, nq, D, seed=97)
+    end = start + q_len
+    lo = torch.tensor([0] * off + [0, 0, end // 2, 3], dtype=torch.int32, device=DEV)
+    hi = torch.tensor([0] * off + [end, end - 9, end, end - 1], dtype=torch.int32, device=DEV)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), off, q_len, start, (lo, hi))
+    out = ops.attention(q, kc, vc, off, q_len, start, pos, (lo, hi))
+    assert _rel(out, ref) < 1e-2
+    # rows with no visible key are exactly zero
+    o = out.view(B, q_len, nq * D)
+    assert torch.all(o[2, : max(0, end // 2 - start)] == 0)
+
+
 def test_gemm_sm_budget_same_result():
     """Capping the persistent grid changes the schedule, not the result."""
     x = _randn(200, 2048, seed=93)

@@ -132,6 +132,19 @@ def test_config_reads_transformers5_names():
     assert cfg.num_experts == 64 and cfg.rope_theta == 5e5
 
 
+def test_key_ranges_from_mask():
+    from afd_demo_b200.parallel.micro_batch import key_ranges_from_mask
+    assert key_ranges_from_mask(None) is None
+    assert key_ranges_from_mask(torch.ones(3, 5, dtype=torch.long)) is None
+    m = torch.tensor([[1, 1, 1, 0, 0], [0, 0, 1, 1, 1], [1, 1, 1, 1, 1]])
+    lo, hi = key_ranges_from_mask(m)
+    assert lo.tolist() == [0, 2, 0] and hi.tolist() == [3, 5, 5] and lo.dtype == torch.int32
+    with pytest.raises(ValueError):
+        key_ranges_from_mask(torch.tensor([[1, 0, 1, 1]]))
+    with pytest.raises(ValueError):
+        key_ranges_from_mask(torch.tensor([[0, 0, 0], [1, 1, 1]]))
+
+
 def test_sparse_layer_rule():
     cfg = tiny_qwen3_moe()
     cfg.mlp_only_layers = [1]
