@@ -37,6 +37,15 @@ def _ids():
     return torch.randint(0, 1024, (4, 24), generator=torch.Generator().manual_seed(3))
 
 
+def _mask():
+    # right, left and no padding across the batch (each attention rank gets a slice)
+    m = torch.ones(4, 24, dtype=torch.long)
+    m[1, 20:] = 0
+    m[2, :6] = 0
+    m[3, 15:] = 0
+    return m
+
+
 def _worker(rank, world, port, ckpt, modes, out_dir):
     import torch
 
@@ -55,6 +64,8 @@ def _worker(rank, world, port, ckpt, modes, out_dir):
     res = {}
     for name, kw in modes.items():
         res[name] = m.generate(_ids(), max_new_tokens=5, do_sample=False, **kw)
+    res["padded_prefill"] = m.run_forward(_ids(), "dbo", 2, reset_cache=True,
+                                          attention_mask=_mask())
     if ctx.is_attention_node:
         torch.save(res, os.path.join(out_dir, f"attn{ctx.attn_index}.pt"))
     ctx.barrier()
@@ -75,12 +86,13 @@ def _reference(ckpt):
     devmod.init_backend("cpu")
     m = DisaggregatedQwenModel.from_pretrained(ckpt, device="cpu", dtype=torch.float32,
                                                max_seq_len=64, max_batch_size=4)
-    return m.generate(_ids(), max_new_tokens=5, do_sample=False, use_decode_dbo=False)
+    toks = m.generate(_ids(), max_new_tokens=5, do_sample=False, use_decode_dbo=False)
+    return toks, m.run_forward(_ids(), "serial", 1, reset_cache=True, attention_mask=_mask())
 
 
 @pytest.mark.parametrize("world", [2, 4])
 def test_multi_rank_matches_single_process(ckpt, world):
-    want = _reference(ckpt)
+    want, want_logits = _reference(ckpt)
     out = tempfile.mkdtemp(prefix="afd_out_")
     mp.start_processes(_worker, args=(world, _free_port(), ckpt, MODES, out), nprocs=world,
                        join=True, start_method="spawn")
@@ -89,6 +101,10 @@ def test_multi_rank_matches_single_process(ckpt, world):
         got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))[name]
                          for a in range(n_attn)])
         assert torch.equal(got, want), (world, name)
+    # padded prefill: each attention rank applies its slice of the mask
+    got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))["padded_prefill"]
+                     for a in range(n_attn)])
+    torch.testing.assert_close(got, want_logits, rtol=1e-4, atol=1e-4)
 
 
 def test_single_process_schedules_agree(ckpt):
