@@ -133,3 +133,43 @@ def test_run_single_oom_exit_code(tmp_path):
                        timeout=300)
     assert p.returncode == 2, p.stdout[-2000:]
     assert "OOM DETECTED" in p.stdout
+
+
+REF_SCRIPTS = ROOT / "baseline" / "_ref" / "scripts"
+
+
+def _no_pyc():
+    return dict(os.environ, PYTHONDONTWRITEBYTECODE="1")  # leave the install untouched
+
+
+@pytest.mark.skipif(not (REF_SCRIPTS / "gen_experiment_report.py").exists(),
+                    reason="the reference install (baseline/_ref) is absent")
+def test_reference_scripts_read_our_outputs(matrix, tmp_path):
+    """Schema parity, checked by the reference's own tools: its report
+    generator and baseline audit (scripts/gen_experiment_report.py,
+    scripts/audit_experiment_baselines.py, unmodified) read this framework's
+    timing JSONs and serial cache."""
+    cache = matrix / "serial" / "cache" / "b2_s32_t4.json"
+    for mode in ("serial", "prefill-dbo", "decode-dbo", "decode-dbo-crosslayer"):
+        tag = f"{mode}_b2_s32_t4"
+        out = tmp_path / f"{mode}.md"
+        p = subprocess.run(
+            [sys.executable, "gen_experiment_report.py",
+             "--attn-timing", str(matrix / mode / f"timing_attention_{tag}.json"),
+             "--ffn-timing", str(matrix / mode / f"timing_ffn_{tag}.json"),
+             "--output", str(out), "--mode", mode, "--batch", "2", "--seq", "32",
+             "--tokens", "4", "--serial-baseline", str(cache)],
+            cwd=REF_SCRIPTS, capture_output=True, text=True, timeout=120, env=_no_pyc())
+        assert p.returncode == 0, (mode, p.stderr[-2000:])
+        text = out.read_text()
+        assert "Layer averages" in text
+        if mode != "serial":
+            assert "speedup" in text
+    audit = tmp_path / "audit.csv"
+    p = subprocess.run([sys.executable, "audit_experiment_baselines.py", "--root", str(matrix),
+                        "--output-csv", str(audit)],
+                       cwd=REF_SCRIPTS, capture_output=True, text=True, timeout=120, env=_no_pyc())
+    assert p.returncode == 0, p.stderr[-2000:]
+    rows = list(csv.DictReader(open(audit)))
+    assert len(rows) == 3 and all(r["status"] == "ok" for r in rows)
+    assert {r["note"] for r in rows} == {"decode_tpot_ms", "prefill_ms"}
