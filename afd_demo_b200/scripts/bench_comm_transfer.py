@@ -35,6 +35,18 @@ Roofline of a transfer: bytes crossing the busiest GPU's NVLink ports
 (tokens * row bytes * peers) / 770 GB/s (measured peer copy bandwidth per
 direction); of the fused GEMM: the slower of that and FLOPs / 1656.5 TFLOP/s.
 
+Host-timed section (2 ranks; also the only section with ``--backend cpu``,
+gloo): the reference's own measurement and output schema -- per payload size
+the sender's isend enqueue time, isend start -> Work.wait return, the
+receiver's irecv post -> Work.wait return and, with ``--blocking``, blocking
+send / recv, each summarised as mean / median / p95 / min / max over
+``--iters`` host perf_counter samples after a barrier and a ``--sender-delay-ms``
+pause. With NCCL, Work.wait only orders the stream, so these spans are host
+enqueue figures, not transfer times; the device-timed section above is the
+measurement. JSON: ``{"meta", "results"}`` as the reference writes it, plus
+``"device"`` for the device-timed rows; CSV: the reference's nine columns
+(device rows go to ``<stem>_device.csv``).
+
 Launch: torchrun --nproc-per-node N -m afd_demo_b200.scripts.bench_comm_transfer
 """
 
@@ -46,8 +58,9 @@ import json
 import os
 import statistics
 import sys
+import time
 from pathlib import Path
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -83,20 +96,175 @@ def parse():
     ap.add_argument("--output", default="results/comm_bench/comm_transfer.json")
     ap.add_argument("--csv-output", default="")
     ap.add_argument("--timeout-ms", type=float, default=20000.0)
+    # host-timed section (the reference's flags and defaults)
+    ap.add_argument("--backend", choices=["auto", "cuda", "cpu"], default="auto")
+    ap.add_argument("--dtype", choices=sorted(HOST_DTYPES), default="float16")
+    ap.add_argument("--sender-delay-ms", type=float, default=1.0)
+    ap.add_argument("--blocking", action="store_true")
+    ap.add_argument("--host-only", action="store_true", help="skip the device-timed section")
+    ap.add_argument("--device-only", action="store_true", help="skip the host-timed section")
     return ap.parse_args()
+
+
+HOST_DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32,
+               "uint8": torch.uint8}
+HOST_CSV_COLUMNS = ("size_mib_requested", "tensor_mib", "tensor_bytes", "sender_enqueue_mean_ms",
+                    "sender_completion_mean_ms", "receiver_wait_mean_ms", "blocking_send_mean_ms",
+                    "blocking_recv_mean_ms", "completion_bandwidth_mib_s")
+
+
+def _summary(samples: List[float]) -> Dict[str, float]:
+    """mean / median / p95 (linear interpolation between order statistics) /
+    min / max of host-timed samples in ms."""
+    if not samples:
+        return {"mean": 0.0, "median": 0.0, "p95": 0.0, "min": 0.0, "max": 0.0}
+    t = sorted(samples)
+    pos = 0.95 * (len(t) - 1)
+    i = int(pos)
+    p95 = t[i] + (t[min(i + 1, len(t) - 1)] - t[i]) * (pos - i)
+    return {"mean": statistics.fmean(t), "median": statistics.median(t), "p95": p95,
+            "min": t[0], "max": t[-1]}
+
+
+def host_timed(a, rank: int, device: torch.device, backend: str, dist_backend: str
+               ) -> Optional[dict]:
+    """The reference's two-rank host-timed p2p measurement (rank 0 sends to
+    rank 1). Returns the merged {"meta", "results"} dict on rank 0."""
+    sync = torch.cuda.synchronize if device.type == "cuda" else (lambda: None)
+    dt = HOST_DTYPES[a.dtype]
+    el = torch.empty((), dtype=dt).element_size()
+    delay = a.sender_delay_ms / 1e3
+    peer = 1 - rank
+    local = []
+    for si, size in enumerate(float(x) for x in a.sizes_mib.split(",") if x):
+        x = torch.empty(max(1, -(-max(1, int(size * 2**20)) // el)), dtype=dt, device=device)
+        recv = torch.empty_like(x)
+        nbytes = x.numel() * el
+
+        def exchange(tag: int, blocking: bool) -> float:
+            dist.barrier()
+            sync()
+            if rank == 0:
+                if delay > 0:
+                    time.sleep(delay)
+                t0 = time.perf_counter()
+                if blocking:
+                    dist.send(x, dst=peer, tag=tag)
+                    return (time.perf_counter() - t0) * 1e3, None
+                w = dist.isend(x, dst=peer, tag=tag)
+                t1 = time.perf_counter()
+                w.wait()
+                return (t1 - t0) * 1e3, (time.perf_counter() - t0) * 1e3
+            t0 = time.perf_counter()
+            if blocking:
+                dist.recv(recv, src=peer, tag=tag)
+            else:
+                dist.irecv(recv, src=peer, tag=tag).wait()
+            return (time.perf_counter() - t0) * 1e3, None
+
+        for i in range(a.warmup):
+            exchange(10_000 + i, False)
+        dist.barrier()
+        enq, comp, rwait, bsend, brecv = [], [], [], [], []
+        for i in range(a.iters):
+            t_a, t_b = exchange(20_000 + si * 10_000 + i, False)
+            if rank == 0:
+                enq.append(t_a)
+                comp.append(t_b)
+            else:
+                rwait.append(t_a)
+        dist.barrier()
+        if a.blocking:
+            for i in range(a.iters):
+                t_a, _ = exchange(200_000 + si * 10_000 + i, True)
+                (bsend if rank == 0 else brecv).append(t_a)
+            dist.barrier()
+        local.append({"size_mib_requested": size, "tensor_bytes": nbytes,
+                      "tensor_mib": nbytes / 2**20, "enq": enq, "comp": comp, "rwait": rwait,
+                      "bsend": bsend, "brecv": brecv})
+    both: List[Optional[list]] = [None, None]
+    dist.all_gather_object(both, local)
+    if rank != 0:
+        return None
+    rows = []
+    for snd, rcv in zip(both[0], both[1]):
+        comp = _summary(snd["comp"])
+        row = {"size_mib_requested": snd["size_mib_requested"], "tensor_bytes": snd["tensor_bytes"],
+               "tensor_mib": snd["tensor_mib"], "sender_enqueue_ms": _summary(snd["enq"]),
+               "sender_completion_ms": comp, "receiver_wait_ms": _summary(rcv["rwait"]),
+               "completion_bandwidth_mib_s": (snd["tensor_mib"] * 1e3 / comp["mean"]
+                                              if comp["mean"] > 0 else 0.0)}
+        if a.blocking:
+            row["blocking_send_ms"] = _summary(snd["bsend"])
+            row["blocking_recv_ms"] = _summary(rcv["brecv"])
+        rows.append(row)
+    meta = {"backend": backend, "dist_backend": dist_backend, "dtype": a.dtype,
+            "warmup": a.warmup, "iters": a.iters, "sender_delay_ms": a.sender_delay_ms,
+            "world_size": 2,
+            "note": ("host perf_counter spans: isend start -> Work.wait return (sender), "
+                     "irecv post -> Work.wait return (receiver); with NCCL, Work.wait only "
+                     "orders the stream, so see 'device' for device-timed transfers")}
+    return {"meta": meta, "results": rows}
+
+
+def write_host_csv(path: Path, host: dict) -> None:
+    with path.open("w", newline="") as f:
+        wr = csv.DictWriter(f, fieldnames=list(HOST_CSV_COLUMNS))
+        wr.writeheader()
+        for r in host["results"]:
+            wr.writerow({
+                "size_mib_requested": r["size_mib_requested"], "tensor_mib": r["tensor_mib"],
+                "tensor_bytes": r["tensor_bytes"],
+                "sender_enqueue_mean_ms": r["sender_enqueue_ms"]["mean"],
+                "sender_completion_mean_ms": r["sender_completion_ms"]["mean"],
+                "receiver_wait_mean_ms": r["receiver_wait_ms"]["mean"],
+                "blocking_send_mean_ms": r.get("blocking_send_ms", {}).get("mean", ""),
+                "blocking_recv_mean_ms": r.get("blocking_recv_ms", {}).get("mean", ""),
+                "completion_bandwidth_mib_s": r["completion_bandwidth_mib_s"]})
 
 
 def main() -> int:
     a = parse()
-    from afd_demo_b200 import ops
-
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     if world < 2:
         raise SystemExit("needs >= 2 ranks (1 attention + FFN ranks)")
+    backend = a.backend
+    if backend == "auto":
+        backend = "cuda" if torch.cuda.is_available() else "cpu"
+    out_path = Path(a.output)
+    csv_path = Path(a.csv_output) if a.csv_output else out_path.with_suffix(".csv")
+    if backend == "cpu":
+        if world != 2:
+            raise SystemExit("the host-timed (cpu/gloo) benchmark runs on exactly 2 ranks")
+        dist.init_process_group("gloo")
+        host = host_timed(a, rank, torch.device("cpu"), "cpu", "gloo")
+        if rank == 0:
+            out_path.parent.mkdir(parents=True, exist_ok=True)
+            out_path.write_text(json.dumps(host, indent=2))
+            write_host_csv(csv_path, host)
+            print(f"wrote {out_path} and {csv_path}")
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+
+    from afd_demo_b200 import ops
+
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
     dist.init_process_group("nccl", device_id=dev)
+    host = None
+    if world == 2 and not a.device_only:
+        host = host_timed(a, rank, dev, "cuda", "nccl")
+    if a.host_only:
+        if rank == 0:
+            out_path.parent.mkdir(parents=True, exist_ok=True)
+            out_path.write_text(json.dumps(host, indent=2))
+            write_host_csv(csv_path, host)
+            print(f"wrote {out_path} and {csv_path}")
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+        return 0
     C = ops.ext()
     n_ffn = world - 1
     sizes = [float(s) for s in a.sizes_mib.split(",") if s]
@@ -288,18 +456,21 @@ def main() -> int:
     ok = torch.tensor([int(st[0])], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MAX)
     if rank == 0:
-        out = {"world": world, "n_ffn": n_ffn, "iters": a.iters, "warmup": a.warmup,
-               "device_timed": True, "status_ok": int(ok) == 0, "results": results}
-        p = Path(a.output)
-        p.parent.mkdir(parents=True, exist_ok=True)
-        p.write_text(json.dumps(out, indent=2))
-        csv_path = Path(a.csv_output) if a.csv_output else p.with_suffix(".csv")
+        device = {"world": world, "n_ffn": n_ffn, "iters": a.iters, "warmup": a.warmup,
+                  "device_timed": True, "status_ok": int(ok) == 0, "results": results}
+        out = dict(host) if host is not None else {}
+        out["device"] = device
+        out_path.parent.mkdir(parents=True, exist_ok=True)
+        out_path.write_text(json.dumps(out, indent=2))
+        dev_csv = csv_path.with_name(csv_path.stem + "_device.csv")
         keys = sorted({k for r in results for k in r})
-        with csv_path.open("w", newline="") as f:
+        with dev_csv.open("w", newline="") as f:
             wr = csv.DictWriter(f, fieldnames=keys)
             wr.writeheader()
             wr.writerows(results)
-        print(f"wrote {p} and {csv_path}")
+        if host is not None:
+            write_host_csv(csv_path, host)
+        print(f"wrote {out_path}, {dev_csv}" + (f" and {csv_path}" if host is not None else ""))
     for p_ in peer.values():
         C.ipc_close(p_)
     dist.barrier(device_ids=[local])

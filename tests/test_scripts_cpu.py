@@ -173,3 +173,33 @@ def test_reference_scripts_read_our_outputs(matrix, tmp_path):
     rows = list(csv.DictReader(open(audit)))
     assert len(rows) == 3 and all(r["status"] == "ok" for r in rows)
     assert {r["note"] for r in rows} == {"decode_tpot_ms", "prefill_ms"}
+
+
+def test_comm_bench_host_section_reference_schema(tmp_path):
+    """The comm microbenchmark on 2 gloo ranks writes the reference's JSON
+    layout ({"meta", "results"}, per-span mean/median/p95/min/max) and its
+    nine CSV columns."""
+    out = tmp_path / "comm.json"
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    p = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port",
+                        str(_free_port()), "-m", "afd_demo_b200.scripts.bench_comm_transfer",
+                        "--backend", "cpu", "--sizes-mib", "0.004,1", "--iters", "4",
+                        "--warmup", "1", "--blocking", "--output", str(out)],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
+    d = json.loads(out.read_text())
+    assert set(d) == {"meta", "results"}
+    assert d["meta"]["dist_backend"] == "gloo" and d["meta"]["world_size"] == 2
+    assert [r["size_mib_requested"] for r in d["results"]] == [0.004, 1.0]
+    for r in d["results"]:
+        for span in ("sender_enqueue_ms", "sender_completion_ms", "receiver_wait_ms",
+                     "blocking_send_ms", "blocking_recv_ms"):
+            assert set(r[span]) == {"mean", "median", "p95", "min", "max"}
+            assert r[span]["min"] <= r[span]["p95"] <= r[span]["max"]
+    rows = list(csv.DictReader(open(out.with_suffix(".csv"))))
+    assert list(rows[0]) == ["size_mib_requested", "tensor_mib", "tensor_bytes",
+                             "sender_enqueue_mean_ms", "sender_completion_mean_ms",
+                             "receiver_wait_mean_ms", "blocking_send_mean_ms",
+                             "blocking_recv_mean_ms", "completion_bandwidth_mib_s"]
+    assert int(rows[1]["tensor_bytes"]) == 2**20
