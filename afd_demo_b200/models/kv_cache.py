@@ -57,10 +57,13 @@ class KVCache:
     def get_seq_length(self, layer_idx: int = 0) -> int:
         return self.seq_len
 
-    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int
-               ) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Append [B, n_kv, q, D] at the current length of layer `layer_idx`;
-        the length advances once every layer has appended the same count."""
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs=None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Append [B, n_kv, q, D] at the current length of layer `layer_idx`
+        and return the layer's keys / values so far, as
+        ``DynamicCache.update(key, value, layer_idx, cache_kwargs)`` does
+        (`cache_kwargs`, RoPE metadata in HF, is not needed here); the length
+        advances once every layer has appended the same count."""
         B, _, q, _ = key_states.shape
         s = self.seq_len
         self.k[layer_idx, :B, :, s:s + q] = key_states
