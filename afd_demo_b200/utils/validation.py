@@ -7,14 +7,15 @@ from typing import Dict, Tuple
 import torch
 
 
-def compare_tensors(a: torch.Tensor, b: torch.Tensor, rtol: float = 1e-3, atol: float = 1e-3,
+def compare_tensors(a: torch.Tensor, b: torch.Tensor, rtol: float = 1e-3, atol: float = 1e-5,
                     name: str = "tensor") -> Tuple[bool, Dict[str, float]]:
-    """allclose plus max/mean absolute and relative differences."""
+    """allclose(a, b) plus max/mean absolute differences and max/mean
+    differences relative to |a| (+1e-10), with the reference's defaults."""
     if a.shape != b.shape:
         return False, {"error": f"shape mismatch {tuple(a.shape)} vs {tuple(b.shape)}"}
     af, bf = a.detach().float().cpu(), b.detach().float().cpu()
     diff = (af - bf).abs()
-    rel = diff / bf.abs().clamp_min(1e-8)
+    rel = diff / (af.abs() + 1e-10)
     metrics = {
         "max_abs_diff": float(diff.max()) if diff.numel() else 0.0,
         "mean_abs_diff": float(diff.mean()) if diff.numel() else 0.0,
@@ -24,9 +25,11 @@ def compare_tensors(a: torch.Tensor, b: torch.Tensor, rtol: float = 1e-3, atol: 
     return bool(torch.allclose(af, bf, rtol=rtol, atol=atol)), metrics
 
 
-def validate_output(output: torch.Tensor, expected: torch.Tensor, rtol: float = 1e-2,
-                    atol: float = 1e-2) -> bool:
-    ok, _ = compare_tensors(output, expected, rtol, atol)
+def validate_output(output: torch.Tensor, reference: torch.Tensor, rtol: float = 1e-3,
+                    atol: float = 1e-5) -> bool:
+    """Whether `output` is within tolerance of `reference` (allclose with the
+    reference as the expected side)."""
+    ok, _ = compare_tensors(reference, output, rtol, atol, name="model_output")
     return ok
 
 

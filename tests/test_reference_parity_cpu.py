@@ -1,0 +1,74 @@
+"""Host-side parity with the reference's own modules, loaded unmodified from
+the reference install in baseline/_ref: micro-batch splitting and merging
+(src/pipeline/micro_batch.py), position ids and causal masks, and tensor
+comparison (src/utils/validation.py). Same inputs, same outputs."""
+
+import importlib.util
+from pathlib import Path
+
+import pytest
+import torch
+
+from afd_demo_b200.parallel import micro_batch as ours_mb
+from afd_demo_b200.utils import validation as ours_val
+
+REF = Path(__file__).resolve().parents[1] / "baseline" / "_ref" / "src"
+
+
+def _load(rel: str, name: str):
+    path = REF / rel
+    if not path.exists():
+        pytest.skip("the reference install (baseline/_ref) is absent")
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.fixture(scope="module")
+def ref_mb():
+    return _load("pipeline/micro_batch.py", "_ref_micro_batch")
+
+
+@pytest.fixture(scope="module")
+def ref_val():
+    return _load("utils/validation.py", "_ref_validation")
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 5, 8, 9])
+@pytest.mark.parametrize("nmb", [1, 2, 3, 4])
+def test_split_and_merge(ref_mb, B, nmb):
+    cpu = torch.device("cpu")
+    ids = torch.arange(B * 6).view(B, 6)
+    mask = (torch.rand(B, 6, generator=torch.Generator().manual_seed(B)) > 0.3).long()
+    mine = ours_mb.MicroBatchManager(nmb, cpu).split_batch(ids, mask)
+    theirs = ref_mb.MicroBatchManager(nmb, cpu).split_batch(ids, mask)
+    assert [m.batch_size for m in mine] == [m.batch_size for m in theirs]
+    assert [m.id for m in mine] == [m.id for m in theirs]
+    for a, b in zip(mine, theirs):
+        assert torch.equal(a.input_ids, b.input_ids)
+        assert torch.equal(a.attention_mask, b.attention_mask)
+        assert a.seq_len == b.seq_len
+    outs = [m.input_ids.float() * 2 for m in mine]
+    assert torch.equal(ours_mb.MicroBatchManager(nmb, cpu).merge_results(outs),
+                       ref_mb.MicroBatchManager(nmb, cpu).merge_results(outs))
+
+
+def test_positions_and_causal_mask(ref_mb):
+    cpu = torch.device("cpu")
+    assert torch.equal(ours_mb.create_position_ids(3, 7, cpu),
+                       ref_mb.create_position_ids(3, 7, cpu))
+    assert torch.equal(ours_mb.create_causal_mask(2, 5, cpu), ref_mb.create_causal_mask(2, 5, cpu))
+
+
+@pytest.mark.parametrize("scale", [0.0, 1e-5, 1e-2, 1.0])
+def test_compare_tensors(ref_val, scale):
+    a = torch.randn(64, 32, generator=torch.Generator().manual_seed(0))
+    b = a + scale * torch.randn(64, 32, generator=torch.Generator().manual_seed(1))
+    close_o, met_o = ours_val.compare_tensors(a, b)
+    close_r, met_r = ref_val.compare_tensors(a, b)
+    assert close_o == close_r
+    for k, v in met_r.items():
+        assert k in met_o
+        assert met_o[k] == pytest.approx(v, rel=1e-6, abs=1e-12), k
+    assert ours_val.validate_output(a, b) == ref_val.validate_output(a, b)
