@@ -1,6 +1,7 @@
 """Host-side parity with the reference's own modules, loaded unmodified from
 the reference install in baseline/_ref: micro-batch splitting and merging
-(src/pipeline/micro_batch.py), position ids and causal masks, and tensor
+(src/pipeline/micro_batch.py), position ids and causal masks, the timing JSON
+(src/utils/timing.py) and tensor
 comparison (src/utils/validation.py). Same inputs, same outputs."""
 
 import importlib.util
@@ -72,3 +73,42 @@ def test_compare_tensors(ref_val, scale):
         assert k in met_o
         assert met_o[k] == pytest.approx(v, rel=1e-6, abs=1e-12), k
     assert ours_val.validate_output(a, b) == ref_val.validate_output(a, b)
+
+
+@pytest.fixture(scope="module")
+def ref_timing():
+    return _load("utils/timing.py", "_ref_timing")
+
+
+def _fill(mod, node):
+    pt = mod.PipelineTiming(node=node, num_layers=3, num_micro_batches=2, total_time_ms=9.5,
+                            comm_timing_mode="completion")
+    pt.prefill_ms = 4.25
+    pt.decode_tpot_ms = 1.5
+    pt.decode_steps = 3
+    t = 0.0
+    kinds = ["attn_compute", "send_transfer", "recv_wait", "moe_router", "moe_experts",
+             "ffn_compute", "recv_post", "send_start", "moe_shared_or_dense"]
+    for l in range(3):
+        for m in range(2):
+            for i, k in enumerate(kinds):
+                ev = mod.TimingEvent(k, l, m, t, t + 0.0001 * (i + 1), node,
+                                     tensor_bytes=4096 * (i + 1) if "send" in k else None,
+                                     completion_source="wait" if k == "send_transfer" else None)
+                pt.add_event(ev)
+                t += 0.0002
+    return pt
+
+
+def test_timing_json_and_merge(ref_timing):
+    from afd_demo_b200.utils import timing as ours
+
+    assert {e.value for e in ours.EventType} == {e.value for e in ref_timing.EventType}
+    for node in ("attention", "ffn"):
+        assert _fill(ours, node).to_dict() == _fill(ref_timing, node).to_dict()
+    mine = ours.merge_timings(_fill(ours, "attention"), _fill(ours, "ffn"))
+    theirs = ref_timing.merge_timings(_fill(ref_timing, "attention"), _fill(ref_timing, "ffn"))
+    assert mine == theirs
+    # and the JSON round trip through this framework's reader
+    back = ours.PipelineTiming.from_dict(_fill(ref_timing, "ffn").to_dict())
+    assert back.to_dict() == _fill(ref_timing, "ffn").to_dict()
