@@ -5,6 +5,7 @@ the reference install in baseline/_ref: micro-batch splitting and merging
 comparison (src/utils/validation.py). Same inputs, same outputs."""
 
 import importlib.util
+import sys
 from pathlib import Path
 
 import pytest
@@ -22,6 +23,7 @@ def _load(rel: str, name: str):
         pytest.skip("the reference install (baseline/_ref) is absent")
     spec = importlib.util.spec_from_file_location(name, path)
     mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod  # dataclasses look their module up while being built
     spec.loader.exec_module(mod)
     return mod
 
@@ -112,3 +114,26 @@ def test_timing_json_and_merge(ref_timing):
     # and the JSON round trip through this framework's reader
     back = ours.PipelineTiming.from_dict(_fill(ref_timing, "ffn").to_dict())
     assert back.to_dict() == _fill(ref_timing, "ffn").to_dict()
+
+
+def test_serial_baseline_resolution():
+    """scripts/experiment_baselines.py: mode classes and the serial baseline
+    chosen for every kind of serial cache entry."""
+    ref = _load("../scripts/experiment_baselines.py", "_ref_baselines")
+    from afd_demo_b200.scripts import experiment_baselines as ours
+
+    modes = [None, "", "serial", "prefill", "prefill-dbo", "prefill_dbo", "decode", "decode-dbo",
+             "decode_dbo", "decode-dbo-crosslayer", "dbo_crosslayer", "crosslayer", "dbo", "weird"]
+    for m in modes:
+        assert ours.normalize_mode(m) == ref.normalize_mode(m), m
+    for p in ["results/decode-dbo/x.json", "results/prefill-dbo/x.json", "results/serial/x.json",
+              "r/decode-dbo-crosslayer/timing_attention_decode-dbo-crosslayer_b2.json", "a/b.json"]:
+        assert ours.infer_mode_from_path(p) == ref.infer_mode_from_path(p), p
+    caches = [{}, {"prefill_ms": 12.0}, {"decode_tpot_ms": 3.0}, {"decode_step_ms": 9.0},
+              {"total_time_ms": 5.0}, {"prefill_ms": 12.0, "decode_tpot_ms": 3.0},
+              {"prefill_ms": None, "decode_tpot_ms": 0.0}, {"prefill_ms": "7.5"}]
+    for c in caches:
+        for m in modes:
+            a, b = ours.resolve_serial_baseline(c, m), ref.resolve_serial_baseline(c, m)
+            assert (a.value_ms, a.unit, a.source, a.available) == \
+                   (b.value_ms, b.unit, b.source, b.available), (c, m)
