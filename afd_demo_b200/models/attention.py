@@ -21,7 +21,7 @@ shard layers over the role's visible GPUs. Here one B200 holds every layer
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Optional, Sequence
 
 import torch
 

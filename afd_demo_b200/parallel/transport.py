@@ -29,8 +29,8 @@ from __future__ import annotations
 
 import datetime
 import logging
-from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Sequence, Tuple
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist

@@ -1,7 +1,5 @@
 """sm_100a kernels against PyTorch fp32 statements of the same ops."""
 
-import math
-
 import pytest
 import torch
 
