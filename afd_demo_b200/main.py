@@ -35,6 +35,15 @@ import torch
 
 DEFAULT_MODEL_PATH = os.environ.get("MODEL_PATH", "qwen3-30b-a3b")
 
+# Quiet third-party libraries as the reference's CLI does (src/main.py:27-38).
+# Its default HF_ENDPOINT mirror is not set: checkpoints are read from local
+# directories only, nothing is downloaded.
+for _k, _v in (("TRANSFORMERS_VERBOSITY", "error"), ("HF_HUB_DISABLE_PROGRESS_BARS", "1"),
+               ("HF_HUB_VERBOSITY", "error"), ("TOKENIZERS_PARALLELISM", "false")):
+    os.environ.setdefault(_k, _v)
+warnings.filterwarnings("ignore", category=FutureWarning)
+warnings.filterwarnings("ignore", category=DeprecationWarning)
+
 
 def setup_logging(verbose: bool = False) -> logging.Logger:
     level = logging.DEBUG if verbose else logging.INFO
