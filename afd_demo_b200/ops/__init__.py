@@ -638,11 +638,24 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
 
 
 # ------------------------------------------------------------- sampling --
+class _ArgmaxWorkspace(_GateCounters):
+    """Workspace of the split argmax: per-row counters (left zeroed by the
+    kernel) and per-chunk partials, one buffer per (device, stream)."""
+
+    _pool: dict = {}
+    _retired: list = []
+
+
 def argmax(logits: torch.Tensor) -> torch.Tensor:
+    """First index of the row maximum (torch.argmax semantics for finite
+    values) [rows, V] bf16 -> [rows] int64. Large rows are split over several
+    CTAs with a last-CTA reduction."""
     if not _cuda(logits) or logits.dtype != torch.bfloat16:
         return torch_ref.argmax(logits)
     out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
-    ext().argmax(logits, out)
+    n = ext().argmax_workspace_ints(logits.shape[0], logits.shape[1])
+    ws = _ArgmaxWorkspace.get(logits.device, n - 1)
+    ext().argmax(logits, out, ws)
     return out
 
 

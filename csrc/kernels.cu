@@ -758,6 +758,80 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logit
   }
 }
 
+// Split argmax: CTA (c, row) reduces chunk c of the row (16-byte loads) into
+// a partial (value, index) in the workspace; the last CTA of the row (per-row
+// counter, reset by it) reduces the partials. Same tie and NaN rules as
+// argmax_kernel: the first index of the maximum, NaN never chosen.
+// Workspace (int32): counters [rows] (zero) | values [rows * n] | indices [rows * n].
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxChunk = 8192;  // elements per CTA: 4 x 16-byte loads per thread
+
+__device__ __forceinline__ void argmax_take(float v, int i, float& best, int& bi) {
+  if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+}
+
+__device__ __forceinline__ void argmax_warp(float& best, int& bi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffff, best, o);
+    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+    argmax_take(ov, oi, best, bi);
+  }
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_split_kernel(
+    const __nv_bfloat16* logits, int V, int ld, int64_t* out, int* ws) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.y, chunk = blockIdx.x, n = gridDim.x, rows = gridDim.y;
+  const int start = chunk * kArgmaxChunk;
+  const int end = min(V, start + kArgmaxChunk);
+  const int vend = start + ((end - start) / 8) * 8;
+  const __nv_bfloat16* p = logits + (size_t)row * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = start + threadIdx.x * 8; i < vend; i += kArgmaxThreads * 8) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(p + i));
+    const uint32_t* w = &q.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a, b;
+      unpack_bf16x2(w[j], a, b);
+      argmax_take(a, i + 2 * j, best, bi);
+      argmax_take(b, i + 2 * j + 1, best, bi);
+    }
+  }
+  for (int i = vend + threadIdx.x; i < end; i += kArgmaxThreads) argmax_take(bf16_to_f(p[i]), i, best, bi);
+  argmax_warp(best, bi);
+  const int wp = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) { sv[wp] = best; si[wp] = bi; }
+  __syncthreads();
+  int* cnt = ws;
+  float* pv = reinterpret_cast<float*>(ws + rows);
+  int* pi = ws + rows + rows * n;
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < kArgmaxThreads / 32; ++k) argmax_take(sv[k], si[k], best, bi);
+    pv[row * n + chunk] = best;
+    pi[row * n + chunk] = bi;
+    __threadfence();
+    s_last = atomicAdd(&cnt[row], 1) == n - 1;
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x >= 32) return;
+  __threadfence();
+  best = -INFINITY;
+  bi = 0x7fffffff;
+  for (int c = l; c < n; c += 32) argmax_take(__ldcg(pv + row * n + c), __ldcg(pi + row * n + c), best, bi);
+  argmax_warp(best, bi);
+  if (l == 0) {
+    out[row] = bi;
+    cnt[row] = 0;
+  }
+}
+
 // ---------------------------------------------------------------- flags ---
 __global__ void signal_flags_kernel(FlagArgs a) {
   pdl_wait();
@@ -1007,10 +1081,20 @@ int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s) {
   return (int)launch_k(moe_combine_kernel, dim3(T), dim3(kNormThreads), 0, s, a);
 }
 
+int argmax_workspace_ints(int rows, int V) {
+  return rows + 2 * rows * ((V + kArgmaxChunk - 1) / kArgmaxChunk);
+}
+
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
-                  cudaStream_t s) {
+                  int* ws, cudaStream_t s) {
   if (rows == 0) return 0;
-  return (int)launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, logits, V, ld, out);
+  const bool split = ws != nullptr && V > kArgmaxChunk && ld % 8 == 0 &&
+                     reinterpret_cast<uintptr_t>(logits) % 16 == 0 && rows <= 65535;
+  if (!split)
+    return (int)launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, logits, V, ld, out);
+  const dim3 grid((V + kArgmaxChunk - 1) / kArgmaxChunk, rows);
+  return (int)launch_k(argmax_split_kernel, grid, dim3(kArgmaxThreads), 0, s, logits, V, ld, out,
+                       ws);
 }
 
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s) {

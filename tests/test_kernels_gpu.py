@@ -223,6 +223,29 @@ def test_argmax():
     x = _randn(5, 151936, seed=70)
     x[2, 12345] = 100.0
     assert torch.equal(ops.argmax(x), x.float().argmax(-1))
+    assert torch.equal(ops.argmax(x), x.float().argmax(-1))  # workspace counters reset
+
+
+@pytest.mark.parametrize("V", [100, 8192, 8200, 151936, 151937])
+def test_argmax_ties_and_strided_rows(V):
+    """Ties across chunks go to the first index; a ragged tail, a NaN (never
+    chosen, as in the one-CTA kernel) and row views of a wider matrix (the
+    one-CTA fallback when the rows are not 16-byte aligned)."""
+    x = _randn(3, V, seed=71)
+    x[0, V - 1] = 50.0
+    x[0, V // 3] = 50.0  # tie: the first index wins
+    x[1, 7] = float("nan")
+    x[1, V // 2] = 60.0
+    ref = x.float().nan_to_num(-1e30).argmax(-1)
+    assert torch.equal(ops.argmax(x), ref)
+    wide = _randn(3, V + 3, seed=72)
+    view = wide[:, 1:V + 1]
+    assert torch.equal(ops.argmax(view), view.float().argmax(-1))
+    # aligned rows whose length is not a multiple of 8: scalar tail of the last chunk
+    wide = _randn(3, V + 16, seed=73)
+    view = wide[:, :V + 3]
+    view[2, V + 2] = 70.0
+    assert torch.equal(ops.argmax(view), view.float().argmax(-1))
 
 
 def test_flags_roundtrip_and_timeout():
