@@ -182,12 +182,17 @@ def _moe_block_n(rows: int) -> int:
     return 64 if rows <= 64 else (128 if rows < 2048 else _MOE_BN_LARGE)
 
 
+# upper bound of the split-K factor (AFD_MAX_SPLITS for A/B measurements)
+_MAX_SPLITS = int(os.environ.get("AFD_MAX_SPLITS", "16"))
+
+
 def _k_splits(tiles: int, k_iters: int) -> int:
     """Split-K factor for GEMMs with too few output tiles to fill the GPU:
     the largest power of two with tiles * s <= SMs and >= 2 k-steps per split."""
     s = 1
     n = num_sms()
-    while tiles * s * 2 <= n and k_iters % (s * 2) == 0 and k_iters // (s * 2) >= 2:
+    while (tiles * s * 2 <= n and k_iters % (s * 2) == 0 and k_iters // (s * 2) >= 2
+           and s * 2 <= _MAX_SPLITS):
         s *= 2
     return s
 
@@ -366,9 +371,10 @@ class MoEWorkspace:
         self.block_n = block_n
 
 
-# token counts up to which the MoE combine runs inside the down GEMM (one CTA
-# per 128 output features sums every token's rows); larger batches use the
-# one-CTA-per-token combine kernel
+# decode-sized token counts: up to here the F2A rows are stored by the combine
+# itself (straight to the attention ranks), or, with AFD_FUSED_COMBINE=1, by
+# the down GEMM's epilogue; above, the combine writes locally and one bulk
+# peer copy per attention rank moves the rows
 _FUSED_COMBINE_MAX_TOKENS = 256
 
 
@@ -415,7 +421,7 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
            None, ws.row_weight, False, bn, ws.max_blocks * (H // 128), [], 0, [], 0, None, None,
            None, 1, None, None, None)
-    if peers and _SPLIT_F2A:
+    if peers and _SPLIT_F2A and T > _FUSED_COMBINE_MAX_TOKENS:
         # prefill sizes: combine locally, then one bulk peer copy per attention
         # rank's segment (the combine kernel's scattered NVLink stores run at
         # about half the link bandwidth; the copy kernel reaches ~0.7 of it)
@@ -430,6 +436,8 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
             C.peer_copy(local[lo:hi], [int(dst) + int(peer_row_offset) * row_bytes], [int(flag)],
                         int(signal_value), done_counter, epoch, grid)
         return out
+    # decode sizes: the combine stores each token's row straight into its
+    # attention rank's buffer (one kernel; no local copy and second launch)
     C.moe_combine(ws.y, ws.inv, T, k, residual, out, list(peers), list(seg_offsets),
                   int(peer_row_offset), list(flags), int(signal_value), done_counter, epoch)
     return out
