@@ -446,6 +446,22 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
 _ALIGN_CHUNK = 2048  # routed entries per CTA of the multi-CTA routing
 
 
+# AFD_BOUNDS_CHECK=1: validate the routing tables on the host after every
+# routing step (debug mode, one device sync per MoE layer; see ops/checks.py)
+_BOUNDS_CHECK = os.environ.get("AFD_BOUNDS_CHECK", "0") == "1"
+
+
+def _check_routing(ids: torch.Tensor, weights: torch.Tensor, expert_start: int, E_loc: int,
+                   ws: "MoEWorkspace") -> None:
+    if not _BOUNDS_CHECK or torch.cuda.is_current_stream_capturing():
+        return
+    from .checks import check_routing_tables
+    torch.cuda.current_stream().synchronize()
+    check_routing_tables(ids, weights, expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                         ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks,
+                         ws.num_rows)
+
+
 def _align(ids: torch.Tensor, weights: torch.Tensor, expert_start: int, E_loc: int,
            ws: "MoEWorkspace") -> None:
     """Expert-sorted rows and row blocks from top-k ids: one CTA up to two
@@ -484,6 +500,7 @@ def moe_experts(xn: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     if ws is None:
         ws = MoEWorkspace(T, k, E_loc, H, I2 // 2, _moe_block_n(T), xn.device, xn.dtype)
     _align(ids, weights, expert_start, E_loc, ws)
+    _check_routing(ids, weights, expert_start, E_loc, ws)
     return _moe_gemms_combine(xn, ws, w_gate_up, w_down, residual, out, T, k, peers, seg_offsets,
                               peer_row_offset, flags, signal_value, done_counter, epoch)
 
@@ -604,6 +621,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
                    _gate_groups(T, E), expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows,
                    *_wait_args(wait))
+        _check_routing(ws.ids, ws.weights, expert_start, E_loc, ws)
         mark(False, "router")
         mark(True, "experts")
         y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T,
@@ -620,6 +638,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
     else:
         C.router_topk(logits, ws.ids, ws.weights, top_k, bool(norm_topk_prob))
         _align(ws.ids, ws.weights, expert_start, E_loc, ws)
+    _check_routing(ws.ids, ws.weights, expert_start, E_loc, ws)
     mark(False, "router")
     mark(True, "experts")
     y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T, top_k,
