@@ -102,6 +102,24 @@ def test_moe_ffn_block_fused_combine(T, E_loc, start, monkeypatch):
     assert _rel(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("T,E_loc,start", [(16, 128, 0), (300, 128, 0), (1024, 32, 32)])
+def test_routing_tables_pass_bounds_check(T, E_loc, start, monkeypatch):
+    """AFD_BOUNDS_CHECK=1 validates the routing tables of the fused gate (16
+    tokens), the one-CTA route kernel (300) and the multi-CTA align (1024) on
+    the host; the layer output is unchanged."""
+    monkeypatch.setattr(ops, "_BOUNDS_CHECK", True)
+    H, I, E = 2048, 768, 128
+    h = _randn(T, H, seed=21)
+    pw = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    wr = _randn(E, H, scale=0.02, seed=22)
+    wgu = _randn(E_loc, 2 * I, H, scale=0.02, seed=23)
+    wd = _randn(E_loc, H, I, scale=0.02, seed=24)
+    ref = torch_ref.ffn_layer(h, pw, wr, wgu, wd, 8, 1e-6, expert_start=start,
+                              add_residual=(start == 0))
+    out = ops.moe_ffn(h, pw, wr, wgu, wd, 8, 1e-6, True, start, add_residual=(start == 0))
+    assert _rel(out, ref) < 2e-2
+
+
 def test_moe_residual_and_ep_partials_sum():
     T, H, I, E = 48, 2048, 768, 128
     xn = _randn(T, H, seed=9)
