@@ -229,17 +229,27 @@ class DisaggregatedQwenModel:
     @torch.no_grad()
     def forward_prefill(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                         mode: str = "serial", num_micro_batches: int = 1,
-                        crosslayer: bool = False) -> Optional[torch.Tensor]:
-        """Prefill (resets and fills the KV cache); last-position logits
-        [B_local, V]. The reference's generate always prefills serially and
-        unsplit; `mode="dbo"` runs the micro-batched overlap instead."""
-        return self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True,
-                                attention_mask=attention_mask)
+                        crosslayer: bool = False, last_only: bool = False
+                        ) -> Optional[torch.Tensor]:
+        """Prefill (resets and fills the KV cache). Logits [B_local, S, V] on
+        attention ranks, as the reference's forward_prefill returns them
+        (src/model/disaggregated.py:377-443); `last_only` projects only the
+        last position ([B_local, V]), which is all sampling needs. The
+        reference's generate always prefills serially and unsplit;
+        `mode="dbo"` runs the micro-batched overlap instead."""
+        S = input_ids.shape[1]
+        out = self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True,
+                               attention_mask=attention_mask, last_only=last_only)
+        if out is None or last_only:
+            return out
+        return out.view(-1, S, out.shape[-1])
 
     @torch.no_grad()
     def forward_decode(self, input_ids: torch.Tensor) -> Optional[torch.Tensor]:
-        """One serial decode step for tokens [B, 1]; logits [B_local, V]."""
-        return self.run_forward(input_ids, "serial", 1)
+        """One serial decode step for tokens [B, 1]; logits [B_local, 1, V] on
+        attention ranks (the reference's shape, src/model/disaggregated.py:445-506)."""
+        out = self.run_forward(input_ids, "serial", 1)
+        return None if out is None else out.unsqueeze(1)
 
     def forward_layer_sync(self, *a, **kw):  # pragma: no cover - name kept for API parity
         raise NotImplementedError("per-layer host round trips are replaced by run_forward(mode='serial')")

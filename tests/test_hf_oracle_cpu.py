@@ -113,3 +113,20 @@ def test_padding_mask_matches_hf(models, side):
     for mode, nmb in (("serial", 1), ("dbo", 2)):
         last = ours.run_forward(ids, mode, nmb, reset_cache=True, attention_mask=mask).float()
         assert (last - ref[:, -1]).abs().max().item() < 1e-3 * max(1.0, ref[:, -1].abs().max().item())
+
+
+def test_forward_prefill_and_decode_shapes_match_hf(models):
+    """forward_prefill returns logits for every position and forward_decode
+    [B, 1, V], the reference's shapes; both equal HF's logits."""
+    hf, ours, ids = models
+    with torch.no_grad():
+        ref = hf(ids).logits.float()
+    full = ours.forward_prefill(ids).float()
+    assert full.shape == ref.shape
+    assert (full - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+    nxt = ref[:, -1].argmax(-1, keepdim=True)
+    step = ours.forward_decode(nxt).float()
+    with torch.no_grad():
+        ref2 = hf(torch.cat([ids, nxt], 1)).logits[:, -1:].float()
+    assert step.shape == ref2.shape
+    assert (step - ref2).abs().max().item() < 1e-3 * max(1.0, ref2.abs().max().item())
