@@ -251,10 +251,59 @@ class DisaggregatedQwenModel:
         out = self.run_forward(input_ids, "serial", 1)
         return None if out is None else out.unsqueeze(1)
 
-    def forward_layer_sync(self, *a, **kw):  # pragma: no cover - name kept for API parity
-        raise NotImplementedError("per-layer host round trips are replaced by run_forward(mode='serial')")
+    # ------------------------------------------------ per-layer entry points
+    def _one_layer(self, layer_idx: int, hidden_states: torch.Tensor, start: int,
+                   attention_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        if not (self.ctx.is_attention_node and self.ctx.is_ffn_node):
+            raise NotImplementedError(
+                "per-layer calls run where both roles live (one process); across ranks the "
+                "layers run inside forward / forward_prefill / generate")
+        aw, fw = self.attention_worker, self.ffn_worker
+        B, S, H = hidden_states.shape
+        x = hidden_states.reshape(B * S, H).to(self.device, self.dtype)
+        aw.key_range = (key_ranges_from_mask(attention_mask.to(self.device))
+                        if attention_mask is not None and attention_mask.dim() == 2 and S > 1
+                        else None)
+        try:
+            h = aw.forward_attention_layer(layer_idx, [x], 0, S, start_pos=start)
+        finally:
+            aw.key_range = None
+        return fw.forward_ffn_layer(layer_idx, h, add_residual=True).view(B, S, H)
 
-    forward_layer_with_cache = forward_layer_sync
+    @torch.no_grad()
+    def forward_layer_sync(self, layer_idx: int, hidden_states: torch.Tensor,
+                           attention_mask: Optional[torch.Tensor] = None,
+                           position_ids: Optional[torch.Tensor] = None,
+                           position_embeddings=None) -> torch.Tensor:
+        """One layer (attention + FFN) of a whole sequence, positions 0..S-1,
+        without a KV cache to continue: hidden [B, S, H] -> [B, S, H], as the
+        reference's validation path (src/model/disaggregated.py:142-224). The
+        layer's KV-cache rows serve as scratch; layer 0 resets the cache.
+        `attention_mask` may be a [B, S] padding mask; positions are always
+        0..S-1 and `position_embeddings` are computed inside the kernels, so
+        both position arguments are accepted for the reference's signature
+        and not needed."""
+        if layer_idx == 0 or self.kv_cache.seq_len != 0:
+            self.kv_cache.reset(hidden_states.shape[0])
+        return self._one_layer(layer_idx, hidden_states, 0, attention_mask)
+
+    @torch.no_grad()
+    def forward_layer_with_cache(self, layer_idx: int, hidden_states: torch.Tensor,
+                                 attention_mask: Optional[torch.Tensor] = None,
+                                 position_ids: Optional[torch.Tensor] = None,
+                                 position_embeddings=None, use_cache: bool = True
+                                 ) -> torch.Tensor:
+        """One layer for tokens that continue the KV cache: S prompt tokens
+        (prefill; call reset_kv_cache() first) or S = 1 (decode), as the
+        reference's src/model/disaggregated.py:307-375. The cache length
+        advances by S after the last layer, so calling every layer in order
+        is one forward step."""
+        S = hidden_states.shape[1]
+        out = self._one_layer(layer_idx, hidden_states, self.kv_cache.seq_len,
+                              attention_mask if S > 1 else None)
+        if use_cache and layer_idx == self.num_layers - 1:
+            self.kv_cache.advance(S)
+        return out
 
     def _make_causal_mask(self, batch_size: int, query_len: int, key_len: int) -> torch.Tensor:
         return additive_causal_mask(batch_size, query_len, key_len, self.device, self.dtype)

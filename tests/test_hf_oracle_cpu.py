@@ -130,3 +130,38 @@ def test_forward_prefill_and_decode_shapes_match_hf(models):
         ref2 = hf(torch.cat([ids, nxt], 1)).logits[:, -1:].float()
     assert step.shape == ref2.shape
     assert (step - ref2).abs().max().item() < 1e-3 * max(1.0, ref2.abs().max().item())
+
+
+def _head(model, h):
+    aw = model.attention_worker
+    B, S, H = h.shape
+    return aw.forward_lm_head([h.reshape(B * S, H)], S, last_only=False).view(B, S, -1)
+
+
+def test_per_layer_entry_points_match_hf(models):
+    """forward_layer_sync (whole sequence, no cache) and
+    forward_layer_with_cache (prefill, then a decode token), layer by layer
+    from the embedding to the LM head, as the reference's per-layer path."""
+    hf, ours, ids = models
+    B, S = ids.shape
+    emb = lambda t: ours.attention_worker.embed(t).view(t.shape[0], t.shape[1], -1)  # noqa: E731
+    with torch.no_grad():
+        ref = hf(ids).logits.float()
+    h = emb(ids)
+    for l in range(ours.num_layers):
+        h = ours.forward_layer_sync(l, h)
+    got = _head(ours, h).float()
+    assert (got - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+    ours.reset_kv_cache()
+    h = emb(ids)
+    for l in range(ours.num_layers):
+        h = ours.forward_layer_with_cache(l, h)
+    assert ours.kv_cache.get_seq_length() == S
+    nxt = ref[:, -1].argmax(-1, keepdim=True)
+    h = emb(nxt)
+    for l in range(ours.num_layers):
+        h = ours.forward_layer_with_cache(l, h)
+    step = _head(ours, h).float()
+    with torch.no_grad():
+        ref2 = hf(torch.cat([ids, nxt], 1)).logits[:, -1:].float()
+    assert (step - ref2).abs().max().item() < 1e-3 * max(1.0, ref2.abs().max().item())
