@@ -82,3 +82,17 @@ class StoppingCriteria:
 
     def get_finished_mask(self) -> Optional[torch.Tensor]:
         return self._finished
+
+    def should_stop(self, input_ids: torch.Tensor, current_length: int) -> torch.Tensor:
+        """Per-sequence stop mask [B] from the ids so far: every sequence at
+        `max_length`, else the sequences whose last id is EOS (the reference's
+        stateless check, src/utils/sampling.py:160-186)."""
+        B = input_ids.shape[0]
+        if current_length >= self.max_length:
+            return torch.ones(B, dtype=torch.bool, device=input_ids.device)
+        if self.eos_token_id is None:
+            return torch.zeros(B, dtype=torch.bool, device=input_ids.device)
+        return input_ids[:, -1] == self.eos_token_id
+
+    def all_stopped(self, input_ids: torch.Tensor, current_length: int) -> bool:
+        return bool(self.should_stop(input_ids, current_length).all())

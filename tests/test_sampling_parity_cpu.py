@@ -59,3 +59,14 @@ def test_seeded_sampling_and_greedy(ref, temperature, top_k, top_p):
     assert torch.equal(a, b)
     assert torch.equal(ours.sample_next_token(x, do_sample=False),
                        ref.sample_next_token(x, do_sample=False))
+
+
+def test_stopping_criteria(ref):
+    ids = torch.tensor([[5, 9, 2], [5, 9, 7], [1, 1, 2]])
+    for eos in (None, 2, 7):
+        for cur in (3, 9, 10, 11):
+            a = ours.StoppingCriteria(10, eos).should_stop(ids, cur)
+            b = ref.StoppingCriteria(10, eos).should_stop(ids, cur)
+            assert torch.equal(a, b), (eos, cur)
+            assert ours.StoppingCriteria(10, eos).all_stopped(ids, cur) == \
+                ref.StoppingCriteria(10, eos).all_stopped(ids, cur)
