@@ -309,6 +309,9 @@ def run_inference_demo(args) -> None:
                                   timeout_ms=args.comm_timeout_ms)
     logger.info(f"[{ctx.role.upper()}] model_type={model.model_type}, moe={model.is_moe}, "
                 f"router={model.has_router}, comm={model.comm_impl}")
+    if args.verbose:
+        from .utils.profiler import print_memory_stats
+        print_memory_stats()
     ctx.barrier()
     if args.warmup_p2p:
         w = ctx.warmup(num_rounds=args.warmup_rounds)
@@ -391,6 +394,9 @@ def run_generation_demo(args) -> None:
                                   random_init=args.random_init or None, seed=args.seed,
                                   num_micro_batches=args.num_micro_batches,
                                   timeout_ms=args.comm_timeout_ms)
+    if args.verbose:
+        from .utils.profiler import print_memory_stats
+        print_memory_stats()
     ctx.barrier()
     if args.warmup_p2p:
         w = ctx.warmup(num_rounds=args.warmup_rounds)

@@ -51,6 +51,18 @@ def is_cuda() -> bool:
     return DEVICE_TYPE == "cuda"
 
 
+is_available = is_cuda  # the reference's name
+
+
+def device_module():
+    """torch.cuda, or None on the CPU backend."""
+    return torch.cuda if is_cuda() else None
+
+
+def current_device_str(local_rank: int = 0) -> str:
+    return f"cuda:{local_rank}" if is_cuda() else "cpu"
+
+
 def device_count() -> int:
     return torch.cuda.device_count() if is_cuda() else 0
 
@@ -91,6 +103,20 @@ def stream_context(stream):
 def empty_cache() -> None:
     if is_cuda():
         torch.cuda.empty_cache()
+
+
+def memory_allocated(device=None) -> int:
+    """Bytes held by tensors (0 on the CPU backend)."""
+    return torch.cuda.memory_allocated(device) if is_cuda() else 0
+
+
+def max_memory_allocated(device=None) -> int:
+    return torch.cuda.max_memory_allocated(device) if is_cuda() else 0
+
+
+def memory_reserved(device=None) -> int:
+    """Bytes held by the caching allocator (0 on the CPU backend)."""
+    return torch.cuda.memory_reserved(device) if is_cuda() else 0
 
 
 def memory_allocated_gb() -> float:

@@ -74,6 +74,17 @@ class TimingEvent:
         return d
 
 
+@dataclass
+class LayerTiming:
+    """Per-micro-batch times of one layer in ms (the reference's container,
+    src/utils/timing.py:81-89)."""
+    layer_idx: int
+    attn_compute: List[float] = field(default_factory=list)
+    ffn_compute: List[float] = field(default_factory=list)
+    send_time: List[float] = field(default_factory=list)
+    recv_wait: List[float] = field(default_factory=list)
+
+
 _OPTIONAL_KEYS = (
     "prefill_seq_len", "actual_prompt_len", "prefill_ms", "decode_loop_ms", "decode_steps",
     "decode_tpot_ms", "timed_decode_step", "timed_decode_step_base", "timed_decode_step_note",
@@ -231,6 +242,11 @@ class TimingTracker:
         else:
             torch.cuda.synchronize()
 
+    def track(self, event_type: EventType, layer_idx: int, mb_idx: int):
+        """Context manager around one span: host perf_counter start and end,
+        recorded as an event (the reference's sync-mode helper)."""
+        return _TimingContext(self, event_type, layer_idx, mb_idx)
+
     def mark_start(self, event_type: EventType, layer_idx: int, mb_idx: int,
                    stream: Optional["torch.cuda.Stream"] = None) -> None:
         key = (event_type, layer_idx, mb_idx)
@@ -324,6 +340,24 @@ class TimingTracker:
         else:
             self.timing.total_time_ms = (time.perf_counter() - self.start_time) * 1000
         return self.timing
+
+
+class _TimingContext:
+    def __init__(self, tracker: "TimingTracker", event_type: EventType, layer_idx: int,
+                 mb_idx: int):
+        self.tracker = tracker
+        self.event_type = event_type
+        self.layer_idx = layer_idx
+        self.mb_idx = mb_idx
+
+    def __enter__(self):
+        self.start_time = time.perf_counter()
+        return self
+
+    def __exit__(self, *exc) -> bool:
+        self.tracker.record_event(self.event_type, self.layer_idx, self.mb_idx,
+                                  self.start_time, time.perf_counter())
+        return False
 
 
 def merge_timings(attn: PipelineTiming, ffn: PipelineTiming) -> Dict[str, Any]:

@@ -137,3 +137,34 @@ def test_serial_baseline_resolution():
             a, b = ours.resolve_serial_baseline(c, m), ref.resolve_serial_baseline(c, m)
             assert (a.value_ms, a.unit, a.source, a.available) == \
                    (b.value_ms, b.unit, b.source, b.available), (c, m)
+
+
+def test_profiler_interface():
+    """utils/profiler.py against the reference's (src/utils/profiler.py):
+    the same names, signatures and statistics for the same recorded times."""
+    ref = _load("utils/profiler.py", "_ref_profiler")
+    from afd_demo_b200.utils import profiler as ours
+
+    a, b = ours.Profiler(), ref.Profiler()
+    for P in (a, b):
+        for v in (1.0, 2.5, 4.0):
+            P.record("a", v)
+        with P.timer("t", use_cuda=False):
+            pass
+    assert a.get_stats("a") == b.get_stats("a")
+    assert a.get_stats("missing") == b.get_stats("missing")
+    assert [ln.split("|")[:2] for ln in a.report().splitlines() if "|" in ln and "t " not in ln] == \
+           [ln.split("|")[:2] for ln in b.report().splitlines() if "|" in ln and "t " not in ln]
+    assert ours.TimingResult("x", 6.0, 3).avg_ms == ref.TimingResult("x", 6.0, 3).avg_ms
+    for T in (ours.Timer, ref.Timer):
+        with T("x") as t:
+            pass
+        assert t.elapsed_ms >= 0.0
+    calls = []
+
+    @ours.profile_function("f", use_cuda=False)
+    def f(x):
+        calls.append(x)
+        return x + 1
+
+    assert f(1) == 2 and calls == [1] and ours.get_profiler().get_stats("f")["count"] >= 1

@@ -340,3 +340,17 @@ def test_yaml_run_config(tmp_path):
     bad.write_text("pipeline:\n  not_a_flag: 1\n")
     with pytest.raises(ValueError):
         parse_args(["--config", str(bad)])
+
+
+def test_tracker_track_context_and_layer_timing():
+    from afd_demo_b200.utils.timing import EventType, LayerTiming, TimingTracker
+    tr = TimingTracker("attention", 2, 2, mode="sync")
+    with tr.track(EventType.ATTN_COMPUTE, 1, 0):
+        pass
+    pt = tr.finish()
+    ev = pt.to_dict()["events"]
+    assert [(e["type"], e["layer"], e["mb"]) for e in ev] == [("attn_compute", 1, 0)]
+    assert ev[0]["end"] >= ev[0]["start"] >= 0.0
+    lt = LayerTiming(3)
+    lt.attn_compute.append(1.5)
+    assert lt.layer_idx == 3 and lt.ffn_compute == []
