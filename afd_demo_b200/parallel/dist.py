@@ -114,6 +114,11 @@ class DistributedContext:
     def initialized(self) -> bool:
         return self._ready
 
+    is_initialized = initialized  # the reference's name
+
+    def _config_from_env(self) -> DistributedConfig:
+        return config_from_env()
+
     # ------------------------------------------------------------------
     @property
     def rank(self) -> int:
