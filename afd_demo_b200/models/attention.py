@@ -43,6 +43,7 @@ class AttentionWorker:
         self.cache = KVCache(cfg.num_hidden_layers, max_batch, cfg.num_key_value_heads, max_seq,
                              cfg.head_dim, self.device, dtype)
         self.tracker = None  # optional TimingTracker for sub-stage events
+        self.layers = [AttentionLayer(self, l) for l in range(self.num_layers)]
         # (lo, hi) visible key range per cache row for the current prefill
         # (padding masks), set by the model around one forward; None = causal only
         self.key_range = None
@@ -63,7 +64,7 @@ class AttentionWorker:
     def forward_attention_layer(self, layer_idx: int, x_parts: Sequence[torch.Tensor],
                                 batch_offset: int, q_len: int, start_pos: Optional[int] = None,
                                 sink=None, out: Optional[torch.Tensor] = None,
-                                wait=None) -> torch.Tensor:
+                                wait=None, add_residual: bool = True) -> torch.Tensor:
         """One attention block for the micro-batch whose sequences occupy cache
         rows [batch_offset, batch_offset + T // q_len). `x_parts` are the
         layer inputs (the F2A partials); returns h = x + o_proj(attn). `wait`
@@ -87,6 +88,8 @@ class AttentionWorker:
                                        cfg.rms_norm_eps)
             o = ops.attention(q, k_l, v_l, batch_offset, q_len, start, self.cache.pos_dev,
                               self.key_range)
+        if not add_residual:  # attention output alone (per-layer view below)
+            return ops.linear(o, lw.w_o, out=out)
         if sink is not None:
             return ops.linear(o, lw.w_o, residual=x, out=out, **sink.gemm_kwargs())
         return ops.linear(o, lw.w_o, residual=x, out=out)
@@ -104,3 +107,43 @@ class AttentionWorker:
             parts = [p.view(-1, q_len, H)[:, -1].contiguous() for p in parts]
         _, xn = ops.sum_rmsnorm(parts, self.w.final_norm, self.cfg.rms_norm_eps)
         return ops.linear(xn, self.w.lm_head)
+
+
+class AttentionLayer:
+    """Per-layer view of an AttentionWorker with the reference's call
+    (src/model/attention_worker.py:24-155): input RMSNorm, q/k/v projection,
+    q/k RMSNorm, RoPE, KV-cache append, causal attention, o_proj. Returns
+    (attn_output, residual) as [B, S, H] each, plus the KV cache when
+    `use_cache` (keys/values appended at the cache's current length, which
+    the caller advances, e.g. ``KVCache.advance``). Without `use_cache` the
+    sequence sits at positions 0..S-1 and the layer's cache rows are scratch.
+    Positions come from the cache length, so `position_ids` and
+    `position_embeddings` are accepted for the signature only; an
+    `attention_mask` may be a [B, S] padding mask."""
+
+    def __init__(self, worker: "AttentionWorker", layer_idx: int):
+        self.worker = worker
+        self.layer_idx = layer_idx
+
+    def forward(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
+                past_key_value=None, output_attentions: bool = False, use_cache: bool = False,
+                position_embeddings=None):
+        w = self.worker
+        B, S, H = hidden_states.shape
+        x = hidden_states.reshape(B * S, H).to(w.device, w.dtype)
+        start = w.cache.seq_len if use_cache else 0
+        if not use_cache and w.cache.seq_len != 0:
+            raise ValueError("use_cache=False needs an empty KV cache (its rows are scratch)")
+        from ..parallel.micro_batch import key_ranges_from_mask
+        w.key_range = (key_ranges_from_mask(attention_mask.to(w.device))
+                       if attention_mask is not None and attention_mask.dim() == 2 and S > 1
+                       else None)
+        try:
+            o = w.forward_attention_layer(self.layer_idx, [x], 0, S, start_pos=start,
+                                          add_residual=False)
+        finally:
+            w.key_range = None
+        out = (o.view(B, S, H), x.view(B, S, H))
+        return out + (w.cache,) if use_cache else out
+
+    __call__ = forward

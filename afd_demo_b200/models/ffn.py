@@ -21,13 +21,14 @@ residual, so the attention side's sum over FFN ranks is the layer output.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Optional
 
 import torch
 
 from .. import ops
 from ..config import ModelConfig
-from ..utils.timing import EventType
+from ..utils.timing import EventType, TimingTracker
 from .weights import FFNWeights
 
 
@@ -41,6 +42,7 @@ class FFNWorker:
         self.expert_range = weights.expert_range
         self.supports_moe_timing = cfg.is_moe
         self.tracker = None  # optional TimingTracker for router / experts spans
+        self.layers = [FFNLayer(self, l) for l in range(self.num_layers)]
 
     def _mark(self, start: bool, et: EventType, l: int, mb: int):
         if self.tracker is not None:
@@ -74,3 +76,58 @@ class FFNWorker:
                            tracker_marks=lambda start, name: self._mark(start, stage[name],
                                                                         layer_idx, mb_idx),
                            wait=wait, **kw)
+
+
+@dataclass
+class FFNStageTiming:
+    """Host-observed FFN stage times in seconds (the reference's
+    src/model/ffn_worker.py:23-28)."""
+    router_s: float = 0.0
+    experts_s: float = 0.0
+    shared_or_dense_s: float = 0.0
+
+
+class FFNLayer:
+    """Per-layer view of an FFNWorker with the reference's call
+    (src/model/ffn_worker.py:31-122): h (+ residual, when given separately)
+    -> h + moe(post_attention_norm(h)), [B, S, H] or [T, H]. With
+    `return_timing`, the router and expert stages are timed on the host with
+    a device synchronisation around each (a debugging aid, as in the
+    reference)."""
+
+    def __init__(self, worker: "FFNWorker", layer_idx: int):
+        self.worker = worker
+        self.layer_idx = layer_idx
+
+    @property
+    def is_sparse_moe(self) -> bool:
+        return self.worker.w.layers[self.layer_idx].w_router is not None
+
+    def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                output_device=None, return_timing: bool = False):
+        w = self.worker
+        shape = hidden_states.shape
+        h = hidden_states if residual is None else residual + hidden_states
+        h = h.reshape(-1, shape[-1]).to(w.device, w.dtype)
+        saved = w.tracker
+        tr = TimingTracker("ffn", w.num_layers, 1, mode="sync") if return_timing else saved
+        w.tracker = tr
+        try:
+            out = w.forward_ffn_layer(self.layer_idx, h, add_residual=True).view(shape)
+        finally:
+            w.tracker = saved
+        if output_device is not None:
+            out = out.to(output_device)
+        if not return_timing:
+            return out
+        st = FFNStageTiming()
+        for ev in tr.finish().events:
+            if ev.event_type == EventType.MOE_ROUTER.value:
+                st.router_s += ev.duration_ms / 1e3
+            elif ev.event_type == EventType.MOE_EXPERTS.value:
+                st.experts_s += ev.duration_ms / 1e3
+            elif ev.event_type == EventType.MOE_SHARED_OR_DENSE.value:
+                st.shared_or_dense_s += ev.duration_ms / 1e3
+        return out, st
+
+    __call__ = forward

@@ -165,3 +165,28 @@ def test_per_layer_entry_points_match_hf(models):
     with torch.no_grad():
         ref2 = hf(torch.cat([ids, nxt], 1)).logits[:, -1:].float()
     assert (step - ref2).abs().max().item() < 1e-3 * max(1.0, ref2.abs().max().item())
+
+
+def test_layer_views_match_hf_and_fused_path(models):
+    """AttentionLayer / FFNLayer (the reference's per-layer modules): the
+    FFN layer equals HF's post-attention norm + MoE block + residual; the
+    attention layer's (attn_output + residual) equals the fused layer
+    output."""
+    hf, ours, ids = models
+    B, S = ids.shape
+    aw, fw = ours.attention_worker, ours.ffn_worker
+    x = aw.embed(ids).view(B, S, -1)
+    blk = hf.model.layers[0]
+    with torch.no_grad():
+        ref_ffn = x + blk.mlp(blk.post_attention_layernorm(x))
+    got, st = fw.layers[0](x, return_timing=True)
+    assert (got - ref_ffn).abs().max().item() < 1e-3 * max(1.0, ref_ffn.abs().max().item())
+    assert fw.layers[0].is_sparse_moe and st.router_s >= 0.0 and st.experts_s > 0.0
+    ours.reset_kv_cache()
+    attn, res = aw.layers[0](x)
+    ours.reset_kv_cache()
+    h = aw.forward_attention_layer(0, [x.reshape(B * S, -1)], 0, S, start_pos=0)
+    torch.testing.assert_close((attn + res).reshape(B * S, -1), h, rtol=1e-5, atol=1e-5)
+    ours.reset_kv_cache()
+    attn2, res2, cache = aw.layers[0](x, use_cache=True)
+    assert cache is aw.cache and torch.equal(attn2, attn) and torch.equal(res2, res)
