@@ -354,3 +354,17 @@ def test_tracker_track_context_and_layer_timing():
     lt = LayerTiming(3)
     lt.attn_compute.append(1.5)
     assert lt.layer_idx == 3 and lt.ffn_compute == []
+
+
+def test_every_switch_is_documented():
+    """Each AFD_* environment variable the code reads has a README line."""
+    import re
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    names = set()
+    for p in list((root / "afd_demo_b200").rglob("*.py")) + [root / "bench.py"]:
+        names |= set(re.findall(r'environ(?:\.get)?\(?\[?"(AFD_[A-Z0-9_]+)"', p.read_text()))
+    for p in (root / "csrc").glob("*"):
+        names |= set(re.findall(r'getenv\("(AFD_[A-Z0-9_]+)"', p.read_text()))
+    readme = (root / "README.md").read_text()
+    assert names and not [n for n in sorted(names) if n not in readme]
