@@ -34,8 +34,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 METRIC = ("Qwen3-30B-A3B decode TPOT ms & prefill TTFT ms, DBO vs serial, at 1/2/4/8 B200")
-# published cross-layer decode TPOT (ms) of the reference at seq 256, by batch
-# (4xV100; BASELINE.md decode table): value / (1000 * b / TPOT)
+# published cross-layer decode TPOT (ms) of the reference at seq 256, by batch,
+# measured on 4xV100 (reference results/baseline_audit.csv, decode-dbo-crosslayer
+# rows); vs_baseline = value / (1000 * b / TPOT)
 REF_XL_TPOT_S256 = {2: 243.7, 4: 417.1, 8: 502.9, 16: 739.4, 32: 884.2, 64: 1274.1,
                     96: 1596.4, 128: 1757.4, 192: 1873.6}
 
