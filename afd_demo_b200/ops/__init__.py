@@ -3,7 +3,7 @@ PyTorch statement (``torch_ref``) on CPU tensors.
 
 There is no silent fallback on the GPU: a CUDA tensor with the extension
 missing raises. The extension is ``afd_demo_b200/_C*.so`` built in place by
-``python setup.py build_ext --inplace`` (``__graft_entry__.build()``).
+``python setup.py build_ext --inplace`` (or the build entry point at the repository root).
 """
 
 from __future__ import annotations
@@ -64,7 +64,7 @@ def ext():
     if _C is None:
         try:
             from .. import _C as mod  # type: ignore
-        except ImportError as e:  # pragma: no cover - exercised on a box without a build
+        except ImportError as e:  # pragma: no cover - exercised where the extension is not built
             raise RuntimeError(
                 "afd_demo_b200._C is not built: run `python setup.py build_ext --inplace`") from e
         _C = _Counted(mod)

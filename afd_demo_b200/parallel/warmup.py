@@ -5,7 +5,7 @@ Reference: ``warmup_p2p`` (src/distributed/warmup.py:11-96): a few rounds of
 warm latency. Here every attention rank exchanges with every FFN rank, on the
 world group and on any extra (directional) groups, and latencies are taken
 with a device synchronize only on CUDA (the reference calls
-``torch.cuda.synchronize`` unconditionally, which fails on a CPU box).
+``torch.cuda.synchronize`` unconditionally, which fails without a GPU).
 """
 
 from __future__ import annotations

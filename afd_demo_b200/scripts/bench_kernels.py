@@ -9,7 +9,7 @@ reads them from HBM (the set of copies is larger than the 126 MB L2), as the
 48 distinct layers of the model do. Achieved bandwidth = algorithmic bytes /
 time; achieved FLOP rate = algorithmic FLOPs / time; fractions are of the
 measured peaks in MEASURED_PEAKS.json when present (HBM copy bandwidth and
-cuBLAS bf16 burst throughput), else of the pool's fallback figures (6.65 TB/s,
+cuBLAS bf16 burst throughput), else of earlier B200 measurements (6.65 TB/s,
 1.59 PFLOP/s).
 
     python -m afd_demo_b200.scripts.bench_kernels [--tokens 16,32,64,128] [--json out.json]

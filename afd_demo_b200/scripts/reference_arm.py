@@ -1,6 +1,6 @@
 """Reference arm of ``bench.py``: the unmodified reference (afd_demo's ``src``
 package, copied verbatim into ``baseline/_ref``) run through its own public
-API on the same box, metric and config as our arm.
+API on the same machine, metric and config as our arm.
 
 What runs is the reference's stock code path and nothing of this package:
 
@@ -13,7 +13,7 @@ What runs is the reference's stock code path and nothing of this package:
   ``_last_generation_metrics`` give prefill ms and decode TPOT.
 
 The only shared piece is the input data: a random-init Qwen3-30B-A3B
-checkpoint in the HF safetensors layout, written once per box by this
+checkpoint in the HF safetensors layout, written once per machine by this
 package's checkpoint writer (data preparation, outside every timed region)
 and reused by later runs.
 

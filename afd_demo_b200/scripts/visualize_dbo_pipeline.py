@@ -2,7 +2,7 @@
 """Four-lane Gantt chart (A, A->F, F, F->A) of a DBO run as a PNG.
 
 Reference: scripts/visualize_dbo_pipeline.py (matplotlib). This one draws
-with ``afd_demo_b200.utils.png`` (no plotting library on the box).
+with ``afd_demo_b200.utils.png`` (no plotting library needed).
 
 Clock alignment: attention and FFN events come from different clocks (two
 processes, or two trackers). The FFN lane is shifted by the smallest
