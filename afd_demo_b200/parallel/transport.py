@@ -288,12 +288,8 @@ class PeerTransport(Transport):
         esz = torch.tensor([], dtype=dtype).element_size()
         self.Ta = max_tokens_per_mb_attn
         self.Tall = max_tokens_per_mb
-        fa = _align(4 * num_mb * max(self.n_attn, self.n_ffn), 4096)
-        ffn_slot = _align(self.Tall * hidden * esz)
-        self.ffn_layout = _Layout(fa, fa, ffn_slot, 0, fa + num_mb * ffn_slot)
-        attn_slot = _align(self.Ta * hidden * esz)
-        self.attn_layout = _Layout(fa, fa, self.n_ffn * attn_slot, attn_slot,
-                                   fa + num_mb * self.n_ffn * attn_slot)
+        self.ffn_layout, self.attn_layout = self.make_layouts(
+            self.n_attn, self.n_ffn, num_mb, self.Ta, self.Tall, hidden, esz)
         my_layout = self.attn_layout if ctx.role == "attention" else self.ffn_layout
         self.region = self.C.ipc_alloc(my_layout.total, device.index if device.index is not None
                                        else torch.cuda.current_device())
@@ -314,6 +310,20 @@ class PeerTransport(Transport):
             self.peer_base[r] = int(self.C.ipc_open(allh[r]))
         torch.cuda.synchronize()
         dist.barrier(device_ids=[ctx.local_rank])
+
+    @staticmethod
+    def make_layouts(n_attn: int, n_ffn: int, num_mb: int, tokens_attn: int, tokens_all: int,
+                     hidden: int, esz: int):
+        """(FFN region, attention region) layouts: flags first (one int32 per
+        micro-batch and peer, 4 KiB aligned), then the data slots (256-byte
+        aligned): an FFN rank holds one slot per micro-batch for every
+        attention rank's rows, an attention rank one slot per micro-batch and
+        FFN rank."""
+        fa = _align(4 * num_mb * max(n_attn, n_ffn), 4096)
+        ffn_slot = _align(tokens_all * hidden * esz)
+        attn_slot = _align(tokens_attn * hidden * esz)
+        return (_Layout(fa, fa, ffn_slot, 0, fa + num_mb * ffn_slot),
+                _Layout(fa, fa, n_ffn * attn_slot, attn_slot, fa + num_mb * n_ffn * attn_slot))
 
     # address helpers ----------------------------------------------------
     def _ffn_data(self, base: int, m: int) -> int:

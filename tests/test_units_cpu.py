@@ -368,3 +368,50 @@ def test_every_switch_is_documented():
         names |= set(re.findall(r'getenv\("(AFD_[A-Z0-9_]+)"', p.read_text()))
     readme = (root / "README.md").read_text()
     assert names and not [n for n in sorted(names) if n not in readme]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_region_addresses_disjoint(world):
+    """Address arithmetic of the fused transport's peer regions: every flag
+    and data slot of every (micro-batch, peer) lies inside its region, flags
+    precede data, slots never overlap, and each attention rank's rows land in
+    its own segment of the FFN slot."""
+    from afd_demo_b200.config import Topology
+    from afd_demo_b200.parallel.micro_batch import make_plan
+    from afd_demo_b200.parallel.transport import PeerTransport
+
+    topo = Topology.for_world(world)
+    n_attn, n_ffn, H, esz, nmb = len(topo.attn_ranks()), len(topo.ffn_ranks()), 64, 2, 2
+    B, S = 8 * n_attn, 5
+    plan = make_plan(topo, B, nmb, S)
+    Tall = max(s.tokens for s in plan.ffn_slots)
+    Ta = max(s.tokens for row in plan.attn_slots for s in row)
+    ffn_l, attn_l = PeerTransport.make_layouts(n_attn, n_ffn, nmb, Ta, Tall, H, esz)
+    t = PeerTransport.__new__(PeerTransport)
+    t.n_attn, t.n_ffn, t.H, t.ffn_layout, t.attn_layout = n_attn, n_ffn, H, ffn_l, attn_l
+    base = 1 << 40
+    spans = []
+    for m in range(nmb):
+        for a in range(n_attn):
+            f = t._ffn_flag(base, m, a)
+            assert base <= f < base + ffn_l.data_offset
+            spans.append((f, f + 4))
+        lo = t._ffn_data(base, m)
+        seg = plan.ffn_slots[m].seg_offsets
+        for a in range(n_attn):
+            r0 = seg[a]
+            r1 = seg[a + 1] if a + 1 < n_attn else plan.ffn_slots[m].tokens
+            spans.append((lo + r0 * H * esz, lo + r1 * H * esz))
+        assert lo + plan.ffn_slots[m].tokens * H * esz <= base + ffn_l.total
+    for m in range(nmb):
+        for f in range(n_ffn):
+            fl = t._attn_flag(base + (1 << 36), m, f)
+            assert base + (1 << 36) <= fl < base + (1 << 36) + attn_l.data_offset
+            d = t._attn_data(base + (1 << 36), m, f)
+            assert d + Ta * H * esz <= base + (1 << 36) + attn_l.total
+            spans.append((fl, fl + 4))
+            spans.append((d, d + Ta * H * esz))
+    spans = [s for s in spans if s[1] > s[0]]
+    spans.sort()
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 <= b0, "overlapping peer-region spans"
