@@ -131,3 +131,44 @@ def test_dropped_message_times_out_instead_of_hanging():
     assert all(res[r]["error"] is not None for r in (0, 1)), res
     assert "AFDCommTimeout" in (res[0]["error"], res[1]["error"]), res
     assert max(res[r]["seconds"] for r in (0, 1)) < 30, res
+
+
+def _lonely_rank(port, out_dir, timeout_s):
+    from afd_demo_b200.parallel.dist import DistributedConfig, get_distributed_context
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cpu")
+    t0 = time.monotonic()
+    res = {"error": None}
+    try:
+        get_distributed_context().initialize(DistributedConfig(
+            world_size=2, rank=0, backend="gloo", master_addr="127.0.0.1",
+            master_port=str(port), timeout_s=timeout_s))
+    except BaseException as e:  # recorded for the test
+        res["error"] = type(e).__name__
+    res["seconds"] = time.monotonic() - t0
+    with open(os.path.join(out_dir, "r0.json"), "w") as f:
+        json.dump(res, f)
+    os._exit(0)
+
+
+def test_rank_that_never_joins_fails_the_rendezvous():
+    """A peer that never starts: the lone rank's rendezvous ends with an
+    error within the process-group timeout instead of waiting forever."""
+    out = tempfile.mkdtemp(prefix="afd_fault_")
+    p = mp.get_context("spawn").Process(target=_lonely_rank, args=(_free_port(), out, 5.0))
+    p.start()
+    p.join(timeout=90)
+    alive = p.is_alive()
+    if alive:
+        p.kill()
+    assert not alive, "the lone rank waited for its peer forever"
+    res = json.load(open(os.path.join(out, "r0.json")))
+    assert res["error"] is not None and res["seconds"] < 60, res
+
+
+def test_slow_rank_is_not_reported_as_failed():
+    """A rank delayed by 200 ms per step (well inside the failure bounds):
+    both ranks finish without an error."""
+    res = _launch(2, "delay_ms:200:1")
+    assert res[0]["error"] is None and res[1]["error"] is None, res
