@@ -110,58 +110,24 @@ def _norm_init(n: int, name: str, seed: int, device, dtype) -> torch.Tensor:
 def random_attention_weights(cfg: ModelConfig, seed: int = 0, device="cpu",
                              dtype=torch.bfloat16) -> AttentionWeights:
     std = cfg.initializer_range
-    H, Q, KV, D = cfg.hidden_size, cfg.q_size, cfg.kv_size, cfg.head_dim
+    H = cfg.hidden_size
     aw = AttentionWeights(
         embed=_randn((cfg.vocab_size, H), "embed", seed, 1.0, device, dtype),
         final_norm=_norm_init(H, "final_norm", seed, device, dtype),
         lm_head=_randn((cfg.vocab_size, H), "lm_head", seed, std, device, dtype),
     )
     for l in range(cfg.num_hidden_layers):
-        p = f"layers.{l}."
-        aw.layers.append(
-            AttentionLayerWeights(
-                in_norm=_norm_init(H, p + "in_norm", seed, device, dtype),
-                w_qkv=torch.cat(
-                    [
-                        _randn((Q, H), p + "q", seed, std, device, dtype),
-                        _randn((KV, H), p + "k", seed, std, device, dtype),
-                        _randn((KV, H), p + "v", seed, std, device, dtype),
-                    ]
-                ),
-                q_norm=_norm_init(D, p + "q_norm", seed, device, dtype),
-                k_norm=_norm_init(D, p + "k_norm", seed, device, dtype),
-                w_o=_randn((H, Q), p + "o", seed, std, device, dtype),
-            )
-        )
+        aw.layers.append(_layer_only_attention(cfg, l, seed, dtype, device))
     return aw
 
 
 def random_ffn_weights(cfg: ModelConfig, expert_range: Optional[range] = None, seed: int = 0,
                        device="cpu", dtype=torch.bfloat16) -> FFNWeights:
-    std = cfg.initializer_range
-    H, I, E = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts
     if expert_range is None:
-        expert_range = range(E)
+        expert_range = range(cfg.num_experts)
     fw = FFNWeights(expert_range=expert_range)
     for l in range(cfg.num_hidden_layers):
-        p = f"layers.{l}."
-        lw = FFNLayerWeights(post_norm=_norm_init(H, p + "post_norm", seed, device, dtype))
-        if cfg.is_sparse_layer(l):
-            lw.w_router = _randn((E, H), p + "router", seed, std, device, dtype)
-            gu = torch.empty(len(expert_range), 2 * I, H, device=device, dtype=dtype)
-            dn = torch.empty(len(expert_range), H, I, device=device, dtype=dtype)
-            for i, e in enumerate(expert_range):
-                gu[i, :I] = _randn((I, H), p + f"e{e}.gate", seed, std, device, dtype)
-                gu[i, I:] = _randn((I, H), p + f"e{e}.up", seed, std, device, dtype)
-                dn[i] = _randn((H, I), p + f"e{e}.down", seed, std, device, dtype)
-            lw.w_gate_up, lw.w_down, lw.expert_start = gu, dn, expert_range.start
-        else:
-            DI = cfg.intermediate_size
-            lw.w_dense_gate_up = torch.cat(
-                [_randn((DI, H), p + "dense.gate", seed, std, device, dtype),
-                 _randn((DI, H), p + "dense.up", seed, std, device, dtype)])
-            lw.w_dense_down = _randn((H, DI), p + "dense.down", seed, std, device, dtype)
-        fw.layers.append(lw)
+        fw.layers.append(_layer_only_ffn(cfg, l, seed, dtype, device, expert_range))
     return fw
 
 
@@ -262,37 +228,43 @@ def write_random_checkpoint(path: str, cfg: ModelConfig, seed: int = 0,
 
 def _layer_only_attention(cfg: ModelConfig, l: int, seed: int, dtype,
                           device="cpu") -> AttentionLayerWeights:
+    """One layer's attention weights; each tensor is one seeded draw (q, k and
+    v projections together), so initialisation takes a few launches per
+    layer."""
     std = cfg.initializer_range
     H, Q, KV, D = cfg.hidden_size, cfg.q_size, cfg.kv_size, cfg.head_dim
     p = f"layers.{l}."
     return AttentionLayerWeights(
         in_norm=_norm_init(H, p + "in_norm", seed, device, dtype),
-        w_qkv=torch.cat([_randn((Q, H), p + "q", seed, std, device, dtype),
-                         _randn((KV, H), p + "k", seed, std, device, dtype),
-                         _randn((KV, H), p + "v", seed, std, device, dtype)]),
+        w_qkv=_randn((Q + 2 * KV, H), p + "qkv", seed, std, device, dtype),
         q_norm=_norm_init(D, p + "q_norm", seed, device, dtype),
         k_norm=_norm_init(D, p + "k_norm", seed, device, dtype),
         w_o=_randn((H, Q), p + "o", seed, std, device, dtype),
     )
 
 
-def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype, device="cpu") -> FFNLayerWeights:
-    # same per-tensor seeds as random_ffn_weights, one layer at a time
+def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype, device="cpu",
+                    expert_range: Optional[range] = None) -> FFNLayerWeights:
+    """One layer's FFN weights. The experts' gate/up and down projections are
+    one seeded draw each over all experts of the layer, of which this rank
+    keeps `expert_range`: every expert-parallel split therefore holds the
+    same values as one GPU holding all experts."""
     std = cfg.initializer_range
     H, I, E = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts
+    er = range(E) if expert_range is None else expert_range
     p = f"layers.{l}."
     lw = FFNLayerWeights(post_norm=_norm_init(H, p + "post_norm", seed, device, dtype))
     if cfg.is_sparse_layer(l):
         lw.w_router = _randn((E, H), p + "router", seed, std, device, dtype)
-        lw.w_gate_up = torch.stack([
-            torch.cat([_randn((I, H), p + f"e{e}.gate", seed, std, device, dtype),
-                       _randn((I, H), p + f"e{e}.up", seed, std, device, dtype)]) for e in range(E)])
-        lw.w_down = torch.stack([_randn((H, I), p + f"e{e}.down", seed, std, device, dtype)
-                                 for e in range(E)])
+        gu = _randn((E, 2 * I, H), p + "experts.gate_up", seed, std, device, dtype)
+        dn = _randn((E, H, I), p + "experts.down", seed, std, device, dtype)
+        if len(er) != E:  # keep only this rank's experts (no view of the full draw)
+            gu = gu[er.start:er.stop].clone()
+            dn = dn[er.start:er.stop].clone()
+        lw.w_gate_up, lw.w_down, lw.expert_start = gu, dn, er.start
     else:
         DI = cfg.intermediate_size
-        lw.w_dense_gate_up = torch.cat([_randn((DI, H), p + "dense.gate", seed, std, device, dtype),
-                                        _randn((DI, H), p + "dense.up", seed, std, device, dtype)])
+        lw.w_dense_gate_up = _randn((2 * DI, H), p + "dense.gate_up", seed, std, device, dtype)
         lw.w_dense_down = _randn((H, DI), p + "dense.down", seed, std, device, dtype)
     return lw
 

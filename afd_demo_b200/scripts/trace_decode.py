@@ -14,11 +14,19 @@ exact for the serial schedule, which runs on one stream; with two streams
 (co-located DBO) kernels of the two micro-batches interleave and the per-name
 split is only indicative, but the step total still holds.
 
+With ``--standalone-waits`` every receive is its own one-CTA wait kernel
+instead of being folded into the consuming kernel (the RMSNorm on an
+attention rank, the MoE gate on an FFN rank), so the summary separates the
+time a rank spends waiting for its peers (F2A waits on attention ranks, A2F
+waits on FFN ranks) from its kernels' own time. The extra launch per receive
+adds about a microsecond per layer and micro-batch.
+
 This is a diagnostic: profiler timings are not benchmark numbers (bench.py
 times with CUDA events and no profiler).
 
     torchrun --nproc-per-node N -m afd_demo_b200.scripts.trace_decode \
-        --schedule dbo|serial [--steps 2] [--out results/trace] [--summary]
+        --schedule dbo|serial [--steps 2] [--out results/trace] [--summary] \
+        [--standalone-waits] [--attn-gpus A]
 """
 
 from __future__ import annotations
@@ -34,8 +42,13 @@ if __package__ in (None, ""):
     sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
 
 
+WAIT_KERNEL = "wait_flags_kernel"
+
+
 def summarize(path: str) -> str:
-    """Critical-path time per kernel name over the last recorded step."""
+    """Critical-path time per kernel name over the last recorded step, and
+    the step split into peer waits (stand-alone wait kernels), kernel time
+    and idle gaps, per layer."""
     d = json.load(open(path))
     ev = sorted(d["events"], key=lambda e: e[1])
     if not ev:
@@ -55,7 +68,31 @@ def summarize(path: str) -> str:
     for k, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
         out.append(f"  {k:60s} {c:4d} {t / 1e3:7.3f} ms {100 * t / total:5.1f}%  "
                    f"{t / c:7.1f} us each")
+    wait = sum(t for k, (c, t) in agg.items() if WAIT_KERNEL in k)
+    layers = max(1, int(d.get("layers", 1)))
+    peer = "F2A" if d["role"] == "attention" else ("A2F" if d["role"] == "ffn" else "peer")
+    busy = _busy_union(last)
+    span = last[-1][1] + last[-1][2] - min(e[1] for e in last)
+    out.append(f"  split per layer ({layers} layers): {peer} waits {wait / layers:7.1f} us, "
+               f"kernels {(total - wait) / layers:7.1f} us; GPU busy {100 * busy / span:5.1f}% "
+               f"of the step")
     return "\n".join(out)
+
+
+def _busy_union(ev) -> float:
+    """Time covered by at least one kernel (overlaps counted once)."""
+    iv = sorted((s, s + du) for _, s, du in ev)
+    tot, cur_s, cur_e = 0.0, None, None
+    for s, e in iv:
+        if cur_e is None or s > cur_e:
+            if cur_e is not None:
+                tot += cur_e - cur_s
+            cur_s, cur_e = s, e
+        else:
+            cur_e = max(cur_e, e)
+    if cur_e is not None:
+        tot += cur_e - cur_s
+    return tot
 
 
 def main(argv=None) -> int:
@@ -68,7 +105,15 @@ def main(argv=None) -> int:
     ap.add_argument("--model", default="qwen3-30b-a3b")
     ap.add_argument("--out", default="results/trace")
     ap.add_argument("--summary", action="store_true")
+    ap.add_argument("--standalone-waits", action="store_true",
+                    help="one wait kernel per receive (separates peer waits from kernel time)")
+    ap.add_argument("--attn-gpus", type=int, default=None,
+                    help="attention ranks (default: half the world)")
+    ap.add_argument("--comm-impl", default="auto", choices=["auto", "fused", "nccl"])
     a = ap.parse_args(argv)
+    if a.standalone_waits:
+        # read by the engine at import time
+        os.environ["AFD_DEFER_WAITS"] = "0"
 
     import torch
     from torch.profiler import ProfilerActivity, profile
@@ -85,14 +130,14 @@ def main(argv=None) -> int:
     torch.cuda.set_device(local)
     ctx = get_distributed_context()
     ctx.initialize(DistributedConfig(world_size=world, rank=rank, local_rank=local,
-                                     backend="nccl", timeout_s=120,
+                                     backend="nccl", timeout_s=120, n_attn=a.attn_gpus,
                                      master_addr=os.environ.get("MASTER_ADDR", "127.0.0.1"),
                                      master_port=os.environ.get("MASTER_PORT", "29500")))
     B, S = a.batch_per_gpu * world, a.seq
     m = DisaggregatedQwenModel.from_pretrained(
         a.model, device=f"cuda:{local}", dtype=torch.bfloat16,
         max_seq_len=S + a.warmup + a.steps + 8, max_batch_size=B, random_init=True, seed=0,
-        num_micro_batches=2)
+        num_micro_batches=2, comm_impl=a.comm_impl)
     ids = torch.randint(0, m.config.vocab_size, (B, S),
                         generator=torch.Generator().manual_seed(1234)).to(f"cuda:{local}")
     logits = m.run_forward(ids, "dbo", 2, crosslayer=True, reset_cache=True)
@@ -122,7 +167,9 @@ def main(argv=None) -> int:
     path = out / f"trace_{a.schedule}_r{rank}.json"
     role = "both" if (m.ctx.is_attention_node and m.ctx.is_ffn_node) else m.ctx.role
     path.write_text(json.dumps({"rank": rank, "role": role, "schedule": a.schedule,
-                                "steps": a.steps, "events": events}))
+                                "steps": a.steps, "layers": m.num_layers,
+                                "topology": m.topology.tag(), "batch": B,
+                                "standalone_waits": a.standalone_waits, "events": events}))
     if a.summary:
         print(summarize(str(path)), flush=True)
     m.release_graphs()

@@ -60,6 +60,12 @@ def parse():
                         "layer); the last one inside the NVTX range 'profile_step'; no JSON")
     p.add_argument("--layers", type=int, default=None,
                    help="override the layer count (profiling small cases only)")
+    p.add_argument("--attn-gpus", type=int, default=None,
+                   help="attention ranks for N > 1 (default N/2; the rest are FFN ranks)")
+    p.add_argument("--cells", choices=["auto", "none"], default="auto",
+                   help="auto: also measure the benchmark configs' cells that match this N "
+                        "(2 GPUs: serial b4 s128; 8 GPUs: prefill b32 s512, decode batch "
+                        "16/64/256) and, for N > 1, the decode step over NCCL isend/irecv")
     return p.parse_args()
 
 
@@ -116,6 +122,111 @@ def reference_arm(args, rank):
         print(json.dumps(line), flush=True)
 
 
+def measure_cells(model, args, B, S, T, local, world, timed, ctx):
+    """The benchmark configs' cells that match this GPU count, measured on
+    the same loaded model (device time, max over ranks):
+
+    * 2 GPUs: serial prefill + serial decode, batch 4, prompt 128, 20 tokens,
+      through ``generate`` (the reference's serial A/F baseline cell);
+    * 8 GPUs: prefill TTFT at batch 32, prompt 512, DBO (2 micro-batches)
+      and serial; cross-layer DBO and serial decode TPOT at batch 16, 64 and
+      256, prompt 256, 20 tokens, through ``generate``;
+    * N > 1: the headline decode step with the A2F/F2A hand-offs over NCCL
+      isend/irecv (the reference's mechanism) instead of the fused
+      peer-memory path, both run eagerly (the NCCL path keeps host-side work
+      handles and is not graph-captured), next to the fused path's eager
+      step, so the transport's own gain is visible.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from afd_demo_b200 import ops
+    from afd_demo_b200.parallel.transport import NcclTransport
+
+    dev = f"cuda:{local}"
+    V = model.config.vocab_size
+    out = {}
+
+    def mx(vals):
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def ids_of(b, s, seed):
+        return torch.randint(0, V, (b, s), generator=torch.Generator().manual_seed(seed)).to(dev)
+
+    def gen(ids, dbo, graph=True):
+        model.generate(ids, max_new_tokens=T, do_sample=False, use_decode_dbo=dbo,
+                       num_decode_micro_batches=2, decode_use_crosslayer=dbo,
+                       prefill_mode="serial" if not dbo else "dbo",
+                       num_prefill_micro_batches=1 if not dbo else 2, use_cuda_graph=graph)
+        m = model._last_generation_metrics
+        return m["prefill_ms"], m["decode_tpot_ms"]
+
+    if args.gpus == 2 and B >= 4:
+        ids = ids_of(4, 128, 7)
+        gen(ids, False)  # warm: graphs for this batch
+        pf, tp = mx(list(gen(ids, False)))
+        out["serial_b4_s128_2gpu"] = {"prefill_ms": pf, "decode_tpot_ms": tp,
+                                      "tok_s": 1000.0 * 4 / tp}
+        model.release_graphs()
+    if args.gpus == 8 and B >= 256:
+        ids = ids_of(32, 512, 8)
+        run = lambda mode, nmb: model.run_forward(ids, mode, nmb, crosslayer=True,  # noqa: E731
+                                                  reset_cache=True)
+        run("dbo", 2)
+        run("serial", 1)
+        t_dbo = timed(lambda: run("dbo", 2), 3) / 3
+        t_ser = timed(lambda: run("serial", 1), 3) / 3
+        out["prefill_b32_s512_8gpu"] = {"dbo_ms": t_dbo, "serial_ms": t_ser,
+                                        "dbo_speedup": t_ser / t_dbo}
+        sweep = {}
+        for b in (16, 64, 256):
+            ids = ids_of(b, S, 9 + b)
+            row = {}
+            for name, dbo in (("dbo_crosslayer", True), ("serial", False)):
+                gen(ids, dbo)  # warm: graphs for this batch
+                _, tp = mx([gen(ids, dbo)[1]])
+                row[name + "_tpot_ms"] = tp
+                row[name + "_tok_s"] = 1000.0 * b / tp
+            row["dbo_speedup"] = row["serial_tpot_ms"] / row["dbo_crosslayer_tpot_ms"]
+            sweep[str(b)] = row
+            model.release_graphs()
+        out["decode_s256_8gpu"] = sweep
+    if world > 1:
+        # eager decode steps: fused peer-memory transport vs NCCL isend/irecv
+        logits = model.run_forward(ids_of(B, S, 1234), "dbo", 2, crosslayer=True,
+                                   reset_cache=True)
+        tok = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        r = model.local_batch(B)
+        hold = {"l": logits}
+
+        def step():
+            if model.ctx.is_attention_node:
+                tok[r.start:r.stop, 0] = ops.argmax(hold["l"])
+            hold["l"] = model.decode_step(tok, "dbo", 2, True, False)
+
+        for _ in range(2):
+            step()
+        fused_eager = timed(step, 5) / 5
+        saved = (model.transport, model.comm_impl)
+        model.transport = NcclTransport(ctx, model.hidden_size, model.dtype, model.device,
+                                        crosslayer=True)
+        model.comm_impl = "nccl"
+        try:
+            for _ in range(2):
+                step()
+            nccl_eager = timed(step, 5) / 5
+        finally:
+            model.transport, model.comm_impl = saved
+        out["transport_decode_tpot_ms"] = {
+            "batch": B, "mode": "decode DBO, cross-layer, eager (no CUDA graph)",
+            "fused_peer_memory": fused_eager, "nccl_isend_irecv": nccl_eager,
+            "fused_speedup": nccl_eager / fused_eager}
+    return out
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -139,12 +250,15 @@ def main():
     torch.cuda.set_device(local)
     ctx = get_distributed_context()
     ctx.initialize(DistributedConfig(world_size=world, rank=rank, local_rank=local,
-                                     backend="nccl", timeout_s=120,
+                                     backend="nccl", timeout_s=120, n_attn=args.attn_gpus,
                                      master_addr=os.environ.get("MASTER_ADDR", "127.0.0.1"),
                                      master_port=os.environ.get("MASTER_PORT", "29500")))
     B = args.batch or args.batch_per_gpu * args.gpus
     S, T = args.seq, args.tokens
-    max_seq = S + max(T, args.warmup + args.steps + 2, args.profile + 2) + 8
+    cells_on = args.cells == "auto" and not args.profile and args.model == "qwen3-30b-a3b"
+    # the 8-GPU prefill cell runs a 512-token prompt
+    s_cells = 512 if (cells_on and args.gpus == 8) else S
+    max_seq = max(S, s_cells) + max(T, args.warmup + args.steps + 2, args.profile + 2) + 8
     # only the full model is the benchmark's config; anything else is labelled
     # as what it is and gets no baseline ratio
     headline = args.model == "qwen3-30b-a3b" and args.layers is None
@@ -288,6 +402,8 @@ def main():
                if model.ctx.is_attention_node else 0,
                "api": "DisaggregatedQwenModel.generate(host_io=True, use_cuda_graph=True)"}
 
+    cells = measure_cells(model, args, B, S, T, local, world, timed, ctx) if cells_on else None
+
     value = 1000.0 * B / tpot_xl
     ref = REF_XL_TPOT_S256.get(B) if (S == 256 and headline) else None
     mc = model.config
@@ -308,6 +424,9 @@ def main():
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": (value / (1000.0 * B / ref)) if ref else None,
+        "vs_baseline_basis": ("the reference's published cross-layer decode throughput at the "
+                              "same batch and prompt, measured on 4x V100-32GB (other "
+                              "hardware); not a same-box comparison") if ref else None,
         "dtype": "bf16",
         "data": "synthetic token ids uniform in [0, vocab), random-init weights",
         "config": {"model": model_label, "global_batch": B, "seq_len": S,
@@ -322,6 +441,7 @@ def main():
         "prefill_ttft_ms": {"dbo": ttft_dbo, "serial": ttft_serial,
                             "speedup": ttft_serial / ttft_dbo},
         "clocks": clk,
+        "cells": cells,
         "e2e": e2e,
         "gpu_launches": launches,
     }

@@ -47,7 +47,13 @@ __global__ void __launch_bounds__(D) decode_attention_kernel(DecodeAttnArgs a) {
   const int nsplit = gridDim.z;
   const int tid = threadIdx.x;
   const int warp = tid / 32, lane = tid % 32;
-  const int kv_len = *a.start_pos + 1;
+  int kv_len = *a.start_pos + 1;
+  if (kv_len < 1 || kv_len > a.s_max) {
+    // the position lies outside the cache rows: read nothing, output zeros
+    if (tid == 0 && b == 0 && kvh == 0 && split == 0)
+      report_status(a.status, kBoundsViolation, 60);
+    kv_len = 0;
+  }
   const int cb = a.batch_offset + b;
   const float scale = rsqrtf((float)D);
 
@@ -451,6 +457,13 @@ __global__ void __launch_bounds__(kFdWarps * 32) decode_attention_fused_kernel(F
   const int pos = *a.start_pos;
   const int kv_len = pos + 1;
   const int cb = a.batch_offset + b;
+  if (pos < 0 || pos >= a.s_max) {
+    // no cache row for the new token: write nothing to the cache, output zeros
+    if (tid == 0 && b == 0 && kvh == 0) report_status(a.status, kBoundsViolation, 61);
+    for (int i = tid; i < G * D; i += blockDim.x)
+      a.out[((size_t)b * a.nq + kvh * G) * D + i] = f_to_bf16(0.f);
+    return;
+  }
   __nv_bfloat16* kbase = a.k_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
   __nv_bfloat16* vbase = a.v_cache + ((size_t)cb * a.nkv + kvh) * a.s_max * D;
 
@@ -646,12 +659,9 @@ static int fused_launch(const FusedDecodeArgs& a, int B, cudaStream_t s) {
   static_assert((kFdWarps * 2 * kFdKeys * (D + 8)) * 2 >=
                     (2 * kFdWarps * 16 + kFdWarps * G * D) * 4,
                 "merge buffers must fit in the tile region");
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(decode_attention_fused_kernel<G, D>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    set = true;
-  }
+  const cudaError_t e = set_max_dynamic_smem(
+      reinterpret_cast<const void*>(decode_attention_fused_kernel<G, D>), smem);
+  if (e != cudaSuccess) return (int)e;
   return (int)launch_k(decode_attention_fused_kernel<G, D>, dim3(B, a.nkv), dim3(kFdWarps * 32), smem, s, a);
 }
 
@@ -690,12 +700,9 @@ int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s) {
   dim3 grid((a.q_len + kPBM - 1) / kPBM, a.nq, B);
   if (a.D == 128) {
     const int smem = (kPBM + 2 * kPBN) * (128 + 8) * 2;
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(prefill_attention_kernel<128>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set = true;
-    }
+    const cudaError_t e = set_max_dynamic_smem(
+        reinterpret_cast<const void*>(prefill_attention_kernel<128>), smem);
+    if (e != cudaSuccess) return (int)e;
     launch_k(prefill_attention_kernel<128>, grid, dim3(128), smem, s, a);
   } else if (a.D == 64) {
     const int smem = (kPBM + 2 * kPBN) * (64 + 8) * 2;

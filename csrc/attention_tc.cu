@@ -368,13 +368,9 @@ int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s)
   if (e) return e;
   e = encode(&mp.v, a.v_cache, 3, kdims, kstr, kbox);
   if (e) return e;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t r = cudaFuncSetAttribute(prefill_attention_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
-    if (r != cudaSuccess) return (int)r;
-    attr = true;
-  }
+  const cudaError_t r =
+      set_max_dynamic_smem(reinterpret_cast<const void*>(prefill_attention_tc_kernel), kTcSmem);
+  if (r != cudaSuccess) return (int)r;
   dim3 grid((a.q_len + kTcBM - 1) / kTcBM, a.nq, B);
   return (int)launch_k(prefill_attention_tc_kernel, grid, dim3(kTcThreads), kTcSmem, s, mp.q,
                        mp.k, mp.v, a);

@@ -13,6 +13,10 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 namespace afd {
 
 // ---------------------------------------------------------------- status ---
@@ -21,7 +25,7 @@ enum StatusCode : int {
   kOk = 0,
   kTimeoutMbarrier = 1,   // an intra-CTA pipeline barrier never completed
   kTimeoutPeerFlag = 2,   // a flag another GPU should raise never arrived
-  kBoundsViolation = 3,   // AFD_BOUNDS_CHECK build: an index left its range
+  kBoundsViolation = 3,   // an index or position left its range (the access was skipped)
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -76,6 +80,25 @@ inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current
+// device. The attribute belongs to the (kernel, device) pair, so the set is
+// remembered per device: a process that launches on several GPUs sets it on
+// each one before its first launch there.
+inline cudaError_t set_max_dynamic_smem(const void* kern, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(kern, dev);
+  const auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
 }
 
 // ------------------------------------------------------------------ bf16 ---

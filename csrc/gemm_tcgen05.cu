@@ -570,13 +570,8 @@ static cudaError_t launch_variant(const CUtensorMap& tw, const CUtensorMap& tx, 
                                   int grid, cudaStream_t stream) {
   using L = GemmSmem<SWIGLU, BN, STAGES>;
   auto kern = gemm_swapab_kernel<SWIGLU, BN, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kTotal);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  const cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), L::kTotal);
+  if (e != cudaSuccess) return e;
   return launch_k(kern, dim3(grid), dim3(kThreads), L::kTotal, stream, tw, tx, a);
 }
 

@@ -58,6 +58,9 @@ struct DecodeAttnArgs {
   float* ml_part;             // [B, nq, nsplit, 2]
   const int* start_pos;       // position of the query token (kv_len = start + 1)
   int batch_offset, nq, nkv, D, s_max;
+  // optional [2] status word: a *start_pos outside [0, s_max) is recorded as
+  // kBoundsViolation and the kernel reads no key (outputs are zeros)
+  int* status;
 };
 
 // Decode attention with the new token's q/k RMSNorm + RoPE + KV append folded
@@ -75,6 +78,7 @@ struct FusedDecodeArgs {
   const int* start_pos;
   int batch_offset, nq, nkv, D, s_max;
   float eps;
+  int* status;                // optional; same out-of-range rule as DecodeAttnArgs
 };
 
 int launch_decode_attention_fused(const FusedDecodeArgs& a, int B, cudaStream_t s);
