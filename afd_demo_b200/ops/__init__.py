@@ -24,7 +24,7 @@ _KERNEL_CALLS = {"gemm", "sum_rmsnorm", "qk_norm_rope_cache", "decode_attention"
                  "prefill_attention", "router_topk", "moe_align", "moe_gather", "moe_combine",
                  "argmax", "signal_flags", "wait_flags", "add_i32", "peer_copy",
                  "decode_attention_fused", "moe_route", "moe_gate", "gemm_down_combine",
-                 "moe_align_mt"}
+                 "moe_align_mt", "decode_attention_tc"}
 
 
 class LaunchCounter:
@@ -275,6 +275,101 @@ def qk_norm_rope_cache(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Te
     return q
 
 
+# Decode attention kernel: "tc" = tcgen05/TMEM/TMA kernel (head_dim 128, 4 or 8
+# query heads per kv head; other shapes use the mma.sync kernels), "mma" =
+# the mma.sync fused kernel and the split-KV SIMT kernel (A/B measurements).
+_DECODE_ATTN = os.environ.get("AFD_DECODE_ATTN", "tc")
+_DECODE_TILE = 128  # keys per tile of the tcgen05 decode kernel
+
+# cost model of the tcgen05 decode kernel, in units of one 128-key tile's
+# softmax round on one CTA: a work item's fixed cost (Q, pipeline fill,
+# output) and a split merge; the HBM time of one tile across the GPU
+_DEC_ITEM_COST = 2.0
+_DEC_MERGE_COST = 3.0
+_DEC_TILE_HBM = 0.01
+
+
+def decode_splits(B: int, nkv: int, kv_len: int, sms: Optional[int] = None) -> int:
+    """Key splits per (sequence, kv head) for the tcgen05 decode kernel: the
+    count with the lowest estimated time, max(the busiest CTA's tiles and
+    item overheads, the whole KV read at HBM speed) plus a merge when split.
+    Splitting pays only when there are fewer (sequence, kv head) pairs than
+    SMs and the sequences are long."""
+    n = sms or num_sms()
+    tiles = max(1, (kv_len + _DECODE_TILE - 1) // _DECODE_TILE)
+    hbm = B * nkv * tiles * _DEC_TILE_HBM
+    best, best_cost = 1, None
+    for s in range(1, min(tiles, 16) + 1):
+        waves = (B * nkv * s + n - 1) // n
+        per = (tiles + s - 1) // s
+        cost = max(waves * (per + _DEC_ITEM_COST), hbm) + (_DEC_MERGE_COST if s > 1 else 0.0)
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
+
+
+class _DecodeCounters:
+    """Zeroed per-(sequence, kv head) merge counters of the tcgen05 decode
+    kernel (the merging CTA resets its counter), one buffer per (device,
+    stream); outgrown buffers stay alive for captured graphs."""
+
+    _pool: dict = {}
+    _retired: list = []
+
+    @classmethod
+    def get(cls, device, n: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        c = cls._pool.get(key)
+        if c is None or c.numel() < n:
+            if c is not None:
+                cls._retired.append(c)
+            c = torch.zeros(max(n, 1024), device=device, dtype=torch.int32)
+            cls._pool[key] = c
+        return c
+
+
+def _tc_decode_ok(nq: int, nkv: int, D: int) -> bool:
+    return _DECODE_ATTN == "tc" and bool(ext().decode_tc_supported(nq, nkv, D))
+
+
+def decode_attention_tc(q: Optional[torch.Tensor], k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        batch_offset: int, start_pos: int, start_pos_dev: torch.Tensor,
+                        nsplit: Optional[int] = None, status: Optional[torch.Tensor] = None,
+                        fused: Optional[tuple] = None) -> torch.Tensor:
+    """tcgen05 decode attention: q [B, nq, D] (one query per sequence, at
+    position *start_pos_dev) over cache rows [batch_offset, +B); returns
+    [B, nq, D]. `start_pos` (host) sizes the key splits; the kernel reads the
+    position from the device, so graph replays may grow it. `fused` =
+    (qkv [B, (nq + 2 nkv) D], q_norm, k_norm, rope, eps, nq) replaces q: the
+    same launch applies q/k RMSNorm and RoPE and appends the token's K and V."""
+    nkv, D = k_cache.shape[1], k_cache.shape[3]
+    if fused is not None:
+        qkv, q_norm, k_norm, rope, eps, nq = fused
+        B = qkv.shape[0]
+        dev = qkv.device
+        out = torch.empty(B, nq, D, device=dev, dtype=qkv.dtype)
+    else:
+        B, nq, _ = q.shape
+        dev = q.device
+        out = torch.empty_like(q)
+    if nsplit is None:
+        nsplit = decode_splits(B, nkv, start_pos + 1)
+    o_part = ml_part = cnt = None
+    if nsplit > 1:
+        o_part = torch.empty(B * nq, nsplit, D, device=dev, dtype=torch.float32)
+        ml_part = torch.empty(B * nq, nsplit, 2, device=dev, dtype=torch.float32)
+        cnt = _DecodeCounters.get(dev, B * nkv)
+    if fused is not None:
+        ext().decode_attention_tc(None, k_cache, v_cache, out, start_pos_dev, int(batch_offset),
+                                  int(nsplit), o_part, ml_part, cnt, status, num_sms(), qkv,
+                                  q_norm, k_norm, rope, float(eps))
+    else:
+        ext().decode_attention_tc(q.contiguous(), k_cache, v_cache, out, start_pos_dev,
+                                  int(batch_offset), int(nsplit), o_part, ml_part, cnt, status,
+                                  num_sms(), None, None, None, None, 0.0)
+    return out
+
+
 def decode_attention_fused(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
                            rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            start_pos: int, start_pos_dev: Optional[torch.Tensor],
@@ -288,6 +383,12 @@ def decode_attention_fused(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torc
         return torch_ref.attention(q, k_cache, v_cache, batch_offset, 1, start_pos)
     B = qkv.shape[0]
     D = k_cache.shape[-1]
+    nkv = k_cache.shape[1]
+    if _tc_decode_ok(nq, nkv, D):
+        # q/k RMSNorm + RoPE + KV append + tcgen05 attention in one launch
+        return decode_attention_tc(None, k_cache, v_cache, batch_offset, start_pos,
+                                   start_pos_dev,
+                                   fused=(qkv, q_norm, k_norm, rope, eps, nq)).view(B, nq * D)
     out = torch.empty(B, nq, D, device=qkv.device, dtype=qkv.dtype)
     ext().decode_attention_fused(qkv, q_norm, k_norm, rope, k_cache, v_cache, out,
                                  start_pos_dev, batch_offset, nq, float(eps))
@@ -309,6 +410,9 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, bat
         if key_range is not None:
             raise ValueError("padding key ranges apply to prefill (q_len > 1) only")
         nkv = k_cache.shape[1]
+        if _tc_decode_ok(nq, nkv, D):
+            return decode_attention_tc(q, k_cache, v_cache, batch_offset, start_pos,
+                                       start_pos_dev).view(T, nq * D)
         tiles = (start_pos + 1 + 63) // 64
         nsplit = max(1, min(tiles, (2 * num_sms() + T * nkv - 1) // max(1, T * nkv)))
         o_part = ml_part = None

@@ -88,7 +88,13 @@ def main(argv=None) -> int:
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--json", default="")
+    ap.add_argument("--sections", default="decode,attention,prefill",
+                    help="comma list of: decode (per-layer decode kernels by token count), "
+                         "attention (decode attention over long caches), prefill")
+    ap.add_argument("--attn-batches", default="16,64")
+    ap.add_argument("--attn-kv", default="256,1024,2048,4096")
     a = ap.parse_args(argv)
+    sections = set(a.sections.split(","))
     dev = torch.device("cuda")
     bw, fl, tag = peaks()
     H, I, E, k, nq, nkv, D = 2048, 768, 128, 8, 32, 4, 128
@@ -120,7 +126,7 @@ def main(argv=None) -> int:
     qn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
     rope = ops.rope_table(4096, D, 1e6, dev)
 
-    for T in [int(t) for t in a.tokens.split(",")]:
+    for T in ([int(t) for t in a.tokens.split(",")] if "decode" in sections else []):
         x = rnd(T, H, scale=1.0)
         o_in = rnd(T, nq * D, scale=1.0)
         report("sum_rmsnorm (2 parts)", T,
@@ -158,6 +164,42 @@ def main(argv=None) -> int:
                                             1e-6), a.iters, a.warmup),
                eb + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
 
+    # decode attention over long caches: tcgen05 kernel vs the mma.sync kernel
+    for B in ([int(b) for b in a.attn_batches.split(",")] if "attention" in sections else []):
+        for kv in [int(v) for v in a.attn_kv.split(",")]:
+            S = kv + 8
+            cache_bytes = 2 * B * nkv * S * D * 2
+            n_c = copies_for(cache_bytes // 2)
+            kcs = [rnd(B, nkv, S, D, scale=1.0) for _ in range(n_c)]
+            vcs = [rnd(B, nkv, S, D, scale=1.0) for _ in range(n_c)]
+            q = rnd(B, nq, D, scale=1.0)
+            pos = torch.tensor([kv - 1], device=dev, dtype=torch.int32)
+            nbytes = 2 * B * nkv * kv * D * 2 + 2 * B * nq * D * 2
+            flops = 4 * B * nq * kv * D
+            sp = ops.decode_splits(B, nkv, kv)
+            report(f"decode attn tcgen05 kv={kv} s={sp}", B,
+                   timeit(lambda i: ops.decode_attention_tc(q, kcs[i % n_c], vcs[i % n_c], 0,
+                                                            kv - 1, pos), a.iters, a.warmup),
+                   nbytes, flops)
+            saved = ops._DECODE_ATTN
+            ops._DECODE_ATTN = "mma"
+            try:
+                qkv = rnd(B, QKV, scale=1.0)
+                report(f"decode attn mma.sync kv={kv}", B,
+                       timeit(lambda i: ops.decode_attention_fused(
+                           qkv, qn, qn, rope, kcs[i % n_c], vcs[i % n_c], kv - 1, pos, 0, nq, nkv,
+                           1e-6), a.iters, a.warmup),
+                       nbytes, flops)
+            finally:
+                ops._DECODE_ATTN = saved
+            del kcs, vcs
+
+    if "prefill" not in sections:
+        if a.json:
+            os.makedirs(os.path.dirname(os.path.abspath(a.json)), exist_ok=True)
+            json.dump({"peaks": {"hbm_Bps": bw, "bf16_flops": fl, "basis": tag}, "rows": rows},
+                      open(a.json, "w"), indent=1)
+        return 0
     # prefill-sized dense GEMM and attention
     T = a.prefill_tokens
     xp = rnd(T, H, scale=1.0)

@@ -295,6 +295,63 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
            "decode_attention");
 }
 
+// q [B, nq, D] given (qkv empty), or the fused new-token step from qkv
+// [B, ld] (q/k RMSNorm, RoPE, K/V append into the caches, then attention).
+void decode_attention_tc(const c10::optional<at::Tensor>& q, at::Tensor& k_cache,
+                         at::Tensor& v_cache, at::Tensor& out, const at::Tensor& start_pos,
+                         int64_t batch_offset, int64_t nsplit,
+                         const c10::optional<at::Tensor>& o_part,
+                         const c10::optional<at::Tensor>& ml_part,
+                         const c10::optional<at::Tensor>& counters,
+                         const c10::optional<at::Tensor>& status, int64_t grid,
+                         const c10::optional<at::Tensor>& qkv,
+                         const c10::optional<at::Tensor>& q_norm,
+                         const c10::optional<at::Tensor>& k_norm,
+                         const c10::optional<at::Tensor>& rope, double eps) {
+  CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(out);
+  TORCH_CHECK(out.is_contiguous() && out.dim() == 3, "out must be contiguous [B, nq, D]");
+  TORCH_CHECK(start_pos.scalar_type() == at::kInt, "start_pos must be int32");
+  TORCH_CHECK(q.has_value() != qkv.has_value(), "give q or qkv");
+  afd::DecodeTcArgs a{};
+  if (q.has_value()) {
+    CHECK_BF16(*q);
+    TORCH_CHECK(q->is_contiguous(), "q must be contiguous");
+    a.q = cbf(*q);
+  } else {
+    CHECK_BF16(*qkv);
+    TORCH_CHECK(q_norm.has_value() && k_norm.has_value() && rope.has_value(),
+                "the fused step needs q_norm, k_norm and the rope table");
+    TORCH_CHECK(rope->scalar_type() == at::kFloat, "rope table must be fp32");
+    TORCH_CHECK(qkv->stride(1) == 1, "qkv rows must be contiguous");
+    a.qkv = cbf(*qkv);
+    a.ld_qkv = (int)qkv->stride(0);
+    a.q_norm = cbf(*q_norm);
+    a.k_norm = cbf(*k_norm);
+    a.rope = rope->data_ptr<float>();
+    a.eps = (float)eps;
+  }
+  a.k_cache = bf(k_cache);
+  a.v_cache = bf(v_cache);
+  a.out = bf(out);
+  a.o_part = opt_ptr<float>(o_part);
+  a.ml_part = opt_ptr<float>(ml_part);
+  a.counters = opt_ptr<int>(counters);
+  a.status = opt_ptr<int>(status);
+  a.start_pos = start_pos.data_ptr<int>();
+  a.B = (int)out.size(0);
+  a.batch_offset = (int)batch_offset;
+  a.nq = (int)out.size(1);
+  a.nkv = (int)k_cache.size(1);
+  a.D = (int)out.size(2);
+  a.s_max = (int)k_cache.size(2);
+  a.nsplit = (int)nsplit;
+  check_rc(afd::launch_decode_attention_tc(a, (int)grid, cur_stream()), "decode_attention_tc");
+}
+
+bool decode_tc_supported(int64_t nq, int64_t nkv, int64_t D) {
+  return afd::decode_tc_supported((int)nq, (int)nkv, (int)D) != 0;
+}
+
 void decode_attention_fused(const at::Tensor& qkv, const at::Tensor& q_norm,
                             const at::Tensor& k_norm, const at::Tensor& rope, at::Tensor& k_cache,
                             at::Tensor& v_cache, at::Tensor& out, const at::Tensor& start_pos,
@@ -670,6 +727,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sum_rmsnorm", &sum_rmsnorm);
   m.def("qk_norm_rope_cache", &qk_norm_rope_cache);
   m.def("decode_attention", &decode_attention);
+  m.def("decode_attention_tc", &decode_attention_tc);
+  m.def("decode_tc_supported", &decode_tc_supported);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax_workspace_ints", &argmax_workspace_ints);
   m.def("decode_attention_fused", &decode_attention_fused);

@@ -208,6 +208,32 @@ int launch_signal_flags(const FlagArgs& a, cudaStream_t s);
 int launch_wait_flags(const FlagArgs& a, cudaStream_t s);
 int launch_add_i32(int* p, int by, cudaStream_t s);
 int launch_decode_attention(const DecodeAttnArgs& a, int B, int nsplit, cudaStream_t s);
+
+// tcgen05/TMEM/TMA decode attention (decode_attention_tc.cu), head_dim 128,
+// G = nq / nkv in {4, 8}; a persistent grid of at most `grid` CTAs.
+struct DecodeTcArgs {
+  const __nv_bfloat16* q;     // [B, nq, D] (unused when qkv is given)
+  __nv_bfloat16* k_cache;     // [B_max, nkv, s_max, D]; written only by the fused step
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;         // [B, nq, D]
+  float* o_part;              // nsplit > 1: [B * nq, nsplit, D]
+  float* ml_part;             // nsplit > 1: [B * nq, nsplit, 2]
+  int* counters;              // nsplit > 1: [B * nkv], zero; left zero
+  const int* start_pos;       // position of the query token (kv_len = start + 1)
+  int* status;                // optional [2]
+  int B, batch_offset, nq, nkv, D, s_max, nsplit;
+  // Fused new-token step (qkv != nullptr): the kernel applies q/k RMSNorm and
+  // RoPE at *start_pos to the token's projections, appends its K and V to the
+  // cache and attends; q is then unused.
+  const __nv_bfloat16* qkv;   // [B, ld_qkv]: q heads | k heads | v heads
+  int ld_qkv;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* rope;          // [max_pos, D]: cos | sin
+  float eps;
+};
+int decode_tc_supported(int nq, int nkv, int D);
+int launch_decode_attention_tc(const DecodeTcArgs& a, int grid, cudaStream_t s);
 int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s);
 // tcgen05/TMEM/TMA version (attention_tc.cu), head_dim 128
 int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s);

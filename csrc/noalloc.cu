@@ -52,13 +52,15 @@ extern "C" int afd_decode_attention_noalloc(const void* q, const void* k_cache,
                                             int n_split, cudaStream_t stream) {
   // every argument is checked here, so the launcher's own argument checks
   // cannot fire and any failure after this point is a launch failure
-  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
-      start_pos == nullptr || batch < 0 || n_q_heads <= 0 || n_kv_heads <= 0 ||
-      n_q_heads % n_kv_heads != 0 || head_dim <= 0 || max_seq <= 0 || batch_offset < 0 ||
-      max_batch < 0 || batch_offset + batch > max_batch || n_split < 1 ||
+  if (batch < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 ||
+      head_dim <= 0 || max_seq <= 0 || batch_offset < 0 || max_batch < 0 ||
+      batch_offset + batch > max_batch || n_split < 1 ||
       !supported_layout(n_q_heads / n_kv_heads, head_dim))
     return AFD_NOALLOC_ERR_BAD_ARG;
-  if (batch == 0) return AFD_NOALLOC_OK;
+  if (batch == 0) return AFD_NOALLOC_OK;  // nothing to read or write (pointers may be null)
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
+      start_pos == nullptr)
+    return AFD_NOALLOC_ERR_BAD_ARG;
   const unsigned long long need = (unsigned long long)batch * n_q_heads * n_split *
                                   (unsigned long long)(head_dim + 2) * sizeof(float);
   if (n_split > 1 && need > AFD_NOALLOC_SCRATCH_BYTES) return AFD_NOALLOC_ERR_TOO_LARGE;

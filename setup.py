@@ -25,7 +25,7 @@ if os.environ.get("AFD_BOUNDS_CHECK"):
     NVCC_FLAGS.append("-DAFD_BOUNDS_CHECK=1")
 
 SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "kernels.cu", "attention.cu", "attention_tc.cu",
-           "noalloc.cu"]
+           "decode_attention_tc.cu", "noalloc.cu"]
 
 setup(
     name="afd_demo_b200",

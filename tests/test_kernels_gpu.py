@@ -181,6 +181,91 @@ def test_decode_attention(B, kv_len):
     assert _rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("B", [16, 64])
+@pytest.mark.parametrize("kv_len", [256, 1024, 2048, 4096])
+def test_decode_attention_tc_long_kv(B, kv_len):
+    """tcgen05 decode attention at the cache lengths where it dominates."""
+    nq, nkv, D, S = 32, 4, 128, 4104
+    kc = _randn(B + 1, nkv, S, D, seed=50)
+    vc = _randn(B + 1, nkv, S, D, seed=51)
+    q = _randn(B, nq, D, seed=52)
+    start = kv_len - 1
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 1, 1, start)
+    out = ops.decode_attention_tc(q, kc, vc, 1, start, pos).view(B, nq * D)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("nsplit", [1, 2, 3, 7, 16, 40])
+@pytest.mark.parametrize("G", [8, 4])
+def test_decode_attention_tc_splits(nsplit, G):
+    """Every split count merges to the same result, including splits that
+    own no key tile (more splits than tiles), for 8 and 4 query heads per
+    kv head."""
+    nkv, D, S, B, kv_len = 4, 128, 2304, 5, 1500
+    nq = G * nkv
+    kc = _randn(B, nkv, S, D, seed=53)
+    vc = _randn(B, nkv, S, D, seed=54)
+    q = _randn(B, nq, D, seed=55)
+    pos = torch.tensor([kv_len - 1], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, 1, kv_len - 1)
+    for _ in range(2):  # the merge counters must be left at zero
+        out = ops.decode_attention_tc(q, kc, vc, 0, kv_len - 1, pos, nsplit=nsplit)
+        assert _rel(out.view(B, nq * D), ref) < 1e-2
+
+
+def test_decode_attention_tc_nan_past_the_end():
+    """Cache rows past the sequence end may hold anything (here NaN): they
+    must not reach the output."""
+    nq, nkv, D, S, B, kv_len = 32, 4, 128, 512, 3, 200
+    kc = _randn(B, nkv, S, D, seed=56)
+    vc = _randn(B, nkv, S, D, seed=57)
+    kc[:, :, kv_len:] = float("nan")
+    vc[:, :, kv_len:] = float("nan")
+    q = _randn(B, nq, D, seed=58)
+    pos = torch.tensor([kv_len - 1], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, 1, kv_len - 1)
+    out = ops.decode_attention_tc(q, kc, vc, 0, kv_len - 1, pos).view(B, nq * D)
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out, ref) < 1e-2
+
+
+def test_decode_attention_tc_bad_position_reads_nothing():
+    nq, nkv, D, S, B = 32, 4, 128, 256, 2
+    kc = _randn(B + 2, nkv, S, D, seed=59)
+    q = _randn(B, nq, D, seed=60)
+    for p in (S, -5):
+        pos = torch.tensor([p], device=DEV, dtype=torch.int32)
+        st = torch.zeros(2, device=DEV, dtype=torch.int32)
+        out = ops.decode_attention_tc(q, kc, kc, 0, 100, pos, status=st)
+        torch.cuda.synchronize()
+        assert int(st[0]) == 3 and torch.count_nonzero(out) == 0
+
+
+@pytest.mark.parametrize("B,kv_len", [(3, 77), (16, 276), (2, 2049)])
+def test_decode_attention_mma_kernels(B, kv_len, monkeypatch):
+    """The mma.sync / SIMT decode kernels (AFD_DECODE_ATTN=mma) stay correct."""
+    monkeypatch.setattr(ops, "_DECODE_ATTN", "mma")
+    nq, nkv, D, S = 32, 4, 128, 2304
+    kc = _randn(B + 1, nkv, S, D, seed=61)
+    vc = _randn(B + 1, nkv, S, D, seed=62)
+    q = _randn(B, nq, D, seed=63)
+    start = kv_len - 1
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 1, 1, start)
+    assert _rel(ops.attention(q, kc, vc, 1, 1, start, pos), ref) < 1e-2
+    qkv = _randn(B, (nq + 2 * nkv) * D, seed=64)
+    qn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    rope = ops.rope_table(S, D, 1e6, DEV)
+    kc2, vc2 = kc.clone(), vc.clone()
+    q_ref = torch_ref.qk_norm_rope_cache(qkv.float(), qn.float(), kn.float(), rope, kc2, vc2, 1,
+                                         1, start, nq, nkv, 1e-6)
+    ref = torch_ref.attention(q_ref, kc2.float(), vc2.float(), 1, 1, start)
+    out = ops.decode_attention_fused(qkv, qn, kn, rope, kc, vc, start, pos, 1, nq, nkv, 1e-6)
+    assert _rel(out, ref) < 1e-2
+
+
 @pytest.mark.parametrize("B,kv_len,G,D", [(1, 1, 8, 128), (3, 77, 8, 128), (16, 276, 8, 128),
                                            (64, 300, 8, 128), (2, 2049, 8, 128), (5, 100, 2, 64),
                                            (4, 500, 8, 64)])
