@@ -78,6 +78,15 @@ class DisaggregatedQwenModel:
         # in a DBO schedule (0: all); AFD_COLOCATED_FFN_SMS overrides
         import os
         self.colocated_ffn_sms = int(os.environ.get("AFD_COLOCATED_FFN_SMS", "0"))
+        # Separate-GPU roles under cross-layer DBO with the fused transport:
+        # one stream per micro-batch on each rank, so that one micro-batch's
+        # latency-bound kernels (norms, attention, MoE gate, combine, hand-offs)
+        # run beside the other's weight-streaming GEMMs. The FFN GEMMs then
+        # leave `mb_gemm_free_sms` SMs to the other stream's kernels.
+        # AFD_MB_STREAMS=0 keeps one stream per rank (A/B measurements).
+        self.mb_streams_enabled = os.environ.get("AFD_MB_STREAMS", "1") != "0"
+        self.mb_gemm_free_sms = int(os.environ.get("AFD_MB_GEMM_FREE_SMS", "20"))
+        self._mb_streams: list = []
 
     # ------------------------------------------------------------ set-up
     @property
@@ -146,6 +155,12 @@ class DisaggregatedQwenModel:
                                            self.dtype, timeout_ms=timeout_ms)
         else:
             raise ValueError(f"unknown comm impl {comm_impl!r}")
+
+    def mb_streams(self, n: int) -> list:
+        """One CUDA stream per micro-batch (created once, reused)."""
+        while len(self._mb_streams) < n:
+            self._mb_streams.append(torch.cuda.Stream(self.device))
+        return self._mb_streams[:n]
 
     def setup_communicator(self, max_seq_len: int = 2048, max_batch_size: int = 4,
                            num_buffers: int = 2) -> None:

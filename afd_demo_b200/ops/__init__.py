@@ -174,12 +174,26 @@ _MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "128"))
 
 
 def _moe_block_n(rows: int) -> int:
-    """Row-block size of the grouped expert GEMMs: 64 for decode-sized
-    batches; 128 for mid-sized ones (two TMEM accumulators per SwiGLU tile,
-    double-buffered); 256 for prefill-sized ones, where 128-row tiles leave
-    the MMA waiting on shared-memory bandwidth. The MMA width follows each
+    """Row-block size of the grouped expert GEMMs by token count: 64 for
+    decode-sized batches (up to 256 tokens: with top-8 of 128 experts an
+    expert sees about T/16 rows, so one 64-row block holds it, and the
+    smaller token tile leaves room for one more weight stage); 128 for
+    mid-sized ones (two TMEM accumulators per SwiGLU tile, double-buffered);
+    `AFD_MOE_BN_LARGE` for prefill-sized ones. The MMA width follows each
     block's actual row count, so a short last block costs little."""
-    return 64 if rows <= 64 else (128 if rows < 2048 else _MOE_BN_LARGE)
+    return 64 if rows <= 256 else (128 if rows < 2048 else _MOE_BN_LARGE)
+
+
+def _wave_splits(units: int, k_iters: int, gain: float = 1.1) -> int:
+    """Split-K factor (1 or 2) for a grouped GEMM whose units fill the
+    persistent grid's last wave poorly: 2 when that raises the share of busy
+    CTA slots by at least `gain` (each split adds a partial-tile store and a
+    reduction)."""
+    n = num_sms()
+    if units <= 0 or k_iters % 2 or k_iters < 4:
+        return 1
+    eff = lambda u: u / (((u + n - 1) // n) * n)  # noqa: E731
+    return 2 if eff(2 * units) >= gain * eff(units) else 1
 
 
 # upper bound of the split-K factor (AFD_MAX_SPLITS for A/B measurements)
@@ -500,12 +514,14 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
         x = torch.empty(R, H, device=xn.device, dtype=xn.dtype)
         C.moe_gather(xn, ws.row_token, ws.num_rows, x, R)
         row_ids = None
-    # decode sizes: ~one row block per hit expert, I/128 feature tiles each --
-    # a few tiles per SM, so splitting K in two evens out the last wave
+    # decode sizes: about one row block per hit expert, I/128 (gate_up) or
+    # H/128 (down) feature tiles each -- a few tiles per SM, so when the last
+    # wave of the persistent grid would run half empty, K is split in two
     max_tiles = ws.max_blocks * (I // 128)
-    est_tiles = min(E_loc, T * k) * (I // 128)
-    gu_splits = 2 if (_GU_SPLIT and T <= 64 and est_tiles < 6 * num_sms()
-                      and (H // 64) % 2 == 0) else 1
+    decode = T <= _FUSED_COMBINE_MAX_TOKENS
+    est_blocks = min(E_loc, T * k)
+    gu_splits = _wave_splits(est_blocks * (I // 128), H // 64) if (decode and _GU_SPLIT) else 1
+    dn_splits = _wave_splits(est_blocks * (H // 128), I // 64) if (decode and _GU_SPLIT) else 1
     gws = gcnt = None
     if gu_splits > 1:
         gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, gu_splits)
@@ -522,9 +538,13 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
                             int(peer_row_offset), list(flags), int(signal_value), done_counter,
                             None, epoch, _CombineCounters.get(xn.device, H // 128))
         return out
+    dws = dcnt = None
+    dn_tiles = ws.max_blocks * (H // 128)
+    if dn_splits > 1:
+        dws, dcnt = _SplitKWorkspace.get(xn.device, dn_tiles, bn, dn_splits)
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
-           None, ws.row_weight, False, bn, ws.max_blocks * (H // 128), [], 0, [], 0, None, None,
-           None, 1, None, None, None)
+           None, ws.row_weight, False, bn, dn_tiles * dn_splits, [], 0, [], 0, None, None,
+           None, dn_splits, dws, dcnt, None)
     if peers and _SPLIT_F2A and T > _FUSED_COMBINE_MAX_TOKENS:
         # prefill sizes: combine locally, then one bulk peer copy per attention
         # rank's segment (the combine kernel's scattered NVLink stores run at
@@ -616,7 +636,7 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 # sequence, AFD_FUSED_COMBINE=1 the combine inside the down GEMM's epilogue.
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
 _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine, then bulk copy
-_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"  # split-K of the decode gate_up GEMM (measured slower)
+_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "1") != "0"  # wave-balancing split-K of the decode expert GEMMs
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slower (esp. with peers)
 
 

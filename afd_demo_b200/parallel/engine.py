@@ -16,6 +16,14 @@ the waits:
 * ``dbo`` + ``crosslayer`` -- micro-batch m enters layer l+1 as soon as its
   own layer-l result is back (reference ``--crosslayer``,
   src/pipeline/decode_scheduler.py:304-332).
+
+Streams: one GPU holding both roles runs the attention blocks on one stream
+and the FFN blocks on another. With the roles on separate GPUs and the fused
+peer-memory transport, cross-layer DBO gives each micro-batch its own stream
+on every rank (the receives are device-side flag waits, so nothing orders
+the two micro-batches but the data): one micro-batch's latency-bound kernels
+then run beside the other's weight-streaming GEMMs, whose grid leaves a few
+SMs free for them.
 """
 
 from __future__ import annotations
@@ -64,18 +72,24 @@ class PipelineEngine:
         serial = mode == "serial"
         s_main = m_.attn_stream
         s_ffn = m_.ffn_stream if (colocated and not serial) else s_main
+        mb_streams = None
+        if (not serial and crosslayer and not colocated and s_main is not None
+                and plan.num_mb > 1 and getattr(m_, "mb_streams_enabled", False)
+                and m_.transport.fused):
+            mb_streams = m_.mb_streams(plan.num_mb)
         caller = torch.cuda.current_stream() if s_main is not None else None
-        for s in {s_main, s_ffn} - {None}:
+        every = {s_main, s_ffn} | set(mb_streams or ())
+        for s in every - {None}:
             s.wait_stream(caller)
         try:
             return self._forward(plan, input_ids, serial, crosslayer, trackers or {}, last_only,
-                                 advance_cache, s_main, s_ffn)
+                                 advance_cache, s_main, s_ffn, mb_streams)
         finally:
-            for s in {s_main, s_ffn} - {None}:
+            for s in every - {None}:
                 caller.wait_stream(s)
 
     def _forward(self, plan, input_ids, serial, crosslayer, trackers, last_only, advance_cache,
-                 s_attn, s_ffn):
+                 s_attn, s_ffn, mb_streams=None):
         m_ = self.model
         ctx = m_.ctx
         tr = m_.transport
@@ -94,11 +108,26 @@ class PipelineEngine:
             m_.ffn_worker.tracker = tf
 
         # co-located DBO: the FFN's persistent GEMMs leave SMs to the attention
-        # stream so the two micro-batches really run side by side
+        # stream so the two micro-batches really run side by side; likewise
+        # with one stream per micro-batch on separate-GPU roles
         ffn_sms = m_.colocated_ffn_sms if (colocated and not serial) else 0
+        if mb_streams is not None and m_.mb_gemm_free_sms > 0:
+            ffn_sms = max(1, ops.num_sms() - m_.mb_gemm_free_sms)
+
+        def st_attn(m: int):
+            return mb_streams[m] if mb_streams is not None else s_attn
+
+        def st_ffn(m: int):
+            return mb_streams[m] if mb_streams is not None else s_ffn
+
+        def fork():
+            # the per-micro-batch streams start after the role stream's work so far
+            if mb_streams is not None:
+                for s in mb_streams:
+                    s.wait_stream(s_attn)
 
         def ffn_block(l: int, m: int):
-            with _on(s_ffn), ops.sm_budget(ffn_sms):
+            with _on(st_ffn(m)), ops.sm_budget(ffn_sms):
                 if tf:
                     tf.mark_start(EventType.RECV_WAIT, l, m)
                 h = tr.a2f_recv(l, m)
@@ -117,10 +146,14 @@ class PipelineEngine:
                     tf.record_send(None, l, m, t0, out)
 
         if not has_attn:
+            fork()
             for l in range(L):
                 for m in range(plan.num_mb):
                     ffn_block(l, m)
             with _on(s_ffn):
+                if mb_streams is not None:
+                    for s in mb_streams:
+                        s_ffn.wait_stream(s)
                 tr.end()
             return None
 
@@ -134,6 +167,10 @@ class PipelineEngine:
             for s in slots:
                 r0 = s.batch_offset * s.q_len
                 xs[s.idx] = [x0[r0:r0 + s.tokens]]
+        fork()
+        if mb_streams is not None:
+            for s in mb_streams:
+                x0.record_stream(s)
         have = {(s.idx, -1) for s in slots}  # (m, l): layer-l output of m received
         waits: Dict[int, object] = {}  # m -> wait left to the consumer of xs[m]
 
@@ -157,7 +194,7 @@ class PipelineEngine:
                         recv(l - 1, s.idx)
             for s in slots:
                 m = s.idx
-                with _on(s_attn):
+                with _on(st_attn(m)):
                     recv(l - 1, m)
                     if ta:
                         ta.mark_start(EventType.ATTN_COMPUTE, l, m)
@@ -176,11 +213,17 @@ class PipelineEngine:
                     with _on(s_attn):
                         recv(l, m)
         logits = []
-        with _on(s_attn):
-            for s in slots:
+        for s in slots:
+            with _on(st_attn(s.idx)):
                 recv(L - 1, s.idx)
                 logits.append(attn.forward_lm_head(xs[s.idx], s.q_len, last_only=last_only,
                                                    wait=waits.pop(s.idx, None)))
+        with _on(s_attn):
+            if mb_streams is not None:
+                for s in mb_streams:
+                    s_attn.wait_stream(s)
+                for t in logits:
+                    t.record_stream(s_attn)
             out = torch.cat(logits, 0) if len(logits) > 1 else logits[0]
             if advance_cache:
                 cache.advance(plan.q_len)
