@@ -102,8 +102,13 @@ class PipelineEngine:
             tr.begin(plan)
         # fold each receive's wait into the consuming kernel, except when
         # timing: then the receive wait is its own (measured) span
+        # With one stream per micro-batch a receive is never folded: a folded
+        # wait spins inside a kernel whose CTAs can fill the GPU, starving the
+        # other micro-batch's stream -- on both ranks at once, a cycle. The
+        # stand-alone wait is one CTA and releases its dependents only once
+        # the flags arrive.
         if tr.fused:
-            tr.defer_waits = _DEFER_WAITS and not (ta or tf)
+            tr.defer_waits = _DEFER_WAITS and not (ta or tf) and mb_streams is None
         if has_ffn:
             m_.ffn_worker.tracker = tf
 

@@ -844,14 +844,17 @@ __global__ void signal_flags_kernel(FlagArgs a) {
 }
 
 // Waits until every flag >= value; bounded by timeout_ns (status on expiry).
+// The dependent launch is released only after the wait, so the next kernel's
+// CTAs do not sit on SMs while the flags are outstanding (with several
+// streams they would starve the other streams' kernels).
 __global__ void wait_flags_kernel(FlagArgs a) {
   pdl_wait();
-  pdl_trigger();
   if (threadIdx.x < a.n && blockIdx.x == 0) {
     const int v = a.value + (a.epoch != nullptr ? *a.epoch : 0);
     wait_flag_geq(a.flags[threadIdx.x], v, a.status, 100 + threadIdx.x, a.timeout_ns);
   }
   __syncthreads();
+  pdl_trigger();
 }
 
 // Copies `bytes` (multiple of 16) from src to every peer buffer with 16-byte
