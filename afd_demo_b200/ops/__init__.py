@@ -641,17 +641,8 @@ _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slo
 
 
 def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
-    return (_FUSED_GATE and T * top_k <= _GATE_MAX_ENTRIES and H <= 4096 and H % 8 == 0 and E <= 256
-            and E % 8 == 0 and top_k <= 16 and _gate_groups(T, E) > 0)
-
-
-def _gate_groups(T: int, E: int) -> int:
-    """Expert groups per token for the fused gate: enough CTAs (T * G ~ 256)
-    to spread the router weight reads, at least one expert per warp."""
-    g = 1
-    while T * g < 256 and E % (g * 2 * 8) == 0:
-        g *= 2
-    return g if E % g == 0 else 0
+    return (_FUSED_GATE and T * top_k <= _GATE_MAX_ENTRIES and H in (1024, 2048, 4096)
+            and E <= 256 and E % 8 == 0 and top_k <= 16)
 
 
 class _GateCounters:
@@ -689,9 +680,12 @@ class _AlignCounters(_GateCounters):
 
 def moe_gate(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor, top_k: int,
              eps: float, norm_topk_prob: bool = True, expert_start: int = 0,
-             n_local: Optional[int] = None) -> Tuple[torch.Tensor, "MoEWorkspace"]:
+             n_local: Optional[int] = None, stamps: Optional[torch.Tensor] = None
+             ) -> Tuple[torch.Tensor, "MoEWorkspace"]:
     """The fused decode gate alone (RMSNorm, router, top-k, routing): returns
-    the normalised input and the routing workspace (ids, weights, row blocks)."""
+    the normalised input and the routing workspace (ids, weights, row blocks).
+    `stamps` (int64 [8], zeroed) receives %globaltimer stamps of the kernel's
+    phases (diagnostics)."""
     T, H = h.shape
     E = w_router.shape[0]
     n_local = E if n_local is None else n_local
@@ -702,9 +696,9 @@ def moe_gate(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
     logits = torch.empty(T, E, device=h.device, dtype=h.dtype)
     ext().moe_gate(h, post_norm_w, w_router, xn, logits, ws.ids, ws.weights,
                    _GateCounters.get(h.device, T), top_k, bool(norm_topk_prob), float(eps),
-                   _gate_groups(T, E), expert_start, n_local, ws.block_n, ws.inv, ws.row_token,
+                   expert_start, n_local, ws.block_n, ws.inv, ws.row_token,
                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows,
-                   *_wait_args(None))
+                   *_wait_args(None), stamps)
     return xn, ws
 
 
@@ -742,9 +736,9 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
         logits = torch.empty(T, E, device=h.device, dtype=h.dtype)
         C.moe_gate(h, post_norm_w, w_router, xn, logits, ws.ids, ws.weights,
                    _GateCounters.get(h.device, T), top_k, bool(norm_topk_prob), float(eps),
-                   _gate_groups(T, E), expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
+                   expert_start, E_loc, ws.block_n, ws.inv, ws.row_token,
                    ws.row_weight, ws.expert_offsets, ws.blocks, ws.num_blocks, ws.num_rows,
-                   *_wait_args(wait))
+                   *_wait_args(wait), None)
         _check_routing(ws.ids, ws.weights, expert_start, E_loc, ws)
         mark(False, "router")
         mark(True, "experts")

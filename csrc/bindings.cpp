@@ -517,13 +517,14 @@ void moe_route(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, i
 // sizes); counters: int32 [>= T + 1], zeroed once and left zeroed
 void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w_router,
               at::Tensor& xn, at::Tensor& logits, at::Tensor& ids, at::Tensor& weights,
-              at::Tensor& counters, int64_t top_k, bool renorm, double eps, int64_t groups,
+              at::Tensor& counters, int64_t top_k, bool renorm, double eps,
               int64_t expert_start, int64_t n_local, int64_t block_n, at::Tensor& inv,
               at::Tensor& row_token, at::Tensor& row_weight, at::Tensor& expert_offsets,
               at::Tensor& blocks, at::Tensor& num_blocks, at::Tensor& num_rows,
               std::vector<int64_t> wait_flags, int64_t wait_value,
               const c10::optional<at::Tensor>& status, int64_t timeout_ns,
-              const c10::optional<at::Tensor>& epoch) {
+              const c10::optional<at::Tensor>& epoch,
+              const c10::optional<at::Tensor>& stamps) {
   TORCH_CHECK(h.stride(1) == 1 && xn.is_contiguous() && logits.is_contiguous() &&
                   w_router.is_contiguous(),
               "moe_gate: contiguous rows expected");
@@ -543,7 +544,9 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
   g.T = T;
   g.H = (int)h.size(1);
   g.E = (int)w_router.size(0);
-  g.G = (int)groups;
+  g.stamps = stamps.has_value()
+                 ? reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>())
+                 : nullptr;
   g.top_k = (int)top_k;
   g.renorm = renorm ? 1 : 0;
   g.eps = (float)eps;

@@ -266,6 +266,66 @@ __device__ __forceinline__ void topk_token(const __nv_bfloat16* logits, int E, i
   }
 }
 
+// topk_token on half a warp: lanes hl = 0..15 of the half own experts
+// hl + 16 i, so two tokens are ranked at once. Same picks, order, ties (the
+// lower expert index first) and weights as topk_token. Both halves must call
+// it together (the shuffles span the warp, 16 lanes wide); `store` = false
+// ranks without writing (a half with no token).
+__device__ __forceinline__ void topk_halfwarp(const __nv_bfloat16* logits, int E, int top_k,
+                                              int renorm, int hl, bool store, int32_t* ids_out,
+                                              float* w_out) {
+  constexpr int kMaxPer = 16;  // E <= 256
+  float v[kMaxPer];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = hl + 16 * i;
+    v[i] = e < E ? bf16_to_f(logits[e]) : -INFINITY;
+    m = fmaxf(m, v[i]);
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 16));
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = hl + 16 * i;
+    v[i] = e < E ? __expf(v[i] - m) : 0.f;
+    s += v[i];
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o, 16);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) v[i] *= inv;
+  float my_w = 0.f;
+  int my_e = 0;
+  float wsum = 0.f;
+  for (int k = 0; k < top_k; ++k) {
+    float best = -1.f;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = hl + 16 * i;
+      if (e < E && (v[i] > best || (v[i] == best && e < be))) { best = v[i]; be = e; }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o, 16);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o, 16);
+      if (ob > best || (ob == best && oe < be)) { best = ob; be = oe; }
+    }
+    if (hl == k) { my_w = best; my_e = be; }
+    wsum += best;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
+      if (hl + 16 * i == be) v[i] = -2.f;  // remove from further rounds
+  }
+  if (store && hl < top_k) {
+    ids_out[hl] = my_e;
+    w_out[hl] = my_w * (renorm ? 1.f / wsum : 1.f);
+  }
+}
+
 __global__ void router_topk_kernel(RouterArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -488,159 +548,295 @@ int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s)
 }
 
 // ------------------------------------------- fused MoE gate (decode) ---
-// Post-attention RMSNorm + router GEMV + softmax/top-k/renormalise + routing
-// in one launch for small token counts. CTA (t, g) normalises token t (same
-// roundings as sum_rmsnorm_kernel; group 0 stores xn), then computes the
-// router logits of experts [g * E/G, (g+1) * E/G) with CUDA-core dot products
-// (fp32 accumulation, one bf16 rounding). The last of a token's G CTAs (per-
-// token counter) runs that token's top-k; the last token to finish (global
-// counter) runs the routing of moe_align_kernel. Counters are reset by the
-// CTAs that consume them, so the buffer stays zeroed between launches.
+// Post-attention RMSNorm + router logits + softmax/top-k/renormalise +
+// routing in one launch for small token counts. CTA (tg, eg) takes the
+// token group tg (kGateTok tokens) and the NTC x 8 experts of group eg:
+//   1. it normalises the group's tokens into a shared-memory tile (same
+//      roundings as sum_rmsnorm_kernel; group 0 also stores xn for the expert
+//      GEMMs);
+//   2. router logits on the tensor cores: m16n8k16 tiles (16 tokens x 8
+//      experts), the CTA's 8 warps splitting the NTC tiles' K range, fp32
+//      accumulation, the warps' partial tiles summed in a fixed order, one
+//      bf16 rounding. Within each 32-wide chunk of H the k order is permuted
+//      so that a lane's A and B fragments of two k16 steps are 8 contiguous
+//      values: one 16-byte load per token row (shared) and per expert row
+//      (global). A and B are permuted alike and the summation order is
+//      fixed, so results are deterministic;
+//   3. the last of a token group's CTAs (per-group counter) runs its
+//      softmax / top-k / renormalise, a warp per token;
+//   4. the last group to finish (global counter) runs the routing of
+//      moe_align_kernel, with ids, weights and slots in shared memory.
+// Counters are reset by the CTAs that consume them. The CTAs are few and
+// short, so the gate also runs well on the handful of SMs another stream's
+// GEMMs leave free.
 constexpr int kGateThreads = 256;
-constexpr int kGateMaxH = 4096;
+constexpr int kGateTok = 16;
 constexpr int kGateMaxEntries = 2048;
 
-template <int kVec>  // router vectors per lane = H / 256
+__host__ __device__ constexpr int gate_row_bytes(int H) { return H * 2 + 64; }  // padded row
+
+static int moe_gate_smem_bytes(int H) {
+  const int tile = kGateTok * gate_row_bytes(H);
+  const int routing = kGateMaxEntries * 12;
+  return tile > routing ? tile : routing;
+}
+
+template <int H, int NTC>  // hidden size; n-tiles (8 experts each) per CTA
 __global__ void __launch_bounds__(kGateThreads) moe_gate_kernel(MoeGateArgs g, MoeAlignArgs a) {
-  __shared__ float xn_s[kGateMaxH];
-  __shared__ float red[kGateThreads / 32];
-  __shared__ __nv_bfloat16 lg_s[256];
+  constexpr int RB = gate_row_bytes(H);
+  constexpr int WPT = 8 / NTC;              // warps per n-tile
+  constexpr int KW = H / WPT;               // K range of one warp
+  constexpr int CH = KW / 32;               // 32-wide chunks per warp
+  constexpr int PB = CH < 8 ? CH : 8;       // chunks loaded per batch
+  static_assert(KW % 32 == 0, "K range per warp must be whole 32-wide chunks");
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ __align__(16) float red[8][32][4];                  // partial C fragments
+  __shared__ __nv_bfloat16 lg_s[kGateTok * 256];                 // a group's logits
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int off[kMaxLocalExperts + 1];
   __shared__ int boff[kMaxLocalExperts + 1];
-  __shared__ int32_t s_ids[kGateMaxEntries];
-  __shared__ float s_w[kGateMaxEntries];
   __shared__ int s_flag;
-  const int t = blockIdx.x / g.G;
-  const int grp = blockIdx.x % g.G;
-  const int H = g.H;
+  const int E = g.E;
+  const int n_eg = E / (8 * NTC);
+  const int tg = blockIdx.x / n_eg, eg = blockIdx.x % n_eg;
+  const int n_groups = (g.T + kGateTok - 1) / kGateTok;
+  const int t0 = tg * kGateTok;
+  const int nt = min(kGateTok, g.T - t0);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  constexpr int kChunks = (kVec + kGateThreads / 32 - 1) / (kGateThreads / 32);
-  // Static weights first, before waiting on the previous kernel: this warp's
-  // first router row and this thread's slice of the norm weight.
-  const int per_grp = g.E / g.G;
-  uint4 wv0[kVec];
+  const int r = lane >> 2, q = lane & 3;  // fragment row / k-quad
+  const int ntile = warp / WPT;            // this warp's n-tile within the CTA
+  const int kbase = (warp % WPT) * KW;     // and its K range
+  const int e0 = (eg * NTC + ntile) * 8;   // first expert of the n-tile
+
+  // static weights first (before waiting on the previous kernel): this
+  // lane's B fragments of the first PB chunks of its K range and its slice
+  // of the norm weight
+  constexpr int VPL = H / 256;  // 16-byte vectors per lane and row
+  const __nv_bfloat16* brow = g.w_router + (size_t)(e0 + r) * H + kbase + q * 8;
+  uint4 bv[PB], nwv[VPL];
 #pragma unroll
-  for (int c = 0; c < kVec; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    wv0[c] = (warp < per_grp && col < H)
-                 ? *reinterpret_cast<const uint4*>(g.w_router +
-                                                   (size_t)(grp * per_grp + warp) * H + col)
-                 : make_uint4(0, 0, 0, 0);
-  }
-  float nwt[kChunks][8];
+  for (int c = 0; c < PB; ++c) bv[c] = *reinterpret_cast<const uint4*>(brow + c * 32);
 #pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    const int col = (c * kGateThreads + threadIdx.x) * 8;
-    if (col < H) load8(g.norm_w + col, nwt[c]);
-  }
+  for (int c = 0; c < VPL; ++c)
+    nwv[c] = *reinterpret_cast<const uint4*>(g.norm_w + (c * 32 + lane) * 8);
+  // phase stamps (diagnostics): [0] start, [1] inputs ready, [2] normed,
+  // [3] logits of CTA 0, [4] latest logits of any CTA, [5] top-k of token
+  // group 0, [6] routing start, [7] routing end
+  const bool stamp0 = g.stamps != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
+  if (stamp0) g.stamps[0] = globaltimer_ns();
   pdl_wait();
   pdl_trigger();
   block_wait(g.wait, 140);
+  if (stamp0) g.stamps[1] = globaltimer_ns();
 
-  // 1. RMSNorm of token t
-  float xv[kChunks][8];
-  float ss = 0.f;
+  // 1. RMSNorm: warp w takes tokens w and w + 8 of the group (both rows
+  //    requested at once); rows past the batch are zero (their logits are
+  //    never used)
+  {
+    constexpr int NR = kGateTok / 8;  // rows per warp
+    uint4 hv[NR][VPL];
 #pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    const int col = (c * kGateThreads + threadIdx.x) * 8;
-    if (col < H) {
-      load8(g.h + (size_t)t * g.ld_h + col, xv[c]);
+    for (int i = 0; i < NR; ++i) {
+      const int tt = warp + 8 * i;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += xv[c][i] * xv[c][i];
+      for (int c = 0; c < VPL; ++c)
+        hv[i][c] = tt < nt ? *reinterpret_cast<const uint4*>(g.h + (size_t)(t0 + tt) * g.ld_h +
+                                                             (c * 32 + lane) * 8)
+                           : make_uint4(0, 0, 0, 0);
     }
-  }
-  const float tot = block_sum<kGateThreads>(ss, red);
-  const float rstd = rsqrtf(tot / (float)H + g.eps);
 #pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    const int col = (c * kGateThreads + threadIdx.x) * 8;
-    if (col < H) {
-      float y[8];
+    for (int i = 0; i < NR; ++i) {
+      const int tt = warp + 8 * i;
+      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        y[i] = round_bf16(nwt[c][i] * round_bf16(xv[c][i] * rstd));
-        xn_s[col + i] = y[i];
+      for (int c = 0; c < VPL; ++c) {
+        const uint32_t* pv = &hv[i][c].x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x0, x1;
+          unpack_bf16x2(pv[e], x0, x1);
+          ss += x0 * x0 + x1 * x1;
+        }
       }
-      if (grp == 0) store8(g.xn + (size_t)t * H + col, y);
+      ss = warp_sum(ss);
+      const float rstd = rsqrtf(ss / (float)H + g.eps);
+      uint8_t* dst = gsm + tt * RB;
+#pragma unroll
+      for (int c = 0; c < VPL; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        const uint32_t* pv = &hv[i][c].x;
+        const uint32_t* pw = &nwv[c].x;
+        uint4 o;
+        uint32_t* po = &o.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x0, x1, w0, w1;
+          unpack_bf16x2(pv[e], x0, x1);
+          unpack_bf16x2(pw[e], w0, w1);
+          po[e] = pack_bf16x2(w0 * round_bf16(x0 * rstd), w1 * round_bf16(x1 * rstd));
+        }
+        *reinterpret_cast<uint4*>(dst + col * 2) = o;  // zero rows stay zero
+        if (eg == 0 && tt < nt) *reinterpret_cast<uint4*>(g.xn + (size_t)(t0 + tt) * H + col) = o;
+      }
     }
   }
   __syncthreads();
+  if (stamp0) g.stamps[2] = globaltimer_ns();
 
-  // 2. router logits of this CTA's experts: warp w takes experts w, w + 8, ...
-  for (int j = warp; j < per_grp; j += kGateThreads / 32) {
-    const int e = grp * per_grp + j;
-    const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
-    // the row's vectors (H <= 4096: at most 16 per lane) are all requested
-    // before the dot product (the first row was requested before the wait)
-    uint4 wv[kVec];
+  // 2. router logits on the tensor cores
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const uint8_t* a_lo = gsm + r * RB + (kbase + q * 8) * 2;
+    const uint8_t* a_hi = gsm + (r + 8) * RB + (kbase + q * 8) * 2;
+#pragma unroll 1
+    for (int c0 = 0; c0 < CH; c0 += PB) {
+      if (c0 > 0) {
 #pragma unroll
-    for (int c = 0; c < kVec; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      wv[c] = j == warp ? wv0[c]
-                        : (col < H ? *reinterpret_cast<const uint4*>(wr + col)
-                                   : make_uint4(0, 0, 0, 0));
-    }
-    float acc = 0.f;
+        for (int c = 0; c < PB; ++c)
+          bv[c] = *reinterpret_cast<const uint4*>(brow + (c0 + c) * 32);
+      }
 #pragma unroll
-    for (int c = 0; c < kVec; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col >= H) break;
-      const uint32_t* pw = &wv[c].x;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float w0, w1;
-        unpack_bf16x2(pw[i], w0, w1);
-        acc += w0 * xn_s[col + 2 * i];
-        acc += w1 * xn_s[col + 2 * i + 1];
+      for (int c = 0; c < PB; ++c) {
+        const uint4 alo = *reinterpret_cast<const uint4*>(a_lo + (c0 + c) * 64);
+        const uint4 ahi = *reinterpret_cast<const uint4*>(a_hi + (c0 + c) * 64);
+        mma_16816_bf16(acc, alo.x, ahi.x, alo.y, ahi.y, bv[c].x, bv[c].y);
+        mma_16816_bf16(acc, alo.z, ahi.z, alo.w, ahi.w, bv[c].z, bv[c].w);
       }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
+  }
+  *reinterpret_cast<float4*>(&red[warp][lane][0]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  __syncthreads();
+  if (warp % WPT == 0) {
+    // the n-tile's first warp sums its WPT warps' partial tiles in warp order
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < WPT; ++w) {
+      const float4 v = *reinterpret_cast<const float4*>(&red[warp + w][lane][0]);
+      sum[0] += v.x;
+      sum[1] += v.y;
+      sum[2] += v.z;
+      sum[3] += v.w;
+    }
+    // C fragment: rows (tokens) r and r + 8, columns (experts) 2q and 2q + 1
+    const int e = e0 + 2 * q;
+    if (r < nt) {
+      g.logits[(size_t)(t0 + r) * E + e] = __float2bfloat16_rn(sum[0]);
+      g.logits[(size_t)(t0 + r) * E + e + 1] = __float2bfloat16_rn(sum[1]);
+    }
+    if (r + 8 < nt) {
+      g.logits[(size_t)(t0 + r + 8) * E + e] = __float2bfloat16_rn(sum[2]);
+      g.logits[(size_t)(t0 + r + 8) * E + e + 1] = __float2bfloat16_rn(sum[3]);
+    }
   }
 
-  // 3. the token's last CTA: softmax / top-k / renormalise
+  // 3. the token group's last CTA: softmax / top-k / renormalise, a warp per token
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[t], 1) == g.G - 1);
+  if (g.stamps != nullptr && threadIdx.x == 0) {
+    const unsigned long long now = globaltimer_ns();
+    if (blockIdx.x == 0) g.stamps[3] = now;
+    atomicMax(&g.stamps[4], now);
+  }
+  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[tg], 1) == n_eg - 1);
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  for (int e = threadIdx.x; e < g.E; e += kGateThreads)
-    lg_s[e] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
-                                          (size_t)t * g.E + e));
+  for (int i = threadIdx.x; i < nt * E; i += kGateThreads)
+    lg_s[i] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
+                                          (size_t)t0 * E + i));
   __syncthreads();
-  if (warp == 0)
-    topk_token(lg_s, g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
-               g.weights + (size_t)t * g.top_k);
-  if (threadIdx.x == 0) g.tok_cnt[t] = 0;
+  {
+    // half-warp h takes token h of the group: all 16 ranked at once
+    const int tt = threadIdx.x / 16;
+    const bool mine = tt < nt;
+    topk_halfwarp(lg_s + (mine ? tt : 0) * E, E, g.top_k, g.renorm, lane & 15, mine,
+                  g.ids + (size_t)(t0 + tt) * g.top_k, g.weights + (size_t)(t0 + tt) * g.top_k);
+  }
+  if (threadIdx.x == 0) g.tok_cnt[tg] = 0;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == g.T - 1);
+  if (g.stamps != nullptr && threadIdx.x == 0 && tg == 0) g.stamps[5] = globaltimer_ns();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == n_groups - 1);
   __syncthreads();
   if (!s_flag) return;
 
-  // 4. the last token: routing over all T tokens
+  // 4. the last group: routing over all T tokens (ids, weights and the
+  //    provisional slots stay in shared memory)
   __threadfence();
+  if (g.stamps != nullptr && threadIdx.x == 0) g.stamps[6] = globaltimer_ns();
+  int32_t* s_ids = reinterpret_cast<int32_t*>(gsm);
+  float* s_w = reinterpret_cast<float*>(gsm + kGateMaxEntries * 4);
+  int* s_slot = reinterpret_cast<int*>(gsm + kGateMaxEntries * 8);
   const int n = g.T * g.top_k;
+  for (int e = threadIdx.x; e < a.n_local; e += kGateThreads) cnt[e] = 0;
   for (int i = threadIdx.x; i < n; i += kGateThreads) {
     s_ids[i] = __ldcg(g.ids + i);
     s_w[i] = __ldcg(g.weights + i);
   }
   __syncthreads();
-  align_body(s_ids, s_w, a, cnt, off, boff);
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    const int e = s_ids[i] - a.expert_start;
+    s_slot[i] = (e >= 0 && e < a.n_local) ? atomicAdd(&cnt[e], 1) : -1;
+  }
+  __syncthreads();
+  scan_and_blocks(cnt, off, boff, a);
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    const int slot = s_slot[i];
+    int row = -1;
+    if (slot >= 0) {
+      row = off[s_ids[i] - a.expert_start] + slot;
+      a.row_token[row] = i / a.top_k;
+      a.row_weight[row] = s_w[i];
+    }
+    a.inv[i] = row;
+  }
   if (threadIdx.x == 0) *g.done_cnt = 0;
+  if (g.stamps != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) g.stamps[7] = globaltimer_ns();
+  }
+}
+
+// n-tiles per CTA: enough CTAs (token groups x expert groups, about 128) to
+// spread the router reads, at most 8 tiles (one per warp)
+static int gate_ntc(int T, int E) {
+  const int n_tg = (T + kGateTok - 1) / kGateTok;
+  int ntc = 1;
+  while (ntc < 8 && (E / (8 * ntc)) % 2 == 0 && n_tg * (E / (8 * ntc)) > 128) ntc *= 2;
+  return ntc;
+}
+
+template <int H, int NTC>
+static int gate_launch(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
+  const int smem = moe_gate_smem_bytes(H);
+  const cudaError_t e =
+      set_max_dynamic_smem(reinterpret_cast<const void*>(moe_gate_kernel<H, NTC>), smem);
+  if (e != cudaSuccess) return (int)e;
+  const dim3 grid(((g.T + kGateTok - 1) / kGateTok) * (g.E / (8 * NTC))), block(kGateThreads);
+  return (int)launch_k(moe_gate_kernel<H, NTC>, grid, block, smem, s, g, a);
+}
+
+template <int H>
+static int gate_launch_h(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
+  switch (gate_ntc(g.T, g.E)) {
+    case 1: return gate_launch<H, 1>(g, a, s);
+    case 2: return gate_launch<H, 2>(g, a, s);
+    case 4: return gate_launch<H, 4>(g, a, s);
+    default: return gate_launch<H, 8>(g, a, s);
+  }
 }
 
 int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
-  if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % g.G != 0 ||
-      g.top_k > 16 || g.H > kGateMaxH || g.H % 8 != 0 || a.n_local > kMaxLocalExperts ||
-      a.block_n <= 0)
+  if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % 8 != 0 ||
+      g.top_k > 16 || a.n_local > kMaxLocalExperts || a.block_n <= 0)
     return 1;
-  const dim3 grid(g.T * g.G), block(kGateThreads);
-  if (g.H <= 1024) return (int)launch_k(moe_gate_kernel<4>, grid, block, 0, s, g, a);
-  if (g.H <= 2048) return (int)launch_k(moe_gate_kernel<8>, grid, block, 0, s, g, a);
-  return (int)launch_k(moe_gate_kernel<16>, grid, block, 0, s, g, a);
+  if ((g.E / 8) % gate_ntc(g.T, g.E) != 0) return 1;
+  switch (g.H) {
+    case 1024: return gate_launch_h<1024>(g, a, s);
+    case 2048: return gate_launch_h<2048>(g, a, s);
+    case 4096: return gate_launch_h<4096>(g, a, s);
+    default: return 1;
+  }
 }
 
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
