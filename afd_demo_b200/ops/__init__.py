@@ -196,19 +196,32 @@ def _wave_splits(units: int, k_iters: int, gain: float = 1.1) -> int:
     return 2 if eff(2 * units) >= gain * eff(units) else 1
 
 
-# upper bound of the split-K factor (AFD_MAX_SPLITS for A/B measurements)
+# upper bound of the split-K factor of the dense decode GEMMs (AFD_MAX_SPLITS for A/B)
 _MAX_SPLITS = int(os.environ.get("AFD_MAX_SPLITS", "16"))
 
 
-def _k_splits(tiles: int, k_iters: int) -> int:
-    """Split-K factor for GEMMs with too few output tiles to fill the GPU:
-    the largest power of two with tiles * s <= SMs and >= 2 k-steps per split."""
-    s = 1
+def _decode_tiling(T: int, N: int, K: int) -> Tuple[int, int]:
+    """(token block, split-K factor) of a decode-sized dense GEMM (T <= 256),
+    from a sweep of every combination on B200 for the qkv and o_proj shapes:
+    64-row token blocks unless that leaves more tiles than SMs (then 128).
+    With fewer than 40 tiles, the split that brings the units to about 128
+    with at least 8 k-steps each; with more, a split of two only when each
+    half still streams 32 k-steps (a split's partial store and last-CTA
+    reduction cost more than shorter streams gain)."""
     n = num_sms()
-    while (tiles * s * 2 <= n and k_iters % (s * 2) == 0 and k_iters // (s * 2) >= 2
-           and s * 2 <= _MAX_SPLITS):
-        s *= 2
-    return s
+    bn = 64
+    while bn < 256 and T > bn and ((T + bn - 1) // bn) * (N // 128) > n:
+        bn *= 2
+    tiles = ((T + bn - 1) // bn) * (N // 128)
+    k_iters = K // 64
+    s = 1
+    if tiles < 40:
+        while (s * 2 <= _MAX_SPLITS and tiles * s * 2 <= 128 and k_iters % (s * 2) == 0
+               and k_iters // (s * 2) >= 8):
+            s *= 2
+    elif tiles * 2 <= n and k_iters % 2 == 0 and k_iters // 2 >= 32 and _MAX_SPLITS >= 2:
+        s = 2
+    return bn, s
 
 
 class _SplitKWorkspace:
@@ -255,15 +268,16 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         out = torch.empty(T, N, device=x.device, dtype=x.dtype)
     if N % 128 != 0:
         raise ValueError(f"linear: output features {N} must be a multiple of 128")
-    bn = _block_n(T)
+    if T <= 256:
+        bn, splits = _decode_tiling(T, N, K)
+    else:
+        bn, splits = _block_n(T), 1
     tiles = ((T + bn - 1) // bn) * (N // 128)
     if T > 256 and 2 * tiles <= num_sms():
         # few output features (e.g. the router) over many tokens: narrower
         # token tiles spread the work over more SMs than split-K would
         bn = 64
         tiles = ((T + bn - 1) // bn) * (N // 128)
-    # split-K only at decode sizes (small partial tiles), when tiles leave SMs idle
-    splits = _k_splits(tiles, K // 64) if T <= 256 else 1
     ws = cnt = None
     if splits > 1:
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)

@@ -568,7 +568,8 @@ int launch_moe_route(const RouterArgs& r, const MoeAlignArgs& a, cudaStream_t s)
 //      moe_align_kernel, with ids, weights and slots in shared memory.
 // Counters are reset by the CTAs that consume them. The CTAs are few and
 // short, so the gate also runs well on the handful of SMs another stream's
-// GEMMs leave free.
+// GEMMs leave free. Up to kGateTokMaxT tokens the per-token kernel below runs
+// instead (it finishes sooner there; phase stamps come from this kernel only).
 constexpr int kGateThreads = 256;
 constexpr int kGateTok = 16;
 constexpr int kGateMaxEntries = 2048;
@@ -826,10 +827,166 @@ static int gate_launch_h(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream
   }
 }
 
+// ------------------------------------- fused MoE gate, per-token CTAs ---
+// The gate for the smallest batches (up to kGateTokMaxT tokens), where one
+// CTA per (token, expert group) finishes sooner than the tiled kernel below:
+// CTA (t, g) normalises token t (group 0 stores xn) and computes the router
+// logits of experts [g * E/G, (g+1) * E/G) with CUDA-core dot products (fp32
+// accumulation, one bf16 rounding); the last of a token's G CTAs runs its
+// top-k; the last token runs the routing of moe_align_kernel.
+constexpr int kGateTokMaxT = 32;
+constexpr int kGateTokMaxH = 4096;
+
+template <int kVec>  // router vectors per lane = H / 256
+__global__ void __launch_bounds__(kGateThreads) moe_gate_token_kernel(MoeGateArgs g, MoeAlignArgs a) {
+  __shared__ float xn_s[kGateTokMaxH];
+  __shared__ float red[kGateThreads / 32];
+  __shared__ __nv_bfloat16 lg_s[256];
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int off[kMaxLocalExperts + 1];
+  __shared__ int boff[kMaxLocalExperts + 1];
+  __shared__ int32_t s_ids[kGateMaxEntries];
+  __shared__ float s_w[kGateMaxEntries];
+  __shared__ int s_flag;
+  const int t = blockIdx.x / g.G;
+  const int grp = blockIdx.x % g.G;
+  const int H = g.H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int kChunks = (kVec + kGateThreads / 32 - 1) / (kGateThreads / 32);
+  // Static weights first, before waiting on the previous kernel: this warp's
+  // first router row and this thread's slice of the norm weight.
+  const int per_grp = g.E / g.G;
+  uint4 wv0[kVec];
+#pragma unroll
+  for (int c = 0; c < kVec; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    wv0[c] = (warp < per_grp && col < H)
+                 ? *reinterpret_cast<const uint4*>(g.w_router +
+                                                   (size_t)(grp * per_grp + warp) * H + col)
+                 : make_uint4(0, 0, 0, 0);
+  }
+  float nwt[kChunks][8];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) load8(g.norm_w + col, nwt[c]);
+  }
+  pdl_wait();
+  pdl_trigger();
+  block_wait(g.wait, 140);
+
+  // 1. RMSNorm of token t
+  float xv[kChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) {
+      load8(g.h + (size_t)t * g.ld_h + col, xv[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += xv[c][i] * xv[c][i];
+    }
+  }
+  const float tot = block_sum<kGateThreads>(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + g.eps);
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * kGateThreads + threadIdx.x) * 8;
+    if (col < H) {
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        y[i] = round_bf16(nwt[c][i] * round_bf16(xv[c][i] * rstd));
+        xn_s[col + i] = y[i];
+      }
+      if (grp == 0) store8(g.xn + (size_t)t * H + col, y);
+    }
+  }
+  __syncthreads();
+
+  // 2. router logits of this CTA's experts: warp w takes experts w, w + 8, ...
+  for (int j = warp; j < per_grp; j += kGateThreads / 32) {
+    const int e = grp * per_grp + j;
+    const __nv_bfloat16* wr = g.w_router + (size_t)e * H;
+    // the row's vectors (H <= 4096: at most 16 per lane) are all requested
+    // before the dot product (the first row was requested before the wait)
+    uint4 wv[kVec];
+#pragma unroll
+    for (int c = 0; c < kVec; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      wv[c] = j == warp ? wv0[c]
+                        : (col < H ? *reinterpret_cast<const uint4*>(wr + col)
+                                   : make_uint4(0, 0, 0, 0));
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kVec; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col >= H) break;
+      const uint32_t* pw = &wv[c].x;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float w0, w1;
+        unpack_bf16x2(pw[i], w0, w1);
+        acc += w0 * xn_s[col + 2 * i];
+        acc += w1 * xn_s[col + 2 * i + 1];
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) g.logits[(size_t)t * g.E + e] = __float2bfloat16_rn(acc);
+  }
+
+  // 3. the token's last CTA: softmax / top-k / renormalise
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(&g.tok_cnt[t], 1) == g.G - 1);
+  __syncthreads();
+  if (!s_flag) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < g.E; e += kGateThreads)
+    lg_s[e] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(g.logits) +
+                                          (size_t)t * g.E + e));
+  __syncthreads();
+  if (warp == 0)
+    topk_token(lg_s, g.E, g.top_k, g.renorm, lane, g.ids + (size_t)t * g.top_k,
+               g.weights + (size_t)t * g.top_k);
+  if (threadIdx.x == 0) g.tok_cnt[t] = 0;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_flag = (atomicAdd(g.done_cnt, 1) == g.T - 1);
+  __syncthreads();
+  if (!s_flag) return;
+
+  // 4. the last token: routing over all T tokens
+  __threadfence();
+  const int n = g.T * g.top_k;
+  for (int i = threadIdx.x; i < n; i += kGateThreads) {
+    s_ids[i] = __ldcg(g.ids + i);
+    s_w[i] = __ldcg(g.weights + i);
+  }
+  __syncthreads();
+  align_body(s_ids, s_w, a, cnt, off, boff);
+  if (threadIdx.x == 0) *g.done_cnt = 0;
+}
+
+static int launch_moe_gate_token(MoeGateArgs g, const MoeAlignArgs& a, cudaStream_t s) {
+  // expert groups: enough CTAs (T * G ~ 256) to spread the router reads, at
+  // least one expert per warp
+  int G = 1;
+  while (g.T * G < 256 && g.E % (G * 2 * 8) == 0) G *= 2;
+  if (g.E % G != 0 || g.H > kGateTokMaxH || g.H % 8 != 0) return 1;
+  g.G = G;
+  const dim3 grid(g.T * G), block(kGateThreads);
+  if (g.H <= 1024) return (int)launch_k(moe_gate_token_kernel<4>, grid, block, 0, s, g, a);
+  if (g.H <= 2048) return (int)launch_k(moe_gate_token_kernel<8>, grid, block, 0, s, g, a);
+  return (int)launch_k(moe_gate_token_kernel<16>, grid, block, 0, s, g, a);
+}
+
 int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s) {
   if (g.T <= 0 || g.T * g.top_k > kGateMaxEntries || g.E > 256 || g.E % 8 != 0 ||
       g.top_k > 16 || a.n_local > kMaxLocalExperts || a.block_n <= 0)
     return 1;
+  if (g.T <= kGateTokMaxT && g.stamps == nullptr) return launch_moe_gate_token(g, a, s);
   if ((g.E / 8) % gate_ntc(g.T, g.E) != 0) return 1;
   switch (g.H) {
     case 1024: return gate_launch_h<1024>(g, a, s);

@@ -127,9 +127,10 @@ struct MoeGateArgs {
   __nv_bfloat16* logits;         // [T, E] scratch
   int32_t* ids;                  // [T, top_k] (out)
   float* weights;                // [T, top_k] (out)
-  int* tok_cnt;                  // [ceil(T / 16)] zeroed, self-cleaning
+  int* tok_cnt;                  // [T] zeroed, self-cleaning
   int* done_cnt;                 // [1] zeroed, self-cleaning
   int T, H, E, top_k, renorm;
+  int G;                         // expert groups of the per-token kernel (set by the launcher)
   unsigned long long* stamps;    // optional [8] %globaltimer stamps of the phases (diagnostics)
   float eps;
   FlagWait wait;                 // h produced by peers (optional)
