@@ -90,7 +90,8 @@ def main(argv=None) -> int:
     ap.add_argument("--json", default="")
     ap.add_argument("--sections", default="decode,attention,prefill",
                     help="comma list of: decode (per-layer decode kernels by token count), "
-                         "attention (decode attention over long caches), prefill")
+                         "attention (decode attention over long caches), prefill, tiling "
+                         "(every token-block / split-K choice of the qkv and o_proj GEMMs)")
     ap.add_argument("--attn-batches", default="16,64")
     ap.add_argument("--attn-kv", default="256,1024,2048,4096")
     a = ap.parse_args(argv)
@@ -163,6 +164,43 @@ def main(argv=None) -> int:
                timeit(lambda i: ops.moe_ffn(h, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
                                             1e-6), a.iters, a.warmup),
                eb + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
+
+    # token-block / split-K sweep of the decode-sized dense GEMMs (the table the
+    # tiling rule of ops.linear was read from)
+    if "tiling" in sections:
+        C = ops.ext()
+        for name, (N, K) in {"qkv": (QKV, H), "o_proj": (H, nq * D)}.items():
+            n_w = copies_for(N * K * 2)
+            wl = [rnd(N, K) for _ in range(n_w)]
+            for T in [int(t) for t in a.tokens.split(",")]:
+                x = rnd(T, K, scale=1.0)
+                out = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+                res = {}
+                for bn in (64, 128, 256):
+                    if bn > 64 and bn // 2 >= T:
+                        continue
+                    tiles = ((T + bn - 1) // bn) * (N // 128)
+                    for sp in (1, 2, 4, 8, 16):
+                        if (K // 64) % sp or K // 64 // sp < 2 or tiles * sp > 4 * 148:
+                            continue
+                        wsp = cnt = None
+                        if sp > 1:
+                            wsp, cnt = ops._SplitKWorkspace.get(x.device, tiles, bn, sp)
+
+                        def f(i, bn=bn, sp=sp, tiles=tiles, wsp=wsp, cnt=cnt):
+                            C.gemm(wl[i % n_w], x, out, N // 128, N, 0, None, None, T, None, None,
+                                   False, bn, tiles * sp, [], 0, [], 0, None, None, None, sp, wsp,
+                                   cnt, None)
+                        res[(bn, sp)] = timeit(f, 20, 3)
+                chosen = ops._decode_tiling(T, N, K) if T <= 256 else None
+                best = min(res, key=res.get)
+                print(f"tiling {name:6s} T={T:4d} chosen {chosen} "
+                      f"{res.get(chosen, float('nan')):6.2f} us, best {best} {res[best]:6.2f} us | "
+                      + " ".join(f"{b}/{sp}:{u:.1f}" for (b, sp), u in sorted(res.items())),
+                      flush=True)
+                rows.append({"op": f"tiling {name}", "tokens": T, "chosen": list(chosen or ()),
+                             "best": list(best),
+                             "us": {f"{b}/{sp}": round(u, 2) for (b, sp), u in res.items()}})
 
     # decode attention over long caches: tcgen05 kernel vs the mma.sync kernel
     for B in ([int(b) for b in a.attn_batches.split(",")] if "attention" in sections else []):
