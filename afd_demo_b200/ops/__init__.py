@@ -650,7 +650,9 @@ _GATE_MAX_ENTRIES = 2048  # routed (token, k) pairs handled by the fused gate ke
 # sequence, AFD_FUSED_COMBINE=1 the combine inside the down GEMM's epilogue.
 _FUSED_GATE = os.environ.get("AFD_FUSED_GATE", "1") != "0"
 _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine, then bulk copy
-_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "1") != "0"  # wave-balancing split-K of the decode expert GEMMs
+# wave-balancing split-K of the decode expert GEMMs: measured slower (a split's
+# partial store and reduction cost more than the fuller last wave gains), so opt-in
+_GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slower (esp. with peers)
 
 

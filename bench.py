@@ -187,7 +187,7 @@ def measure_cells(model, args, B, S, T, local, world, timed, ctx):
             row = {}
             for name, dbo in (("dbo_crosslayer", True), ("serial", False)):
                 gen(ids, dbo)  # warm: graphs for this batch
-                _, tp = mx([gen(ids, dbo)[1]])
+                tp = mx([gen(ids, dbo)[1]])[0]
                 row[name + "_tpot_ms"] = tp
                 row[name + "_tok_s"] = 1000.0 * b / tp
             row["dbo_speedup"] = row["serial_tpot_ms"] / row["dbo_crosslayer_tpot_ms"]
