@@ -94,6 +94,8 @@ def main(argv=None) -> int:
                          "(every token-block / split-K choice of the qkv and o_proj GEMMs)")
     ap.add_argument("--attn-batches", default="16,64")
     ap.add_argument("--attn-kv", default="256,1024,2048,4096")
+    ap.add_argument("--prefill-attn-seqs", default="256",
+                    help="prompt lengths of the prefill attention rows (batch = tokens / length)")
     a = ap.parse_args(argv)
     sections = set(a.sections.split(","))
     dev = torch.device("cuda")
@@ -253,15 +255,17 @@ def main(argv=None) -> int:
            timeit(lambda i: ops.moe_ffn(hp, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
                                         1e-6), max(5, a.iters // 5), 2),
            E * 3 * I * H * 2 + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
-    S = 256
-    B = T // S
-    q = rnd(T, nq, D, scale=1.0)
-    kc = rnd(B, nkv, S, D, scale=1.0)
-    vc = rnd(B, nkv, S, D, scale=1.0)
     pos0 = torch.zeros(1, device=dev, dtype=torch.int32)
-    report(f"prefill attention S={S}", T,
-           timeit(lambda i: ops.attention(q, kc, vc, 0, S, 0, pos0), max(5, a.iters // 5), 2),
-           (T * nq * D * 2) * 2 + 2 * B * nkv * S * D * 2, 2 * 2 * B * nq * S * S * D / 2)
+    for S in [int(v) for v in a.prefill_attn_seqs.split(",")]:
+        B = max(1, T // S)
+        q = rnd(B * S, nq, D, scale=1.0)
+        kc = rnd(B, nkv, S, D, scale=1.0)
+        vc = rnd(B, nkv, S, D, scale=1.0)
+        # causal: half of the S x S score matrix, two products (QK^T and PV)
+        report(f"prefill attention S={S}", B * S,
+               timeit(lambda i: ops.attention(q, kc, vc, 0, S, 0, pos0), max(5, a.iters // 5), 2),
+               (B * S * nq * D * 2) * 2 + 2 * B * nkv * S * D * 2, 2 * 2 * B * nq * S * S * D / 2)
+        del q, kc, vc
     if a.json:
         os.makedirs(os.path.dirname(os.path.abspath(a.json)), exist_ok=True)
         json.dump({"peaks": {"hbm_Bps": bw, "bf16_flops": fl, "basis": tag}, "rows": rows},
