@@ -4,13 +4,17 @@ Reference: scripts/experiment_baselines.py:22-79. A prefill (TTFT) comparison
 uses the serial run's ``prefill_ms``; a decode (TPOT) comparison uses its
 ``decode_tpot_ms``. Legacy fields (``decode_step_ms``, ``total_time_ms /
 tokens``) are never used as a baseline.
+
+The result record (``BaselineResolution``) and its ``source`` tags are the
+interface the report, audit and Gantt scripts read, so they keep the
+reference's names; the rule itself is the table ``_RULES`` below.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Any, Mapping, Optional
+from typing import Any, Mapping, NamedTuple, Optional, Tuple
 
 
 @dataclass(frozen=True)
@@ -25,16 +29,29 @@ class BaselineResolution:
         return self.value_ms is not None and self.value_ms > 0
 
 
+class _Rule(NamedTuple):
+    key: str                    # the serial-cache field that is the baseline
+    unit: str                   # what it measures
+    legacy: Tuple[str, ...]     # fields that look like a baseline but are not one
+    missing: str                # warning when `key` is absent
+
+
+# comparison class -> how its serial baseline is found
+_RULES = {
+    "prefill": _Rule("prefill_ms", "TTFT", (),
+                     "TTFT baseline missing; a TPOT-style total is not comparable"),
+    "decode": _Rule("decode_tpot_ms", "TPOT", ("decode_step_ms",),
+                    "exact TPOT baseline missing"),
+}
+
+
 def normalize_mode(mode: Optional[str]) -> Optional[str]:
-    """'prefill' / 'decode' comparison class of a mode or directory name."""
+    """'prefill' / 'decode' comparison class of a mode or directory name
+    (the first class whose name occurs in it; prefill before decode)."""
     if not mode:
         return None
     m = mode.lower().replace("_", "-")
-    if "prefill" in m:
-        return "prefill"
-    if "decode" in m:
-        return "decode"
-    return None
+    return next((cls for cls in _RULES if cls in m), None)
 
 
 def infer_mode_from_path(path) -> Optional[str]:
@@ -42,23 +59,17 @@ def infer_mode_from_path(path) -> Optional[str]:
 
 
 def resolve_serial_baseline(cache: Mapping[str, Any], mode: Optional[str]) -> BaselineResolution:
-    mode = normalize_mode(mode)
-    if mode == "prefill":
-        v = cache.get("prefill_ms")
-        if v is not None:
-            return BaselineResolution(float(v), "TTFT", "prefill_ms")
-        return BaselineResolution(None, None, "missing",
-                                  "TTFT baseline missing; a TPOT-style total is not comparable")
-    if mode == "decode":
-        v = cache.get("decode_tpot_ms")
-        if v is not None:
-            return BaselineResolution(float(v), "TPOT", "decode_tpot_ms")
-        if cache.get("decode_step_ms") is not None:
-            return BaselineResolution(None, None, "legacy-decode-step-ms",
-                                      "decode_tpot_ms missing; legacy decode_step_ms not used")
-        return BaselineResolution(None, None, "missing", "exact TPOT baseline missing")
-    return BaselineResolution(None, None, "unknown-mode",
-                              "could not infer prefill/decode comparison mode")
+    rule = _RULES.get(normalize_mode(mode))
+    if rule is None:
+        return BaselineResolution(None, None, "unknown-mode",
+                                  "could not infer prefill/decode comparison mode")
+    if cache.get(rule.key) is not None:
+        return BaselineResolution(float(cache[rule.key]), rule.unit, rule.key)
+    for old in rule.legacy:
+        if cache.get(old) is not None:
+            return BaselineResolution(None, None, "legacy-" + old.replace("_", "-"),
+                                      f"{rule.key} missing; legacy {old} not used")
+    return BaselineResolution(None, None, "missing", rule.missing)
 
 
 def serial_cache_path(root: Path, batch, seq, tokens) -> Path:

@@ -402,7 +402,16 @@ def main():
                if model.ctx.is_attention_node else 0,
                "api": "DisaggregatedQwenModel.generate(host_io=True, use_cuda_graph=True)"}
 
-    cells = measure_cells(model, args, B, S, T, local, world, timed, ctx) if cells_on else None
+    cells = None
+    if cells_on:
+        # the cells are extra keys: an error in one (the same on every rank,
+        # e.g. a batch the topology cannot split) must not cost the headline line
+        try:
+            cells = measure_cells(model, args, B, S, T, local, world, timed, ctx)
+        except Exception as e:  # noqa: BLE001
+            print(f"bench: cells skipped: {type(e).__name__}: {e}", file=sys.stderr)
+            cells = {"error": f"{type(e).__name__}: {e}"[:300]}
+            model.release_graphs()
 
     value = 1000.0 * B / tpot_xl
     ref = REF_XL_TPOT_S256.get(B) if (S == 256 and headline) else None
