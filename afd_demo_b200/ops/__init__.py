@@ -307,6 +307,12 @@ def qk_norm_rope_cache(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Te
 # query heads per kv head; other shapes use the mma.sync kernels), "mma" =
 # the mma.sync fused kernel and the split-KV SIMT kernel (A/B measurements).
 _DECODE_ATTN = os.environ.get("AFD_DECODE_ATTN", "tc")
+# prefill attention kernel: "tc" = tcgen05, two query heads of a kv group per
+# CTA (one per CTA when the group is odd), "tc1" = tcgen05 with one head per
+# CTA, "mma" = the mma.sync kernel (A/B measurements; padding masks always
+# take the mma.sync kernel)
+_PREFILL_ATTN = os.environ.get("AFD_PREFILL_ATTN", "tc1")
+_PREFILL_VARIANT = {"tc": 0, "tc1": 1, "mma": 2}
 _DECODE_TILE = 128  # keys per tile of the tcgen05 decode kernel
 
 # cost model of the tcgen05 decode kernel, in units of one 128-key tile's
@@ -452,7 +458,7 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, bat
     else:
         lo, hi = key_range if key_range is not None else (None, None)
         ext().prefill_attention(q, k_cache, v_cache, out, start_pos_dev, q_len, batch_offset,
-                                lo, hi)
+                                lo, hi, _PREFILL_VARIANT[_PREFILL_ATTN])
     return out.view(T, nq * D)
 
 

@@ -90,14 +90,20 @@ def main(argv=None) -> int:
     ap.add_argument("--json", default="")
     ap.add_argument("--sections", default="decode,attention,prefill",
                     help="comma list of: decode (per-layer decode kernels by token count), "
-                         "attention (decode attention over long caches), prefill, tiling "
+                         "attention (decode attention over long caches), prefill (prefill "
+                         "GEMMs and attention), prefill_attn (prefill attention only), tiling "
                          "(every token-block / split-K choice of the qkv and o_proj GEMMs)")
     ap.add_argument("--attn-batches", default="16,64")
     ap.add_argument("--attn-kv", default="256,1024,2048,4096")
     ap.add_argument("--prefill-attn-seqs", default="256",
                     help="prompt lengths of the prefill attention rows (batch = tokens / length)")
+    ap.add_argument("--prefill-attn-variants", default=None,
+                    help="prefill attention kernels to time: tc (two heads per CTA), tc1, mma "
+                         "(default: the op layer's choice)")
     a = ap.parse_args(argv)
     sections = set(a.sections.split(","))
+    if a.prefill_attn_variants is None:
+        a.prefill_attn_variants = ops._PREFILL_ATTN
     dev = torch.device("cuda")
     bw, fl, tag = peaks()
     H, I, E, k, nq, nkv, D = 2048, 768, 128, 8, 32, 4, 128
@@ -234,7 +240,7 @@ def main(argv=None) -> int:
                 ops._DECODE_ATTN = saved
             del kcs, vcs
 
-    if "prefill" not in sections:
+    if "prefill" not in sections and "prefill_attn" not in sections:
         if a.json:
             os.makedirs(os.path.dirname(os.path.abspath(a.json)), exist_ok=True)
             json.dump({"peaks": {"hbm_Bps": bw, "bf16_flops": fl, "basis": tag}, "rows": rows},
@@ -242,29 +248,38 @@ def main(argv=None) -> int:
         return 0
     # prefill-sized dense GEMM and attention
     T = a.prefill_tokens
-    xp = rnd(T, H, scale=1.0)
-    report("linear qkv (prefill)", T,
-           timeit(lambda i: ops.linear(xp, w_qkv[i % n_qkv]), max(5, a.iters // 5), 2),
-           QKV * H * 2 + T * (H + QKV) * 2, 2 * T * H * QKV)
-    op = rnd(T, nq * D, scale=1.0)
-    report("linear o_proj + residual (prefill)", T,
-           timeit(lambda i: ops.linear(op, w_o[i % n_o], residual=xp), max(5, a.iters // 5), 2),
-           H * nq * D * 2 + T * (nq * D + 2 * H) * 2, 2 * T * H * nq * D)
-    hp = rnd(T, H, scale=1.0)
-    report("moe block (prefill)", T,
-           timeit(lambda i: ops.moe_ffn(hp, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e], k,
-                                        1e-6), max(5, a.iters // 5), 2),
-           E * 3 * I * H * 2 + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
+    if "prefill" in sections:
+        xp = rnd(T, H, scale=1.0)
+        report("linear qkv (prefill)", T,
+               timeit(lambda i: ops.linear(xp, w_qkv[i % n_qkv]), max(5, a.iters // 5), 2),
+               QKV * H * 2 + T * (H + QKV) * 2, 2 * T * H * QKV)
+        op = rnd(T, nq * D, scale=1.0)
+        report("linear o_proj + residual (prefill)", T,
+               timeit(lambda i: ops.linear(op, w_o[i % n_o], residual=xp), max(5, a.iters // 5), 2),
+               H * nq * D * 2 + T * (nq * D + 2 * H) * 2, 2 * T * H * nq * D)
+        hp = rnd(T, H, scale=1.0)
+        report("moe block (prefill)", T,
+               timeit(lambda i: ops.moe_ffn(hp, pn, w_r[i % n_qkv], w_gu[i % n_e], w_dn[i % n_e],
+                                            k, 1e-6), max(5, a.iters // 5), 2),
+               E * 3 * I * H * 2 + E * H * 2, 2 * T * k * 3 * I * H + 2 * T * E * H)
+        del xp, op, hp
+    # prefill attention at each prompt length, each kernel variant
     pos0 = torch.zeros(1, device=dev, dtype=torch.int32)
+    default_variant = ops._PREFILL_ATTN
     for S in [int(v) for v in a.prefill_attn_seqs.split(",")]:
         B = max(1, T // S)
         q = rnd(B * S, nq, D, scale=1.0)
         kc = rnd(B, nkv, S, D, scale=1.0)
         vc = rnd(B, nkv, S, D, scale=1.0)
-        # causal: half of the S x S score matrix, two products (QK^T and PV)
-        report(f"prefill attention S={S}", B * S,
-               timeit(lambda i: ops.attention(q, kc, vc, 0, S, 0, pos0), max(5, a.iters // 5), 2),
-               (B * S * nq * D * 2) * 2 + 2 * B * nkv * S * D * 2, 2 * 2 * B * nq * S * S * D / 2)
+        for variant in a.prefill_attn_variants.split(","):
+            ops._PREFILL_ATTN = variant
+            # causal: half of the S x S score matrix, two products (QK^T and PV)
+            report(f"prefill attention S={S} [{variant}]", B * S,
+                   timeit(lambda i: ops.attention(q, kc, vc, 0, S, 0, pos0), max(5, a.iters // 5),
+                          2),
+                   (B * S * nq * D * 2) * 2 + 2 * B * nkv * S * D * 2,
+                   2 * 2 * B * nq * S * S * D / 2)
+        ops._PREFILL_ATTN = default_variant
         del q, kc, vc
     if a.json:
         os.makedirs(os.path.dirname(os.path.abspath(a.json)), exist_ok=True)

@@ -5,6 +5,8 @@ Qwen3-30B-A3B shapes, for a profiler (ncu) to capture one launch:
     python -m afd_demo_b200.scripts.kernel_probe decode_attn 64 2048   # batch, kv length
     python -m afd_demo_b200.scripts.kernel_probe linear qkv 128         # or o_proj; tokens
     python -m afd_demo_b200.scripts.kernel_probe gate 128 32            # tokens, local experts
+    python -m afd_demo_b200.scripts.kernel_probe moe 8192               # tokens (MoE block)
+    python -m afd_demo_b200.scripts.kernel_probe prefill_attn 2048 4    # prompt length, batch
 
     ncu --set full --clock-control none -k regex:<kernel> -s 2 -c 1 -o out \\
         python -m afd_demo_b200.scripts.kernel_probe ...
@@ -30,7 +32,7 @@ H, I, E, TOPK, NQ, NKV, D = 2048, 768, 128, 8, 32, 4, 128
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("op", choices=["decode_attn", "linear", "gate"])
+    ap.add_argument("op", choices=["decode_attn", "linear", "gate", "moe", "prefill_attn"])
     ap.add_argument("args", nargs="*")
     ap.add_argument("--calls", type=int, default=4)
     a = ap.parse_args(argv)
@@ -53,6 +55,17 @@ def main(argv=None) -> int:
         else:
             w, x, r = rnd(H, NQ * D, scale=0.02), rnd(T, NQ * D), rnd(T, H)
             fn = lambda: ops.linear(x, w, residual=r)  # noqa: E731
+    elif a.op == "moe":
+        T, I_ = int(a.args[0]), 768
+        h, wr = rnd(T, H), rnd(E, H, scale=0.02)
+        pn = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        wgu, wdn = rnd(E, 2 * I_, H, scale=0.02), rnd(E, H, I_, scale=0.02)
+        fn = lambda: ops.moe_ffn(h, pn, wr, wgu, wdn, TOPK, 1e-6)  # noqa: E731
+    elif a.op == "prefill_attn":
+        S, B = int(a.args[0]), int(a.args[1]) if len(a.args) > 1 else 1
+        q, kc, vc = rnd(B * S, NQ, D), rnd(B, NKV, S, D), rnd(B, NKV, S, D)
+        pos = torch.zeros(1, device=dev, dtype=torch.int32)
+        fn = lambda: ops.attention(q, kc, vc, 0, S, 0, pos)  # noqa: E731
     else:
         T, e_loc = int(a.args[0]), int(a.args[1]) if len(a.args) > 1 else E
         h, wr = rnd(T, H), rnd(E, H, scale=0.02)

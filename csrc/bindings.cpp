@@ -381,7 +381,7 @@ void decode_attention_fused(const at::Tensor& qkv, const at::Tensor& q_norm,
 void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                        at::Tensor& out, const at::Tensor& start_pos, int64_t q_len,
                        int64_t batch_offset, const c10::optional<at::Tensor>& key_lo,
-                       const c10::optional<at::Tensor>& key_hi) {
+                       const c10::optional<at::Tensor>& key_hi, int64_t variant) {
   afd::PrefillAttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);
@@ -405,14 +405,13 @@ void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at:
     a.key_lo = key_lo->data_ptr<int>();
     a.key_hi = key_hi->data_ptr<int>();
   }
-  // tcgen05 kernel for head_dim 128 without a padding mask; AFD_PREFILL_ATTN=mma
-  // selects the mma.sync kernel (A/B measurements), which also takes key ranges
-  static const bool use_mma = [] {
-    const char* e = std::getenv("AFD_PREFILL_ATTN");
-    return e != nullptr && std::string(e) == "mma";
-  }();
-  if (a.D == 128 && !use_mma && !masked)
-    check_rc(afd::launch_prefill_attention_tc(a, B, cur_stream()), "prefill_attention_tc");
+  // variant 0: tcgen05 kernel for head_dim 128 without a padding mask, two
+  // heads per CTA when the GQA group is even; 1: tcgen05, one head per CTA;
+  // 2: the mma.sync kernel (which also takes key ranges)
+  TORCH_CHECK(variant >= 0 && variant <= 2, "prefill_attention: variant 0, 1 or 2");
+  if (a.D == 128 && variant != 2 && !masked)
+    check_rc(afd::launch_prefill_attention_tc(a, B, cur_stream(), variant == 0),
+             "prefill_attention_tc");
   else
     check_rc(afd::launch_prefill_attention(a, B, cur_stream()), "prefill_attention");
 }

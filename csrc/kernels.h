@@ -238,6 +238,9 @@ int decode_tc_supported(int nq, int nkv, int D);
 int launch_decode_attention_tc(const DecodeTcArgs& a, int grid, cudaStream_t s);
 int launch_prefill_attention(const PrefillAttnArgs& a, int B, cudaStream_t s);
 // tcgen05/TMEM/TMA version (attention_tc.cu), head_dim 128
-int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s);
+// pair_heads: two query heads of one kv group per CTA (ping-pong softmax,
+// P in TMEM) when nq / nkv is even; otherwise one head per CTA
+int launch_prefill_attention_tc(const PrefillAttnArgs& a, int B, cudaStream_t s,
+                                bool pair_heads = true);
 
 }  // namespace afd

@@ -382,6 +382,39 @@ def test_moe_experts_no_local_rows(with_residual):
     assert torch.equal(out, want)
 
 
+@pytest.mark.parametrize("variant", ["tc", "tc1", "mma"])
+@pytest.mark.parametrize("B,q_len,start,off", [(2, 300, 0, 1), (1, 257, 100, 0), (1, 2048, 0, 0)])
+def test_prefill_attention_kernels(B, q_len, start, off, variant, monkeypatch):
+    """Each prefill kernel against the fp32 oracle: tcgen05 with two query
+    heads per CTA (P in TMEM), tcgen05 with one head per CTA, mma.sync."""
+    monkeypatch.setattr(ops, "_PREFILL_ATTN", variant)
+    nq, nkv, D = 32, 4, 128
+    S = max(1024, start + q_len)
+    kc = _randn(B + off, nkv, S, D, seed=53)
+    vc = _randn(B + off, nkv, S, D, seed=54)
+    q = _randn(B * q_len, nq, D, seed=55)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), off, q_len, start)
+    out = ops.attention(q, kc, vc, off, q_len, start, pos)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("nq,nkv", [(8, 8), (12, 4), (16, 2)])
+@pytest.mark.parametrize("variant", ["tc", "tc1"])
+def test_prefill_attention_gqa_groups(nq, nkv, variant, monkeypatch):
+    """Group sizes 1 and 3 (one head per CTA) and 8 (head pairs) with a
+    query tile that straddles the cache's earlier keys."""
+    monkeypatch.setattr(ops, "_PREFILL_ATTN", variant)
+    B, q_len, start, D, S = 2, 200, 60, 128, 512
+    kc = _randn(B, nkv, S, D, seed=56)
+    vc = _randn(B, nkv, S, D, seed=57)
+    q = _randn(B * q_len, nq, D, seed=58)
+    pos = torch.tensor([start], device=DEV, dtype=torch.int32)
+    ref = torch_ref.attention(q.float(), kc.float(), vc.float(), 0, q_len, start)
+    out = ops.attention(q, kc, vc, 0, q_len, start, pos)
+    assert _rel(out, ref) < 1e-2
+
+
 def test_prefill_attention_long_sequence():
     """A 2048-token causal prefill (16 key tiles per query tile)."""
     nq, nkv, D, S, q_len = 32, 4, 128, 2048, 2048
