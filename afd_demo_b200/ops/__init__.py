@@ -311,7 +311,7 @@ _DECODE_ATTN = os.environ.get("AFD_DECODE_ATTN", "tc")
 # CTA (one per CTA when the group is odd), "tc1" = tcgen05 with one head per
 # CTA, "mma" = the mma.sync kernel (A/B measurements; padding masks always
 # take the mma.sync kernel)
-_PREFILL_ATTN = os.environ.get("AFD_PREFILL_ATTN", "tc1")
+_PREFILL_ATTN = os.environ.get("AFD_PREFILL_ATTN", "tc")
 _PREFILL_VARIANT = {"tc": 0, "tc1": 1, "mma": 2}
 _DECODE_TILE = 128  # keys per tile of the tcgen05 decode kernel
 
