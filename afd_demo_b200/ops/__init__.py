@@ -169,8 +169,17 @@ def _block_n(rows: int) -> int:
     return 64 if rows <= 64 else (128 if rows <= 128 else 256)
 
 
-# row-block size of prefill-sized grouped GEMMs (AFD_MOE_BN_LARGE=128 for A/B)
+# row-block size of prefill-sized grouped GEMMs (AFD_MOE_BN_LARGE=256 for A/B)
 _MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "128"))
+# prefill-sized expert GEMMs (at least this many routed rows per local expert on
+# average, 128-row blocks) run on the token-major kernel; AFD_MOE_TM=0 keeps
+# them on the swap-AB kernel (A/B measurements)
+_MOE_TM = os.environ.get("AFD_MOE_TM", "1") != "0"
+_MOE_TM_MIN_ROWS = 96
+# AFD_DENSE_TM=1: prefill-sized dense GEMMs (more than 256 rows, output
+# features a multiple of 256) on the token-major kernel too (A/B measurements;
+# by default they run on the swap-AB kernel with 256-row token tiles)
+_DENSE_TM = os.environ.get("AFD_DENSE_TM", "0") == "1"
 
 
 def _moe_block_n(rows: int) -> int:
@@ -268,12 +277,16 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         out = torch.empty(T, N, device=x.device, dtype=x.dtype)
     if N % 128 != 0:
         raise ValueError(f"linear: output features {N} must be a multiple of 128")
+    tm = False
     if T <= 256:
         bn, splits = _decode_tiling(T, N, K)
+    elif _DENSE_TM and N % 256 == 0:
+        # token-major kernel: 128 token rows x 256 features per tile
+        bn, splits, tm = 128, 1, True
     else:
         bn, splits = _block_n(T), 1
     tiles = ((T + bn - 1) // bn) * (N // 128)
-    if T > 256 and 2 * tiles <= num_sms():
+    if T > 256 and not tm and 2 * tiles <= num_sms():
         # few output features (e.g. the router) over many tokens: narrower
         # token tiles spread the work over more SMs than split-K would
         bn = 64
@@ -283,7 +296,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)
     ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn,
                tiles * splits, list(peers), int(peer_row_offset), list(flags), int(signal_value),
-               done_counter, status, epoch, splits, ws, cnt, None)
+               done_counter, status, epoch, splits, ws, cnt, None, tm)
     return out
 
 
@@ -517,12 +530,16 @@ _FUSED_COMBINE_MAX_TOKENS = 256
 
 
 def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T, k, peers,
-                       seg_offsets, peer_row_offset, flags, signal_value, done_counter, epoch):
+                       seg_offsets, peer_row_offset, flags, signal_value, done_counter, epoch,
+                       n_experts=None):
     """Grouped gate_up GEMM (SwiGLU epilogue) -> grouped down GEMM
     (routing-weight epilogue) -> combine (+ residual, + peer stores). For
     decode-sized batches the gate_up producer gathers token rows straight from
     xn with TMA tile::gather4; prefill-sized batches gather once into expert
-    order so the producer issues one TMA box per 32 rows."""
+    order so the producer issues one TMA box per 32 rows (swap-AB kernel) or
+    per 128 rows (token-major kernel, when the experts average at least
+    _MOE_TM_MIN_ROWS rows; `n_experts` = the router's expert count, default
+    the local one)."""
     C = ext()
     E_loc, I2, H = w_gate_up.shape
     I = I2 // 2
@@ -545,9 +562,13 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     gws = gcnt = None
     if gu_splits > 1:
         gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, gu_splits)
+    # prefill-sized: full 128-row blocks on the token-major kernel (128 x 256 MMAs,
+    # row-segment epilogue); decode-sized: the swap-AB kernel
+    tm = (_MOE_TM and bn == 128 and row_ids is None
+          and T * k >= _MOE_TM_MIN_ROWS * (n_experts or E_loc))
     C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
            0, None, None, True, bn, max_tiles * gu_splits, [], 0, [], 0, None, None, None,
-           gu_splits, gws, gcnt, row_ids)
+           gu_splits, gws, gcnt, row_ids, tm)
     if out is None and not peers:
         out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
     if _FUSED_COMBINE and T <= _FUSED_COMBINE_MAX_TOKENS:
@@ -564,7 +585,7 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
         dws, dcnt = _SplitKWorkspace.get(xn.device, dn_tiles, bn, dn_splits)
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
            None, ws.row_weight, False, bn, dn_tiles * dn_splits, [], 0, [], 0, None, None,
-           None, dn_splits, dws, dcnt, None)
+           None, dn_splits, dws, dcnt, None, tm)
     if peers and _SPLIT_F2A and T > _FUSED_COMBINE_MAX_TOKENS:
         # prefill sizes: combine locally, then one bulk peer copy per attention
         # rank's segment (the combine kernel's scattered NVLink stores run at
@@ -766,7 +787,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
         mark(True, "experts")
         y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T,
                                top_k, peers, seg_offsets, peer_row_offset, flags, signal_value,
-                               done_counter, epoch)
+                               done_counter, epoch, n_experts=E)
         mark(False, "experts")
         return y
     xn = sum_rmsnorm([h], post_norm_w, eps, wait=wait)[1]
@@ -783,7 +804,7 @@ def moe_ffn(h: torch.Tensor, post_norm_w: torch.Tensor, w_router: torch.Tensor,
     mark(True, "experts")
     y = _moe_gemms_combine(xn, ws, w_gate_up, w_down, h if add_residual else None, out, T, top_k,
                            peers, seg_offsets, peer_row_offset, flags, signal_value,
-                           done_counter, epoch)
+                           done_counter, epoch, n_experts=E)
     mark(False, "experts")
     return y
 
@@ -800,7 +821,7 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     bn = _block_n(T)
     units = ((T + bn - 1) // bn) * (I // 128)
     ext().gemm(w_gate_up, xn, act, I // 128, I2, I, None, None, T, None, None, True, bn, units,
-               [], 0, [], 0, None, None, None, 1, None, None, None)
+               [], 0, [], 0, None, None, None, 1, None, None, None, False)
     return linear(act, w_down, residual=residual)
 
 

@@ -198,7 +198,7 @@ def main(argv=None) -> int:
                         def f(i, bn=bn, sp=sp, tiles=tiles, wsp=wsp, cnt=cnt):
                             C.gemm(wl[i % n_w], x, out, N // 128, N, 0, None, None, T, None, None,
                                    False, bn, tiles * sp, [], 0, [], 0, None, None, None, sp, wsp,
-                                   cnt, None)
+                                   cnt, None, False)
                         res[(bn, sp)] = timeit(f, 20, 3)
                 chosen = ops._decode_tiling(T, N, K) if T <= 256 else None
                 best = min(res, key=res.get)

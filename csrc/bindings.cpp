@@ -66,7 +66,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
           const c10::optional<at::Tensor>& done_counter, const c10::optional<at::Tensor>& status,
           const c10::optional<at::Tensor>& epoch, int64_t k_splits,
           const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters,
-          const c10::optional<at::Tensor>& row_ids) {
+          const c10::optional<at::Tensor>& row_ids, bool token_major) {
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
@@ -125,6 +125,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
   p.block_n = (int)block_n;
   p.units_hint = (int)units_hint;
   p.num_sms = g_sm_cap > 0 ? std::min(num_sms(), g_sm_cap) : num_sms();
+  p.token_major = token_major;
   if (a.blocks == nullptr && dense_rows == 0) return;
   check_rc(afd::gemm_swapab_launch(p, cur_stream()), "gemm_swapab");
 }

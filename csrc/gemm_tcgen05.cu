@@ -576,6 +576,7 @@ static cudaError_t launch_variant(const CUtensorMap& tw, const CUtensorMap& tx, 
 }
 
 int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
+  if (p.token_major && gemm_tm_eligible(p)) return gemm_tm_launch(p, stream);
   if (p.args.K % kBK != 0) return 1001;
   if (p.w_rows_total <= 0) return 1002;
   if (p.block_n != 64 && p.block_n != 128 && p.block_n != 256) return 1003;

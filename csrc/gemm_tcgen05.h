@@ -79,9 +79,16 @@ struct GemmLaunch {
   int block_n;              // 64 (decode-sized) or 256
   int units_hint;           // upper bound on work units (<= 0: unknown)
   int num_sms;
+  // token-major kernel (gemm_tm.cu) for block_n 128 when its epilogue
+  // covers the call (no split-K, gathered rows or fused combine)
+  bool token_major;
 };
 
 // Returns 0 on success, a non-zero code describing the failure otherwise.
 int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream);
+
+// Token-major variant (gemm_tm.cu): whether it takes this call, and its launcher.
+bool gemm_tm_eligible(const GemmLaunch& p);
+int gemm_tm_launch(const GemmLaunch& p, cudaStream_t stream);
 
 }  // namespace afd

@@ -24,8 +24,8 @@ NVCC_FLAGS = [
 if os.environ.get("AFD_BOUNDS_CHECK"):
     NVCC_FLAGS.append("-DAFD_BOUNDS_CHECK=1")
 
-SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "kernels.cu", "attention.cu", "attention_tc.cu",
-           "decode_attention_tc.cu", "noalloc.cu"]
+SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "gemm_tm.cu", "kernels.cu", "attention.cu",
+           "attention_tc.cu", "decode_attention_tc.cu", "noalloc.cu"]
 
 setup(
     name="afd_demo_b200",

@@ -39,6 +39,21 @@ def test_dense_gemm(T, N, K):
     assert _rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("T", [300, 1000, 4096])
+def test_dense_gemm_token_major(T, monkeypatch):
+    """Prefill-sized dense GEMM (+ residual) on the token-major kernel, ragged
+    last row block included."""
+    monkeypatch.setattr(ops, "_DENSE_TM", True)
+    K, N = 4096, 2048
+    x = _randn(T, K, seed=29)
+    w = _randn(N, K, scale=0.02, seed=30)
+    r = _randn(T, N, seed=31)
+    ref = x.float() @ w.float().t() + r.float()
+    assert _rel(ops.linear(x, w, residual=r), ref) < 1e-2
+    ref = x.float() @ w.float().t()
+    assert _rel(ops.linear(x, w), ref) < 1e-2
+
+
 @pytest.mark.parametrize("T", [3, 64, 200])
 def test_dense_gemm_residual(T):
     K, N = 4096, 2048
@@ -69,8 +84,30 @@ def test_moe_experts(T, E, k):
     assert _rel(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("tm", [True, False])
+@pytest.mark.parametrize("T,E_loc,start", [(2048, 128, 0), (1600, 128, 0), (3000, 32, 32),
+                                           (4096, 64, 64)])
+def test_moe_experts_prefill_kernels(T, E_loc, start, tm, monkeypatch):
+    """Prefill-sized expert GEMMs on the token-major kernel (128 x 256 MMAs,
+    one token row per TMEM lane) and on the swap-AB kernel, against the fp32
+    statement: full and ragged 128-row blocks, expert-parallel slices."""
+    monkeypatch.setattr(ops, "_MOE_TM", tm)
+    H, I, E, k = 2048, 768, 128, 8
+    xn = _randn(T, H, seed=25)
+    h = _randn(T, H, seed=26)
+    wgu = _randn(E_loc, 2 * I, H, scale=0.02, seed=27)
+    wd = _randn(E_loc, H, I, scale=0.02, seed=28)
+    probs = torch.randn(T, E, device=DEV).softmax(-1)
+    w, ids = probs.topk(k, -1)
+    w = (w / w.sum(-1, keepdim=True)).float()
+    ids = ids.to(torch.int32)
+    ref = torch_ref.moe_experts(xn, ids, w, wgu, wd, start).float() + h.float()
+    out = ops.moe_experts(xn, ids, w, wgu, wd, start, residual=h)
+    assert _rel(out, ref) < 2e-2
+
+
 @pytest.mark.parametrize("T,E_loc,start", [(1, 128, 0), (16, 128, 0), (64, 128, 0), (300, 128, 0),
-                                           (1024, 128, 0), (48, 32, 32)])
+                                           (1024, 128, 0), (48, 32, 32), (2048, 128, 0)])
 def test_moe_ffn_block(T, E_loc, start):
     """RMSNorm + router + fused top-k/routing + gathered grouped GEMMs + combine."""
     H, I, E = 2048, 768, 128
