@@ -176,10 +176,10 @@ _MOE_BN_LARGE = int(os.environ.get("AFD_MOE_BN_LARGE", "128"))
 # them on the swap-AB kernel (A/B measurements)
 _MOE_TM = os.environ.get("AFD_MOE_TM", "1") != "0"
 _MOE_TM_MIN_ROWS = 96
-# AFD_DENSE_TM=1: prefill-sized dense GEMMs (more than 256 rows, output
-# features a multiple of 256) on the token-major kernel too (A/B measurements;
-# by default they run on the swap-AB kernel with 256-row token tiles)
-_DENSE_TM = os.environ.get("AFD_DENSE_TM", "0") == "1"
+# prefill-sized dense GEMMs (more than 256 rows, output features a multiple of
+# 256) on the token-major kernel: "residual" (default) = those with a residual
+# add (o_proj), "all", or "none" = all on the swap-AB kernel (A/B measurements)
+_DENSE_TM = os.environ.get("AFD_DENSE_TM", "residual")
 
 
 def _moe_block_n(rows: int) -> int:
@@ -280,8 +280,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
     tm = False
     if T <= 256:
         bn, splits = _decode_tiling(T, N, K)
-    elif _DENSE_TM and N % 256 == 0:
-        # token-major kernel: 128 token rows x 256 features per tile
+    elif N % 256 == 0 and (_DENSE_TM == "all" or (_DENSE_TM == "residual" and
+                                                   residual is not None)):
+        # token-major kernel: 128 token rows x 256 features per tile; its
+        # row-segment epilogue reads the residual row by row (o_proj: 0.72 of
+        # the bf16 peak at 8192 tokens against 0.58 on the swap-AB kernel,
+        # whose transposing epilogue the residual slows; qkv, without a
+        # residual, is faster on the swap-AB kernel's 256-token tiles)
         bn, splits, tm = 128, 1, True
     else:
         bn, splits = _block_n(T), 1

@@ -541,6 +541,7 @@ __global__ void __launch_bounds__(kP2Threads, 1)
     const int qq = warp & 3;              // TMEM lane quarter of this warp
     const int row = qq * 32 + lane;
     const int pos = start + q0 + row;
+    const int warp_pos0 = start + q0 + qq * 32;  // the position of this warp's first row
     const uint32_t lane_off = (uint32_t)(qq * 32) << 16;
     const uint32_t t_s = tmem + x * kTcBN, t_o = tmem + 2 * kTcBN + x * kTcD;
     const float scale_log2 = rsqrtf((float)kTcD) * 1.4426950408889634f;
@@ -555,20 +556,21 @@ __global__ void __launch_bounds__(kP2Threads, 1)
       }
       tc_fence_after();
       float s[kTcBN];
-#pragma unroll
-      for (int c = 0; c < kTcBN / 32; ++c) {
-        float t[32];
-        tmem_ld32(t_s + lane_off + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
+      tmem_ld128(t_s + lane_off, s);  // four loads, one wait
       const int key0 = j * kTcBN;
       float rmax = -INFINITY;
+      // warp-uniform: every key of the tile is visible to every row of this
+      // warp (the tile lies below the diagonal and inside the sequence)
+      if (key0 + kTcBN - 1 <= warp_pos0 && key0 + kTcBN <= kv_len) {
 #pragma unroll
-      for (int i = 0; i < kTcBN; ++i) {
-        const int key = key0 + i;
-        if (key > pos || key >= kv_len) s[i] = -INFINITY;
-        rmax = fmaxf(rmax, s[i]);
+        for (int i = 0; i < kTcBN; ++i) rmax = fmaxf(rmax, s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kTcBN; ++i) {
+          const int key = key0 + i;
+          if (key > pos || key >= kv_len) s[i] = -INFINITY;
+          rmax = fmaxf(rmax, s[i]);
+        }
       }
       rmax *= scale_log2;  // the max in log2 units (m is kept in these)
       // lazy max: move it only when it grows by more than 8 (log2 units)

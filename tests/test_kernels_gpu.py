@@ -43,7 +43,7 @@ def test_dense_gemm(T, N, K):
 def test_dense_gemm_token_major(T, monkeypatch):
     """Prefill-sized dense GEMM (+ residual) on the token-major kernel, ragged
     last row block included."""
-    monkeypatch.setattr(ops, "_DENSE_TM", True)
+    monkeypatch.setattr(ops, "_DENSE_TM", "all")
     K, N = 4096, 2048
     x = _randn(T, K, seed=29)
     w = _randn(N, K, scale=0.02, seed=30)
