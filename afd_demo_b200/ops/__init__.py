@@ -301,7 +301,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         ws, cnt = _SplitKWorkspace.get(x.device, tiles, bn, splits)
     ext().gemm(w, x, out, N // 128, N, 0, None, None, T, residual, None, False, bn,
                tiles * splits, list(peers), int(peer_row_offset), list(flags), int(signal_value),
-               done_counter, status, epoch, splits, ws, cnt, None, tm)
+               done_counter, status, epoch, splits, ws, cnt, None, tm, False)
     return out
 
 
@@ -564,16 +564,20 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
     est_blocks = min(E_loc, T * k)
     gu_splits = _wave_splits(est_blocks * (I // 128), H // 64) if (decode and _GU_SPLIT) else 1
     dn_splits = _wave_splits(est_blocks * (H // 128), I // 64) if (decode and _GU_SPLIT) else 1
+    # decode sizes: stream-K scheduling of the expert GEMMs (equal k-iteration
+    # ranges per CTA; the few tiles a range boundary cuts are reduced in two
+    # pieces), so the grid's last wave is not left half empty
+    sk = _STREAM_K and decode and gu_splits == 1 and dn_splits == 1
     gws = gcnt = None
-    if gu_splits > 1:
-        gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, gu_splits)
+    if gu_splits > 1 or sk:
+        gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, max(gu_splits, 2))
     # prefill-sized: full 128-row blocks on the token-major kernel (128 x 256 MMAs,
     # row-segment epilogue); decode-sized: the swap-AB kernel
     tm = (_MOE_TM and bn == 128 and row_ids is None
           and T * k >= _MOE_TM_MIN_ROWS * (n_experts or E_loc))
     C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
            0, None, None, True, bn, max_tiles * gu_splits, [], 0, [], 0, None, None, None,
-           gu_splits, gws, gcnt, row_ids, tm)
+           gu_splits, gws, gcnt, row_ids, tm, sk)
     if out is None and not peers:
         out = torch.empty(T, H, device=xn.device, dtype=xn.dtype)
     if _FUSED_COMBINE and T <= _FUSED_COMBINE_MAX_TOKENS:
@@ -586,11 +590,11 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
         return out
     dws = dcnt = None
     dn_tiles = ws.max_blocks * (H // 128)
-    if dn_splits > 1:
-        dws, dcnt = _SplitKWorkspace.get(xn.device, dn_tiles, bn, dn_splits)
+    if dn_splits > 1 or sk:
+        dws, dcnt = _SplitKWorkspace.get(xn.device, dn_tiles, bn, max(dn_splits, 2))
     C.gemm(w_down.view(E_loc * H, I), ws.act, ws.y, H // 128, H, 0, ws.blocks, ws.num_blocks, 0,
            None, ws.row_weight, False, bn, dn_tiles * dn_splits, [], 0, [], 0, None, None,
-           None, dn_splits, dws, dcnt, None, tm)
+           None, dn_splits, dws, dcnt, None, tm, sk)
     if peers and _SPLIT_F2A and T > _FUSED_COMBINE_MAX_TOKENS:
         # prefill sizes: combine locally, then one bulk peer copy per attention
         # rank's segment (the combine kernel's scattered NVLink stores run at
@@ -686,6 +690,8 @@ _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine
 # partial store and reduction cost more than the fuller last wave gains), so opt-in
 _GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slower (esp. with peers)
+# AFD_STREAM_K=0: round-robin tiles for the decode expert GEMMs (A/B measurements)
+_STREAM_K = os.environ.get("AFD_STREAM_K", "1") != "0"
 
 
 def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
@@ -826,7 +832,7 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     bn = _block_n(T)
     units = ((T + bn - 1) // bn) * (I // 128)
     ext().gemm(w_gate_up, xn, act, I // 128, I2, I, None, None, T, None, None, True, bn, units,
-               [], 0, [], 0, None, None, None, 1, None, None, None, False)
+               [], 0, [], 0, None, None, None, 1, None, None, None, False, False)
     return linear(act, w_down, residual=residual)
 
 

@@ -165,6 +165,18 @@ def main(argv=None) -> int:
                timeit(lambda i: ops.moe_experts(x, ids, wts, w_gu[i % n_e], w_dn[i % n_e], 0,
                                                 residual=h), a.iters, a.warmup),
                eb, 2 * T * k * 3 * I * H)
+        for e_loc in (32, 64):
+            # one FFN rank of expert parallelism (4 or 2 FFN ranks): experts 0..e_loc-1
+            # of the same routing; bytes = the local experts hit
+            hit = int((torch.unique(ids) < e_loc).sum())
+            wg, wdn = w_gu[0][:e_loc].contiguous(), w_dn[0][:e_loc].contiguous()
+            wg2, wdn2 = w_gu[1][:e_loc].contiguous(), w_dn[1][:e_loc].contiguous()
+            pair = [(wg, wdn), (wg2, wdn2)]
+            report(f"moe experts EP{e_loc} ({hit} hit)", T,
+                   timeit(lambda i: ops.moe_experts(x, ids, wts, pair[i % 2][0], pair[i % 2][1], 0,
+                                                    residual=h), a.iters, a.warmup),
+                   hit * 3 * I * H * 2, 2 * T * k * 3 * I * H * e_loc / E)
+            del wg, wdn, wg2, wdn2, pair
         report("moe gate (norm+router+top-k+routing)", T,
                timeit(lambda i: ops.moe_gate(h, pn, w_r[i % n_qkv], k, 1e-6), a.iters, a.warmup),
                E * H * 2 + 2 * T * H * 2, 2 * T * E * H)
@@ -198,7 +210,7 @@ def main(argv=None) -> int:
                         def f(i, bn=bn, sp=sp, tiles=tiles, wsp=wsp, cnt=cnt):
                             C.gemm(wl[i % n_w], x, out, N // 128, N, 0, None, None, T, None, None,
                                    False, bn, tiles * sp, [], 0, [], 0, None, None, None, sp, wsp,
-                                   cnt, None, False)
+                                   cnt, None, False, False)
                         res[(bn, sp)] = timeit(f, 20, 3)
                 chosen = ops._decode_tiling(T, N, K) if T <= 256 else None
                 best = min(res, key=res.get)

@@ -66,7 +66,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
           const c10::optional<at::Tensor>& done_counter, const c10::optional<at::Tensor>& status,
           const c10::optional<at::Tensor>& epoch, int64_t k_splits,
           const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters,
-          const c10::optional<at::Tensor>& row_ids, bool token_major) {
+          const c10::optional<at::Tensor>& row_ids, bool token_major, bool stream_k) {
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
@@ -114,6 +114,17 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
                 "split-K workspace too small");
     TORCH_CHECK(a.tile_counters != nullptr && tile_counters->numel() >= tiles,
                 "split-K tile counters too small");
+  }
+  if (stream_k) {
+    // grouped only; two pieces per tile at most; units_hint bounds the tiles
+    TORCH_CHECK(a.blocks != nullptr && k_splits <= 1 && units_hint > 0,
+                "stream-K: grouped GEMM without split-K, with a tile bound");
+    TORCH_CHECK(a.ws != nullptr && ws->numel() >= 2 * units_hint * block_n * 128 *
+                                                      (swiglu ? 2 : 1),
+                "stream-K workspace too small");
+    TORCH_CHECK(a.tile_counters != nullptr && tile_counters->numel() >= units_hint,
+                "stream-K tile counters too small");
+    a.stream_k = 1;
   }
   p.w = w.data_ptr();
   p.w_rows_total = w.numel() / K;

@@ -87,6 +87,52 @@ struct Unit {
 };
 __device__ __forceinline__ Unit unit_of(int u, int tiles) { return {u % tiles, u / tiles}; }
 
+// The k-ranges this CTA works on, in order: (tile, k0, k1) plus the tile's
+// piece index and piece count. Round-robin mode: units (tile, split) dealt
+// round-robin, `splits` equal K ranges per tile. Stream-K mode: the
+// tiles x total_k k-iterations are cut into gridDim.x contiguous ranges of
+// equal length (each at least one tile long), so every CTA streams the same
+// number of weight tiles; a tile cut by a range boundary has two pieces,
+// whose partial sums the later-finishing CTA adds in piece order.
+struct SegIter {
+  bool sk;
+  long long u, hi;      // stream-K: next k-iteration, end of this CTA's range
+  int units, tiles, total_k, k_iters, splits;
+  __device__ SegIter(bool stream_k, int tiles_, int total_k_, int splits_)
+      : sk(stream_k), tiles(tiles_), total_k(total_k_), splits(splits_) {
+    k_iters = total_k / splits;
+    units = tiles * splits;
+    if (sk) {
+      const long long U = (long long)tiles * total_k;
+      u = U * blockIdx.x / gridDim.x;
+      hi = U * (blockIdx.x + 1) / gridDim.x;
+    } else {
+      u = blockIdx.x;
+      hi = units;
+    }
+  }
+  __device__ bool next(int& tile, int& k0, int& k1, int& piece, int& pieces) {
+    if (u >= hi) return false;
+    if (sk) {
+      tile = (int)(u / total_k);
+      k0 = (int)(u % total_k);
+      k1 = (int)min((long long)total_k, k0 + (hi - u));
+      piece = k0 == 0 ? 0 : 1;
+      pieces = (k0 == 0 && k1 == total_k) ? 1 : 2;
+      u += k1 - k0;
+    } else {
+      const Unit un = unit_of((int)u, tiles);
+      tile = un.tile;
+      k0 = un.split * k_iters;
+      k1 = k0 + k_iters;
+      piece = un.split;
+      pieces = splits;
+      u += gridDim.x;
+    }
+    return true;
+  }
+};
+
 __device__ __forceinline__ void epi_bar() {  // the 4 epilogue warps only
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
@@ -202,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (grouped) pdl_wait();
   const int k_splits = args.k_splits > 1 ? args.k_splits : 1;
   const int k_iters = args.K / kBK / k_splits;  // per split
+  const int total_k = args.K / kBK;
   int tiles = total_tiles(args);
   if (tiles < 0 || (args.max_units > 0 && tiles * k_splits > args.max_units)) {
     // a corrupt block count: record it and do no work rather than stream
@@ -210,6 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tiles = 0;
   }
   const int units = tiles * k_splits;
+  // stream-K (grouped, no split-K): only when every CTA's range is at least
+  // one tile long, so that a tile has at most two pieces (same on every CTA)
+  const bool stream_k = args.stream_k && grouped && k_splits == 1 && tiles > 0 &&
+                        (long long)tiles * total_k / gridDim.x >= total_k;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -238,10 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait();
       pdl_trigger();
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-        const Unit un = unit_of(u, tiles);
-        const int4 blk = unit_block(args, un.tile / args.f_tiles);
-        const int ft = un.tile % args.f_tiles;
+      SegIter it(stream_k, tiles, total_k, k_splits);
+      int tile_i, k0, k1, piece, pieces;
+      while (!*abort_flag && it.next(tile_i, k0, k1, piece, pieces)) {
+        const int4 blk = unit_block(args, tile_i / args.f_tiles);
+        const int ft = tile_i % args.f_tiles;
         const int n_boxes = (blk.y + kBoxRows - 1) / kBoxRows;
         const int w_row = blk.z * args.w_rows_per_group + ft * kBM;
         const uint32_t bytes = L::kABytes * (SWIGLU ? 2 : 1) + n_boxes * kBoxRows * kBK * 2;
@@ -250,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < n_boxes * kBoxRows; ++j)
             rows_s[j] = args.row_ids[blk.x + min(j, blk.y - 1)];
         }
-        for (int k = un.split * k_iters; k < (un.split + 1) * k_iters; ++k) {
+        for (int k = k0; k < k1; ++k) {
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes * (SWIGLU ? 2 : 1);
           if (pre > 0) {
@@ -292,8 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;  // local tile counter
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
-        const int4 blk = unit_block(args, unit_of(u, tiles).tile / args.f_tiles);
+      SegIter it(stream_k, tiles, total_k, k_splits);
+      int tile_i, k0, k1, piece, pieces;
+      for (; !*abort_flag && it.next(tile_i, k0, k1, piece, pieces); ++t) {
+        const int4 blk = unit_block(args, tile_i / args.f_tiles);
         const int n_mma = max(32, ((blk.y + 31) / 32) * 32);
         const uint32_t idesc = umma_idesc_bf16(kBM, n_mma);
         const int slot = t % L::kSlots;
@@ -303,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_gate = tmem_base + slot * L::kSlotCols;
         bool ok = true;
-        for (int k = 0; k < k_iters; ++k) {
+        for (int k = k0; k < k1; ++k) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, 21)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
@@ -311,10 +365,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
-            umma_bf16(d_gate, umma_desc_sw128(sa + kk * 32), bdesc, idesc, (k | kk) != 0);
+            const uint32_t acc = (k != k0 || kk != 0) ? 1u : 0u;
+            umma_bf16(d_gate, umma_desc_sw128(sa + kk * 32), bdesc, idesc, acc);
             if (SWIGLU)
               umma_bf16(d_gate + L::kAccCols, umma_desc_sw128(sa + L::kABytes + kk * 32), bdesc,
-                        idesc, (k | kk) != 0);
+                        idesc, acc);
           }
           umma_commit(&empty_bar[stage]);  // smem stage free once these MMAs retire
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -335,8 +390,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* sc = scale_s + (warp - 2) * BN;  // this warp's copy of the tile's row scales
     volatile int* last_flag = abort_flag + 1;
     int t = 0;
-    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++t) {
-      const Unit un = unit_of(u, tiles);
+    SegIter it(stream_k, tiles, total_k, k_splits);
+    int tile_i, k0, k1, piece, pieces;
+    for (; !*abort_flag && it.next(tile_i, k0, k1, piece, pieces); ++t) {
+      const Unit un = {tile_i, piece};
       const int4 blk = unit_block(args, un.tile / args.f_tiles);
       const int ft = un.tile % args.f_tiles;
       const int slot = t % L::kSlots;
@@ -354,10 +411,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int f_base = ft * kBM + q * 32;
       bool emit = true;
       float* wsp = nullptr;
-      if (k_splits > 1) {
-        // split-K: store this split's partial tile (SwiGLU: gate and up) into
-        // its own fp32 slice; the last split to finish sums the slices in split
-        // order, so the result does not depend on which split finished first
+      if (pieces > 1) {
+        // split-K / stream-K piece: store this piece's partial tile (SwiGLU:
+        // gate and up) into its own fp32 slice; the last piece to finish sums
+        // the slices in piece order, so the result does not depend on which
+        // piece finished first
         const size_t tile_elems = (size_t)BN * kBM * (SWIGLU ? 2 : 1);
         wsp = args.ws + (size_t)un.tile * tile_elems + q * 32 + lane;
         float* own = wsp + (size_t)un.split * tiles * tile_elems;
@@ -380,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         epi_bar();
         if (threadIdx.x == 64)
-          *last_flag = (atomicAdd(&args.tile_counters[un.tile], 1) == k_splits - 1);
+          *last_flag = (atomicAdd(&args.tile_counters[un.tile], 1) == pieces - 1);
         epi_bar();
         emit = *last_flag != 0;
         if (emit) __threadfence();
@@ -407,13 +465,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           auto reduce = [&](float (&out)[16], const float* src) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) out[j] = 0.f;
-            for (int sp0 = 0; sp0 < k_splits; sp0 += 4) {
+            for (int sp0 = 0; sp0 < pieces; sp0 += 4) {
               float v[4][16];
 #pragma unroll
               for (int u = 0; u < 4; ++u)
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                  v[u][j] = (sp0 + u < k_splits && c + j < blk.y)
+                  v[u][j] = (sp0 + u < pieces && c + j < blk.y)
                                 ? __ldcg(src + (sp0 + u) * split_stride + (c + j) * kBM)
                                 : 0.f;
 #pragma unroll
@@ -590,6 +648,7 @@ int gemm_swapab_launch(const GemmLaunch& p, cudaStream_t stream) {
   if (r) return 3000 + r;
   GemmArgs a = p.args;
   a.block_n = p.block_n;
+  if (a.stream_k && (a.ws == nullptr || a.tile_counters == nullptr)) return 1009;
   if (a.k_splits > 1) {
     if ((p.args.K / kBK) % a.k_splits != 0) return 1007;
     if (a.ws == nullptr || a.tile_counters == nullptr) return 1008;

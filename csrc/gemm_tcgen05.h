@@ -44,6 +44,10 @@ struct GemmArgs {
   int k_splits;
   float* ws;
   int* tile_counters;
+  // stream-K (grouped mode, k_splits 1): every CTA takes an equal contiguous
+  // range of the tiles x K/64 k-iterations; a tile cut by a range boundary
+  // has two pieces, reduced like two splits (ws: 2 slices, tile_counters)
+  int stream_k;
   // gathered B operand: sorted row r of a block reads row row_ids[r] of x
   // (TMA tile::gather4); nullptr: rows are contiguous in x
   const int* row_ids;

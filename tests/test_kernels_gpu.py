@@ -84,6 +84,30 @@ def test_moe_experts(T, E, k):
     assert _rel(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("sk", [True, False])
+@pytest.mark.parametrize("T,E_loc,start,sms", [(128, 32, 32, 0), (128, 32, 96, 128), (16, 128, 0, 0),
+                                               (64, 128, 0, 100), (256, 64, 64, 0), (5, 32, 0, 0)])
+def test_moe_experts_decode_stream_k(T, E_loc, start, sms, sk, monkeypatch):
+    """Decode-sized expert GEMMs with stream-K ranges (boundary tiles reduced in
+    two pieces) and with round-robin tiles, full grid and a capped grid,
+    against the fp32 statement; twice, so the piece counters are seen reset."""
+    monkeypatch.setattr(ops, "_STREAM_K", sk)
+    H, I, E, k = 2048, 768, 128, 8
+    xn = _randn(T, H, seed=32)
+    h = _randn(T, H, seed=33)
+    wgu = _randn(E_loc, 2 * I, H, scale=0.02, seed=34)
+    wd = _randn(E_loc, H, I, scale=0.02, seed=35)
+    probs = torch.randn(T, E, device=DEV).softmax(-1)
+    w, ids = probs.topk(k, -1)
+    w = (w / w.sum(-1, keepdim=True)).float()
+    ids = ids.to(torch.int32)
+    ref = torch_ref.moe_experts(xn, ids, w, wgu, wd, start).float() + h.float()
+    for _ in range(2):
+        with ops.sm_budget(sms):
+            out = ops.moe_experts(xn, ids, w, wgu, wd, start, residual=h)
+        assert _rel(out, ref) < 2e-2
+
+
 @pytest.mark.parametrize("tm", [True, False])
 @pytest.mark.parametrize("T,E_loc,start", [(2048, 128, 0), (1600, 128, 0), (3000, 32, 32),
                                            (4096, 64, 64)])
