@@ -997,15 +997,32 @@ int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s)
 }
 
 // X_sorted[row] = X[row_token[row]] (16-byte vectors). Rows past num_rows idle.
-__global__ void moe_gather_kernel(MoeGatherArgs a) {
+// A warp per gathered row, 8 rows per CTA; each lane has up to 8 16-byte
+// loads in flight before its stores.
+constexpr int kGatherRowsPerCta = 8;
+__global__ void __launch_bounds__(32 * kGatherRowsPerCta) moe_gather_kernel(MoeGatherArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x;
+  const int row = blockIdx.x * kGatherRowsPerCta + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
   if (row >= *a.num_rows) return;
   const int t = a.row_token[row];
-  const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * a.ld_x);
-  uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)row * a.H);
-  for (int i = threadIdx.x; i < a.H / 8; i += blockDim.x) dst[i] = src[i];
+  const uint4* __restrict__ src = reinterpret_cast<const uint4*>(a.x + (size_t)t * a.ld_x);
+  uint4* __restrict__ dst = reinterpret_cast<uint4*>(a.out + (size_t)row * a.H);
+  const int n = a.H / 8;
+  for (int i0 = 0; i0 < n; i0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < n) v[u] = src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 32 + lane;
+      if (i < n) dst[i] = v[u];
+    }
+  }
 }
 
 // out[t] = (residual ? h[t] : 0) + sum_j y[inv[t, j]]   (bf16 out, fp32 math)
@@ -1023,12 +1040,16 @@ __global__ void __launch_bounds__(kNormThreads) moe_combine_kernel(MoeCombineArg
     if (t >= a.seg_offsets[s] && t < a.seg_offsets[s + 1]) seg = s;
   for (int col = threadIdx.x * 8; col < H; col += kNormThreads * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    // every row's vector is requested before the sums (loads in flight)
+    // every row's vector and the residual are requested before the sums
+    // (loads in flight together)
     uint4 v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       v[j] = rows[j] >= 0 ? *reinterpret_cast<const uint4*>(a.y + (size_t)rows[j] * H + col)
                           : make_uint4(0, 0, 0, 0);
+    uint4 res = make_uint4(0, 0, 0, 0);
+    if (a.residual != nullptr)
+      res = *reinterpret_cast<const uint4*>(a.residual + (size_t)t * a.ld_res + col);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (rows[j] < 0) continue;
@@ -1042,10 +1063,14 @@ __global__ void __launch_bounds__(kNormThreads) moe_combine_kernel(MoeCombineArg
       }
     }
     if (a.residual != nullptr) {
-      float r[8];
-      load8(a.residual + (size_t)t * a.ld_res + col, r);
+      const uint32_t* pr = &res.x;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = round_bf16(acc[i]) + r[i];
+      for (int e = 0; e < 4; ++e) {
+        float r0, r1;
+        unpack_bf16x2(pr[e], r0, r1);
+        acc[2 * e] = round_bf16(acc[2 * e]) + r0;
+        acc[2 * e + 1] = round_bf16(acc[2 * e + 1]) + r1;
+      }
     }
     uint4 u;
     u.x = pack_bf16x2(acc[0], acc[1]);
@@ -1428,7 +1453,9 @@ int launch_moe_align(const MoeAlignArgs& a, cudaStream_t s) {
 int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s) {
   if (a.H % 8 != 0) return 1;
   if (max_rows == 0) return 0;
-  return (int)launch_k(moe_gather_kernel, dim3(max_rows), dim3(256), 0, s, a);
+  return (int)launch_k(moe_gather_kernel,
+                       dim3((max_rows + kGatherRowsPerCta - 1) / kGatherRowsPerCta),
+                       dim3(32 * kGatherRowsPerCta), 0, s, a);
 }
 
 int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s) {
