@@ -203,3 +203,12 @@ def test_comm_bench_host_section_reference_schema(tmp_path):
                              "receiver_wait_mean_ms", "blocking_send_mean_ms",
                              "blocking_recv_mean_ms", "completion_bandwidth_mib_s"]
     assert int(rows[1]["tensor_bytes"]) == 2**20
+
+
+def test_decode_cells_cli():
+    """The one-load matrix script parses its options (it needs GPUs to run)."""
+    p = subprocess.run([sys.executable, "-m", "afd_demo_b200.scripts.decode_cells", "--help"],
+                       capture_output=True, text=True, cwd=ROOT, timeout=120)
+    assert p.returncode == 0, p.stderr
+    for opt in ("--batches", "--seqs", "--modes", "--attn-gpus", "--output"):
+        assert opt in p.stdout
