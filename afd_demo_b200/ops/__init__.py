@@ -690,8 +690,11 @@ _SPLIT_F2A = os.environ.get("AFD_SPLIT_F2A", "1") != "0"  # prefill F2A: combine
 # partial store and reduction cost more than the fuller last wave gains), so opt-in
 _GU_SPLIT = os.environ.get("AFD_GU_SPLIT", "0") == "1"
 _FUSED_COMBINE = os.environ.get("AFD_FUSED_COMBINE", "0") == "1"  # measured slower (esp. with peers)
-# AFD_STREAM_K=0: round-robin tiles for the decode expert GEMMs (A/B measurements)
-_STREAM_K = os.environ.get("AFD_STREAM_K", "1") != "0"
+# AFD_STREAM_K=1: stream-K ranges for the decode expert GEMMs instead of
+# round-robin tiles. Measured no faster (32-128 local experts, 16-256 tokens:
+# the fixed per-call costs, not the last wave, keep the expert-parallel slices
+# at 0.6-0.8 of the HBM bandwidth) and 2-5 us slower per call, so opt-in
+_STREAM_K = os.environ.get("AFD_STREAM_K", "0") == "1"
 
 
 def _gate_fusable(T: int, H: int, E: int, top_k: int) -> bool:
