@@ -209,6 +209,29 @@ def _wave_splits(units: int, k_iters: int, gain: float = 1.1) -> int:
 _MAX_SPLITS = int(os.environ.get("AFD_MAX_SPLITS", "16"))
 
 
+def _dense_token_major(T: int, N: int, has_residual: bool) -> bool:
+    """Whether a dense GEMM runs on the token-major kernel (128 token rows x
+    256 features per tile): prefill sizes (more than 256 rows) with a multiple
+    of 256 output features, and by default only with a residual add. Its
+    row-segment epilogue reads the residual row by row (o_proj: 0.72 of the bf16
+    peak at 8192 tokens against 0.58 on the swap-AB kernel, whose transposing
+    epilogue the residual slows); qkv, without a residual, is faster on the
+    swap-AB kernel's 256-token tiles."""
+    if T <= 256 or N % 256 != 0:
+        return False
+    return _DENSE_TM == "all" or (_DENSE_TM == "residual" and has_residual)
+
+
+def _moe_token_major(block_n: int, gathered: bool, T: int, top_k: int, n_experts: int) -> bool:
+    """Whether the grouped expert GEMMs run on the token-major kernel: 128-row
+    blocks of rows already gathered into expert order, and at least
+    _MOE_TM_MIN_ROWS routed rows per expert on average (fuller blocks: the
+    kernel's M is fixed at 128 rows, where the swap-AB kernel's N follows each
+    block's row count)."""
+    return (_MOE_TM and block_n == 128 and gathered
+            and T * top_k >= _MOE_TM_MIN_ROWS * n_experts)
+
+
 def _decode_tiling(T: int, N: int, K: int) -> Tuple[int, int]:
     """(token block, split-K factor) of a decode-sized dense GEMM (T <= 256),
     from a sweep of every combination on B200 for the qkv and o_proj shapes:
@@ -280,13 +303,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
     tm = False
     if T <= 256:
         bn, splits = _decode_tiling(T, N, K)
-    elif N % 256 == 0 and (_DENSE_TM == "all" or (_DENSE_TM == "residual" and
-                                                   residual is not None)):
-        # token-major kernel: 128 token rows x 256 features per tile; its
-        # row-segment epilogue reads the residual row by row (o_proj: 0.72 of
-        # the bf16 peak at 8192 tokens against 0.58 on the swap-AB kernel,
-        # whose transposing epilogue the residual slows; qkv, without a
-        # residual, is faster on the swap-AB kernel's 256-token tiles)
+    elif _dense_token_major(T, N, residual is not None):
         bn, splits, tm = 128, 1, True
     else:
         bn, splits = _block_n(T), 1
@@ -573,8 +590,7 @@ def _moe_gemms_combine(xn, ws: MoEWorkspace, w_gate_up, w_down, residual, out, T
         gws, gcnt = _SplitKWorkspace.get(xn.device, 2 * max_tiles, bn, max(gu_splits, 2))
     # prefill-sized: full 128-row blocks on the token-major kernel (128 x 256 MMAs,
     # row-segment epilogue); decode-sized: the swap-AB kernel
-    tm = (_MOE_TM and bn == 128 and row_ids is None
-          and T * k >= _MOE_TM_MIN_ROWS * (n_experts or E_loc))
+    tm = _moe_token_major(bn, row_ids is None, T, k, n_experts or E_loc)
     C.gemm(w_gate_up.view(E_loc * I2, H), x, ws.act, I // 128, I2, I, ws.blocks, ws.num_blocks,
            0, None, None, True, bn, max_tiles * gu_splits, [], 0, [], 0, None, None, None,
            gu_splits, gws, gcnt, row_ids, tm, sk)
