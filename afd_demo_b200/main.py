@@ -75,6 +75,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--batch-size", type=int, default=2)
     p.add_argument("--max-seq-len", type=int, default=128)
     p.add_argument("--prefill-seq-len", type=int, default=None)
+    p.add_argument("--prefill-chunk-size", type=int, default=None,
+                   help="prefill in sequence chunks of this many tokens (one forward per "
+                        "chunk over the same KV cache)")
     p.add_argument("--dtype", choices=["float16", "bfloat16", "float32"], default="bfloat16")
     p.add_argument("--prompt", type=str, default="Hello, how are you today?")
     p.add_argument("--timing", action="store_true")
@@ -416,7 +419,8 @@ def run_generation_demo(args) -> None:
                          use_decode_dbo=use_dbo, num_decode_micro_batches=args.num_micro_batches,
                          enable_timing=args.timing, timing_mode=args.timing_mode,
                          comm_timing_mode=args.comm_timing_mode,
-                         decode_use_crosslayer=args.crosslayer, use_cuda_graph=args.cuda_graph)
+                         decode_use_crosslayer=args.crosslayer, use_cuda_graph=args.cuda_graph,
+                         prefill_chunk_size=args.prefill_chunk_size)
     devmod.synchronize()
     gen_time = time.perf_counter() - t0
     met = dict(model._last_generation_metrics)

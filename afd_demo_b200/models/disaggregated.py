@@ -229,6 +229,33 @@ class DisaggregatedQwenModel:
             if aw is not None:
                 aw.key_range = None
 
+    def run_prefill_chunked(self, input_ids: torch.Tensor, chunk: int, mode: str = "serial",
+                            num_micro_batches: int = 1, crosslayer: bool = False,
+                            last_only: bool = True) -> Optional[torch.Tensor]:
+        """Prefill in sequence chunks of `chunk` tokens, one forward per chunk
+        over the same preallocated KV cache: chunk c's queries sit at positions
+        c*chunk .. and attend to every key of the chunks before it (the prefill
+        kernels take a cached prefix). The activations of one forward then
+        scale with the chunk, not the prompt. Each chunk runs the schedule
+        `mode` over the batch's micro-batches. Returns the last position's
+        logits ([B_local, V], `last_only`) or every position's
+        ([B_local * S, V], chunks concatenated per sequence) on attention ranks.
+        Padding masks are not supported here (they apply to one-shot prefill)."""
+        B, S = input_ids.shape
+        if chunk <= 0:
+            raise ValueError("chunk must be positive")
+        outs = []
+        for c0 in range(0, S, chunk):
+            out = self.run_forward(input_ids[:, c0:c0 + chunk], mode, num_micro_batches,
+                                   crosslayer, last_only=last_only, reset_cache=(c0 == 0))
+            outs.append(out)
+        if outs[-1] is None or last_only:
+            return outs[-1]
+        # per chunk [B_local * len, V] -> [B_local, S, V] -> [B_local * S, V]
+        Bl = len(self.local_batch(B))
+        parts = [o.view(Bl, -1, o.shape[-1]) for o in outs]
+        return torch.cat(parts, 1).reshape(Bl * S, -1)
+
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
                 ) -> Optional[torch.Tensor]:
@@ -244,17 +271,25 @@ class DisaggregatedQwenModel:
     @torch.no_grad()
     def forward_prefill(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                         mode: str = "serial", num_micro_batches: int = 1,
-                        crosslayer: bool = False, last_only: bool = False
-                        ) -> Optional[torch.Tensor]:
+                        crosslayer: bool = False, last_only: bool = False,
+                        chunk_size: Optional[int] = None) -> Optional[torch.Tensor]:
         """Prefill (resets and fills the KV cache). Logits [B_local, S, V] on
         attention ranks, as the reference's forward_prefill returns them
         (src/model/disaggregated.py:377-443); `last_only` projects only the
         last position ([B_local, V]), which is all sampling needs. The
         reference's generate always prefills serially and unsplit;
-        `mode="dbo"` runs the micro-batched overlap instead."""
+        `mode="dbo"` runs the micro-batched overlap instead. `chunk_size`
+        prefills the prompt in sequence chunks (``run_prefill_chunked``)."""
         S = input_ids.shape[1]
-        out = self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True,
-                               attention_mask=attention_mask, last_only=last_only)
+        if chunk_size and chunk_size < S:
+            if attention_mask is not None:
+                raise ValueError("chunked prefill takes no padding mask")
+            out = self.run_prefill_chunked(input_ids, chunk_size, mode, num_micro_batches,
+                                           crosslayer, last_only=last_only)
+        else:
+            out = self.run_forward(input_ids, mode, num_micro_batches, crosslayer,
+                                   reset_cache=True, attention_mask=attention_mask,
+                                   last_only=last_only)
         if out is None or last_only:
             return out
         return out.view(-1, S, out.shape[-1])
@@ -372,7 +407,8 @@ class DisaggregatedQwenModel:
                  comm_timing_mode: str = "enqueue", decode_use_crosslayer: bool = False,
                  prefill_mode: str = "serial", num_prefill_micro_batches: int = 1,
                  use_cuda_graph: bool = False, host_io: bool = False,
-                 generator: Optional[torch.Generator] = None) -> torch.Tensor:
+                 generator: Optional[torch.Generator] = None,
+                 prefill_chunk_size: Optional[int] = None) -> torch.Tensor:
         """Prefill, then `max_new_tokens - 1` decode steps (the first token
         comes from the prefill logits), like the reference's generate
         (src/model/disaggregated.py:537-701). EOS does not stop the loop so
@@ -381,7 +417,9 @@ class DisaggregatedQwenModel:
         Returns this attention rank's sequences [B_local, S + max_new_tokens]
         (FFN-only ranks return the input). Metrics land in
         ``_last_generation_metrics``: prefill_ms, decode_loop_ms, decode_steps,
-        decode_tpot_ms (device time between events on the main stream)."""
+        decode_tpot_ms (device time between events on the main stream).
+        `prefill_chunk_size` prefills in sequence chunks of that many tokens
+        (``run_prefill_chunked``); prefill_ms then covers every chunk."""
         from ..parallel.schedulers import DecodeDBOScheduler
 
         B, S = input_ids.shape
@@ -399,8 +437,13 @@ class DisaggregatedQwenModel:
         t_pf0 = ev()
         # prefill DBO pipelines micro-batches across layers, as the reference's
         # AsyncPipelineScheduler does (src/pipeline/async_scheduler.py:281-456)
-        logits = self.run_forward(input_ids, prefill_mode, num_prefill_micro_batches,
-                                  crosslayer=(prefill_mode == "dbo"), reset_cache=True)
+        if prefill_chunk_size and prefill_chunk_size < S:
+            logits = self.run_prefill_chunked(input_ids, prefill_chunk_size, prefill_mode,
+                                              num_prefill_micro_batches,
+                                              crosslayer=(prefill_mode == "dbo"))
+        else:
+            logits = self.run_forward(input_ids, prefill_mode, num_prefill_micro_batches,
+                                      crosslayer=(prefill_mode == "dbo"), reset_cache=True)
         t_pf1 = ev()
         generated = [local] if is_attn else []
         next_tok = None
