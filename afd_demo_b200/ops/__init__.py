@@ -856,12 +856,34 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
 
 
 # ------------------------------------------------------------- sampling --
-class _ArgmaxWorkspace(_GateCounters):
-    """Workspace of the split argmax: per-row counters (left zeroed by the
-    kernel) and per-chunk partials, one buffer per (device, stream)."""
+class _ArgmaxCounters(_GateCounters):
+    """Per-row counters of the split argmax (zeroed; the kernel leaves them
+    zeroed), one buffer per (device, stream). They are kept apart from the
+    partials, whose layout depends on the row count: in a shared buffer a
+    call with fewer rows would leave its partials where a later call with
+    more rows expects zeroed counters."""
 
     _pool: dict = {}
     _retired: list = []
+
+
+class _ArgmaxPartials:
+    """Per-chunk partial maxima of the split argmax (no initial value needed),
+    one buffer per (device, stream); outgrown buffers stay alive for graphs."""
+
+    _pool: dict = {}
+    _retired: list = []
+
+    @classmethod
+    def get(cls, device, n: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        b = cls._pool.get(key)
+        if b is None or b.numel() < n:
+            if b is not None:
+                cls._retired.append(b)
+            b = torch.empty(n, device=device, dtype=torch.int32)
+            cls._pool[key] = b
+        return b
 
 
 def argmax(logits: torch.Tensor) -> torch.Tensor:
@@ -870,10 +892,12 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     CTAs with a last-CTA reduction."""
     if not _cuda(logits) or logits.dtype != torch.bfloat16:
         return torch_ref.argmax(logits)
-    out = torch.empty(logits.shape[0], device=logits.device, dtype=torch.int64)
-    n = ext().argmax_workspace_ints(logits.shape[0], logits.shape[1])
-    ws = _ArgmaxWorkspace.get(logits.device, n - 1)
-    ext().argmax(logits, out, ws)
+    rows = logits.shape[0]
+    out = torch.empty(rows, device=logits.device, dtype=torch.int64)
+    counters = _ArgmaxCounters.get(logits.device, rows)
+    partials = _ArgmaxPartials.get(logits.device,
+                                   ext().argmax_partial_ints(rows, logits.shape[1]))
+    ext().argmax(logits, out, counters, partials)
     return out
 
 

@@ -626,24 +626,31 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv, int64_t T, int64_t 
   check_rc(afd::launch_moe_combine(a, (int)T, cur_stream()), "moe_combine");
 }
 
-void argmax(const at::Tensor& logits, at::Tensor& out, const c10::optional<at::Tensor>& ws) {
+void argmax(const at::Tensor& logits, at::Tensor& out, const c10::optional<at::Tensor>& counters,
+            const c10::optional<at::Tensor>& partials) {
   CHECK_BF16(logits);
   TORCH_CHECK(logits.stride(1) == 1, "argmax: rows must be contiguous");
+  const int rows = (int)logits.size(0);
+  int* c = nullptr;
   int* w = nullptr;
-  if (ws.has_value()) {
-    TORCH_CHECK(ws->scalar_type() == at::kInt && ws->is_cuda() && ws->is_contiguous() &&
-                    ws->numel() >= afd::argmax_workspace_ints((int)logits.size(0),
-                                                              (int)logits.size(1)),
-                "argmax workspace: contiguous int32 CUDA tensor of argmax_workspace_ints ints");
-    w = ws->data_ptr<int>();
+  if (counters.has_value() && partials.has_value()) {
+    TORCH_CHECK(counters->scalar_type() == at::kInt && counters->is_cuda() &&
+                    counters->is_contiguous() && counters->numel() >= rows,
+                "argmax counters: contiguous zeroed int32 CUDA tensor, one per row");
+    TORCH_CHECK(partials->scalar_type() == at::kInt && partials->is_cuda() &&
+                    partials->is_contiguous() &&
+                    partials->numel() >= afd::argmax_partial_ints(rows, (int)logits.size(1)),
+                "argmax partials: contiguous int32 CUDA tensor of argmax_partial_ints ints");
+    c = counters->data_ptr<int>();
+    w = partials->data_ptr<int>();
   }
-  check_rc(afd::launch_argmax(cbf(logits), (int)logits.size(0), (int)logits.size(1),
-                              (int)logits.stride(0), out.data_ptr<int64_t>(), w, cur_stream()),
+  check_rc(afd::launch_argmax(cbf(logits), rows, (int)logits.size(1), (int)logits.stride(0),
+                              out.data_ptr<int64_t>(), c, w, cur_stream()),
            "argmax");
 }
 
-int64_t argmax_workspace_ints(int64_t rows, int64_t V) {
-  return afd::argmax_workspace_ints((int)rows, (int)V);
+int64_t argmax_partial_ints(int64_t rows, int64_t V) {
+  return afd::argmax_partial_ints((int)rows, (int)V);
 }
 
 afd::FlagArgs flag_args(const std::vector<int64_t>& flags, int64_t value,
@@ -744,7 +751,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention_tc", &decode_attention_tc);
   m.def("decode_tc_supported", &decode_tc_supported);
   m.def("prefill_attention", &prefill_attention);
-  m.def("argmax_workspace_ints", &argmax_workspace_ints);
+  m.def("argmax_partial_ints", &argmax_partial_ints);
   m.def("decode_attention_fused", &decode_attention_fused);
   m.def("router_topk", &router_topk);
   m.def("moe_align", &moe_align);

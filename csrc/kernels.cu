@@ -1132,7 +1132,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logit
       const int oi = __shfl_xor_sync(0xffffffff, bi, o);
       if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
     }
-    if (l == 0) out[row] = bi;
+    // a row with no comparable value (all NaN) yields 0: always a valid token id
+    if (l == 0) out[row] = bi < V ? bi : 0;
   }
 }
 
@@ -1158,7 +1159,7 @@ __device__ __forceinline__ void argmax_warp(float& best, int& bi) {
 }
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_split_kernel(
-    const __nv_bfloat16* logits, int V, int ld, int64_t* out, int* ws) {
+    const __nv_bfloat16* logits, int V, int ld, int64_t* out, int* counters, int* partials) {
   __shared__ float sv[kArgmaxThreads / 32];
   __shared__ int si[kArgmaxThreads / 32];
   __shared__ int s_last;
@@ -1187,9 +1188,9 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_split_kernel(
   const int wp = threadIdx.x / 32, l = threadIdx.x % 32;
   if (l == 0) { sv[wp] = best; si[wp] = bi; }
   __syncthreads();
-  int* cnt = ws;
-  float* pv = reinterpret_cast<float*>(ws + rows);
-  int* pi = ws + rows + rows * n;
+  int* cnt = counters;
+  float* pv = reinterpret_cast<float*>(partials);
+  int* pi = partials + rows * n;
   if (threadIdx.x == 0) {
     for (int k = 1; k < kArgmaxThreads / 32; ++k) argmax_take(sv[k], si[k], best, bi);
     pv[row * n + chunk] = best;
@@ -1205,7 +1206,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_split_kernel(
   for (int c = l; c < n; c += 32) argmax_take(__ldcg(pv + row * n + c), __ldcg(pi + row * n + c), best, bi);
   argmax_warp(best, bi);
   if (l == 0) {
-    out[row] = bi;
+    out[row] = bi < V ? bi : 0;  // all NaN: 0, still a valid token id
     cnt[row] = 0;
   }
 }
@@ -1464,20 +1465,21 @@ int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s) {
   return (int)launch_k(moe_combine_kernel, dim3(T), dim3(kNormThreads), 0, s, a);
 }
 
-int argmax_workspace_ints(int rows, int V) {
-  return rows + 2 * rows * ((V + kArgmaxChunk - 1) / kArgmaxChunk);
+int argmax_partial_ints(int rows, int V) {
+  return 2 * rows * ((V + kArgmaxChunk - 1) / kArgmaxChunk);
 }
 
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
-                  int* ws, cudaStream_t s) {
+                  int* counters, int* partials, cudaStream_t s) {
   if (rows == 0) return 0;
-  const bool split = ws != nullptr && V > kArgmaxChunk && ld % 8 == 0 &&
-                     reinterpret_cast<uintptr_t>(logits) % 16 == 0 && rows <= 65535;
+  const bool split = counters != nullptr && partials != nullptr && V > kArgmaxChunk &&
+                     ld % 8 == 0 && reinterpret_cast<uintptr_t>(logits) % 16 == 0 &&
+                     rows <= 65535;
   if (!split)
     return (int)launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, s, logits, V, ld, out);
   const dim3 grid((V + kArgmaxChunk - 1) / kArgmaxChunk, rows);
   return (int)launch_k(argmax_split_kernel, grid, dim3(kArgmaxThreads), 0, s, logits, V, ld, out,
-                       ws);
+                       counters, partials);
 }
 
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s) {

@@ -200,12 +200,15 @@ int launch_moe_gather(const MoeGatherArgs& a, int max_rows, cudaStream_t s);
 // RMSNorm + router + top-k + routing in one launch (T * top_k <= 2048, H <= 4096)
 int launch_moe_gate(const MoeGateArgs& g, const MoeAlignArgs& a, cudaStream_t s);
 int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s);
-// Split argmax (several CTAs per row) when `ws` (argmax_workspace_ints ints,
-// counters zeroed; the kernel leaves them zeroed) is given and the rows are
-// 16-byte aligned; one CTA per row otherwise.
-int argmax_workspace_ints(int rows, int V);
+// Split argmax (several CTAs per row) when `counters` (one per row, zeroed;
+// the kernel leaves them zeroed) and `partials` (argmax_partial_ints ints, no
+// initial value) are given and the rows are 16-byte aligned; one CTA per row
+// otherwise. The two live in separate buffers: the partials' layout depends on
+// the row count, so a shared buffer would leave a smaller call's partials
+// where a larger later call expects zeroed counters.
+int argmax_partial_ints(int rows, int V);
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
-                  int* ws, cudaStream_t s);
+                  int* counters, int* partials, cudaStream_t s);
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s);
 int launch_wait_flags(const FlagArgs& a, cudaStream_t s);
 int launch_add_i32(int* p, int by, cudaStream_t s);

@@ -390,6 +390,29 @@ def test_argmax():
     assert torch.equal(ops.argmax(x), x.float().argmax(-1))  # workspace counters reset
 
 
+def test_argmax_row_counts_change_between_calls():
+    """32 rows, then 8, then 32 again on one stream: the per-row counters of the
+    split kernel must not inherit the 8-row call's partial maxima (they once
+    shared a buffer, and the third call returned unwritten indices)."""
+    for rows in (32, 8, 32, 5, 32):
+        x = _randn(rows, 151936, seed=76 + rows)
+        assert torch.equal(ops.argmax(x), x.float().argmax(-1)), rows
+
+
+@pytest.mark.parametrize("V", [100, 151936])
+def test_argmax_all_nan_row_gives_a_valid_index(V):
+    """A row with no comparable value (all NaN) returns 0, both kernels: the
+    index always stays a valid token id for the next embedding lookup."""
+    x = _randn(3, V, seed=74)
+    x[1] = float("nan")
+    got = ops.argmax(x)
+    assert int(got[1]) == 0
+    assert int(got[0]) == int(x[0].float().argmax()) and int(got[2]) == int(x[2].float().argmax())
+    view = _randn(3, V + 3, seed=75)[:, 1:V + 1]  # unaligned rows: the one-CTA kernel
+    view[0] = float("nan")
+    assert int(ops.argmax(view)[0]) == 0
+
+
 @pytest.mark.parametrize("V", [100, 8192, 8200, 151936, 151937])
 def test_argmax_ties_and_strided_rows(V):
     """Ties across chunks go to the first index; a ragged tail, a NaN (never
