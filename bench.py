@@ -70,48 +70,86 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+    """nvidia-smi sampling of SM clocks and throttle reasons (every 50 ms).
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Started before the warm-up steps, so that nvidia-smi is already sampling
+    when the timed region opens; `mark_start` / `mark_end` bracket the timed
+    region on the host clock, and only samples stamped inside it are
+    summarised. A region shorter than the sampling interval keeps the
+    nearest sample on each side (`samples_in_region` says how many fell
+    inside)."""
+
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.p = None
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    @staticmethod
+    def _stamp(text: str):
+        # nvidia-smi timestamp: "YYYY/MM/DD HH:MM:SS.mmm" in local time
+        import datetime
+        try:
+            return datetime.datetime.strptime(text.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
+    @classmethod
+    def summarise(cls, rows, t0=None, t1=None) -> dict:
+        """rows: split CSV rows of Q. Samples inside [t0, t1] when given (else
+        all); with none inside, the nearest one before and after."""
+        parsed = []
+        for r in rows:
+            try:
+                parsed.append((cls._stamp(r[0]), float(r[2]), float(r[3]),
+                               [v.strip().lower() == "active" for v in r[6:10]]))
+            except (ValueError, IndexError):
+                continue
+        inside = parsed
+        n_in = len(parsed)
+        if t0 is not None and t1 is not None and all(p[0] is not None for p in parsed):
+            inside = [p for p in parsed if t0 <= p[0] <= t1]
+            n_in = len(inside)
+            if not inside:
+                before = [p for p in parsed if p[0] < t0]
+                after = [p for p in parsed if p[0] > t1]
+                inside = before[-1:] + after[:1]
+        sm = [p[1] for p in inside]
+        reasons = sorted({n for p in inside for n, a in zip(cls.NAMES, p[3]) if a})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": inside[-1][2] if inside else None,
+                "reasons": reasons, "samples": len(sm), "samples_in_region": n_in}
+
     def stop(self) -> dict:
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.12)
         self.p.terminate()
         self.p.wait()
         self.f.flush()
         self.f.seek(0)
         rows = [r.strip().split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
         os.unlink(self.f.name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return self.summarise(rows, self.t0, self.t1)
 
 
 def reference_arm(args, rank):
@@ -310,15 +348,19 @@ def main():
         torch.cuda.synchronize()
         ctx.barrier()
 
-    def timed(fn, n):
+    def timed(fn, n, clocks=None):
         bar()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
+        if clocks is not None:
+            clocks.mark_start()
         s.record()
         for _ in range(n):
             fn()
         e.record()
         torch.cuda.synchronize()
+        if clocks is not None:
+            clocks.mark_end()
         ctx.barrier()
         ms = s.elapsed_time(e)
         if world > 1:
@@ -349,12 +391,14 @@ def main():
                 tok[r.start:r.stop, 0] = ops.argmax(holder.get("logits", logits))
             holder["logits"] = model.decode_step(tok, mode, nmb, crosslayer, True)
 
+        # the sampler starts before the warm-up, so it is sampling when the
+        # timed region opens; only its samples inside the region are kept
+        clocks = ClockSampler(local)
+        clocks.start()
         for _ in range(warm):
             step()
         ops.LAUNCHES.reset()
-        clocks = ClockSampler(local)
-        clocks.start()
-        ms = timed(step, steps)
+        ms = timed(step, steps, clocks)
         clk = clocks.stop()
         # kernels of this package in the timed region: graph contents per
         # replay plus the argmax launched outside the graph each step

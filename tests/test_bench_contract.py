@@ -54,3 +54,29 @@ def test_bench_json_contract_small_model():
     assert e2e["value"] > 0 and e2e["h2d_bytes_per_step"] == 8 * 8
     assert e2e["d2h_bytes_per_step"] == 8 * 8
     assert "sm_mhz" in d["clocks"] and "reasons" in d["clocks"]
+
+
+def test_clock_sampler_keeps_samples_of_the_timed_region():
+    """Only nvidia-smi rows stamped inside the timed region are summarised;
+    a region shorter than the interval keeps the nearest row on each side."""
+    import datetime
+
+    sys.path.insert(0, REPO)
+    from bench import ClockSampler
+
+    base = datetime.datetime(2026, 1, 1, 12, 0, 0)
+
+    def row(ms, sm, reasons=("Not Active",) * 4):
+        t = (base + datetime.timedelta(milliseconds=ms)).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        return [t, "0", str(sm), "1965", "700.0", "0x0"] + list(reasons)
+
+    rows = [row(0, 600), row(50, 1900), row(100, 1950),
+            row(150, 1960, ("Not Active", "Not Active", "Not Active", "Active")), row(200, 700)]
+    t = lambda ms: (base + datetime.timedelta(milliseconds=ms)).timestamp()  # noqa: E731
+    d = ClockSampler.summarise(rows, t(40), t(160))
+    assert d["samples_in_region"] == 3 and d["sm_mhz"] == 1950.0
+    assert d["reasons"] == ["sw_power_cap"] and d["sm_max_mhz"] == 1965.0
+    near = ClockSampler.summarise(rows, t(60), t(90))  # no row inside
+    assert near["samples_in_region"] == 0 and near["samples"] == 2
+    assert near["sm_mhz"] == (1900.0 + 1950.0) / 2
+    assert ClockSampler.summarise(rows)["samples"] == 5
