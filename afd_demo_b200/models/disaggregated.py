@@ -256,12 +256,25 @@ class DisaggregatedQwenModel:
         parts = [o.view(Bl, -1, o.shape[-1]) for o in outs]
         return torch.cat(parts, 1).reshape(Bl * S, -1)
 
+    def check_token_ids(self, input_ids: torch.Tensor) -> None:
+        """Raises ValueError unless every id is in [0, vocab_size). The public
+        entry points (generate, forward, forward_prefill) check their prompt
+        once, so that a bad id fails on the host instead of in the GPU's
+        embedding lookup (a device-side assert that poisons the context)."""
+        if input_ids.numel() == 0:
+            return
+        lo, hi = int(input_ids.min()), int(input_ids.max())
+        V = self.config.vocab_size
+        if lo < 0 or hi >= V:
+            raise ValueError(f"token ids must lie in [0, {V}); got [{lo}, {hi}]")
+
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
                 ) -> Optional[torch.Tensor]:
         """Full-sequence serial forward (validation path); logits for every
         position [B_local, S, V] on attention ranks."""
         B, S = input_ids.shape
+        self.check_token_ids(input_ids)
         out = self.run_forward(input_ids, "serial", 1, last_only=False, reset_cache=True,
                                attention_mask=attention_mask)
         if out is None:
@@ -281,6 +294,7 @@ class DisaggregatedQwenModel:
         `mode="dbo"` runs the micro-batched overlap instead. `chunk_size`
         prefills the prompt in sequence chunks (``run_prefill_chunked``)."""
         S = input_ids.shape[1]
+        self.check_token_ids(input_ids)
         if chunk_size and chunk_size < S:
             if attention_mask is not None:
                 raise ValueError("chunked prefill takes no padding mask")
@@ -423,6 +437,7 @@ class DisaggregatedQwenModel:
         from ..parallel.schedulers import DecodeDBOScheduler
 
         B, S = input_ids.shape
+        self.check_token_ids(input_ids)
         ctx = self.ctx
         is_attn = ctx.is_attention_node
         cuda = self.device.type == "cuda"

@@ -60,3 +60,17 @@ def test_cli_flag():
 
     assert parse_args(["--prefill-chunk-size", "64"]).prefill_chunk_size == 64
     assert parse_args([]).prefill_chunk_size is None
+
+
+def test_out_of_range_ids_fail_on_the_host(model):
+    bad = _ids(8).clone()
+    bad[1, 3] = 1024  # vocab of the tiny model is 1024
+    for call in (lambda: model.generate(bad, max_new_tokens=2, do_sample=False),
+                 lambda: model.forward_prefill(bad),
+                 lambda: model.forward(bad)):
+        with pytest.raises(ValueError, match="token ids"):
+            call()
+    neg = _ids(8).clone()
+    neg[0, 0] = -1
+    with pytest.raises(ValueError, match="token ids"):
+        model.forward_prefill(neg)
