@@ -13,7 +13,9 @@
 // Work units are (row block, feature tile). Row blocks come from a device
 // list written by the MoE routing kernel (grouped mode: one or more blocks
 // per expert, <= BN rows each) or are derived from a host row count (dense
-// mode: a single group). Units are dealt round-robin to a persistent grid.
+// mode: a single group). Units are dealt round-robin to a persistent grid,
+// or, in stream-K mode (opt-in, grouped GEMMs), each CTA takes an equal
+// contiguous range of the units' k-iterations (see SegIter).
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator
 // + MMA issuer, warps 2..5 = epilogue (TMEM -> registers -> global). Smem
