@@ -21,6 +21,7 @@ its data-parallel slice; FFN ranks only need the shape.
 
 from __future__ import annotations
 
+import gc
 import logging
 import time
 from typing import Any, Dict, Optional
@@ -403,7 +404,14 @@ class DisaggregatedQwenModel:
     # --------------------------------------------------------- generation
     def generate(self, *args, **kwargs) -> torch.Tensor:
         """See ``_generate``. A failure on this rank is published to the
-        others (when failure detection is on) before it propagates."""
+        others (when failure detection is on) before it propagates.
+
+        Python's cyclic garbage collector is paused for the call (and
+        restored after): the prefill is enqueued from Python, and a full
+        collection over the process's objects in the middle of it leaves the
+        GPU idle for tens of milliseconds."""
+        gc_on = gc.isenabled()
+        gc.disable()
         try:
             return self._generate(*args, **kwargs)
         except AFDPeerFailure:
@@ -411,6 +419,9 @@ class DisaggregatedQwenModel:
         except BaseException as e:
             self.ctx.report_failure(f"{type(e).__name__}: {e}")
             raise
+        finally:
+            if gc_on:
+                gc.enable()
 
     @torch.no_grad()
     def _generate(self, input_ids: torch.Tensor, max_new_tokens: int = 50, temperature: float = 1.0,

@@ -74,3 +74,18 @@ def test_out_of_range_ids_fail_on_the_host(model):
     neg[0, 0] = -1
     with pytest.raises(ValueError, match="token ids"):
         model.forward_prefill(neg)
+
+
+def test_generate_restores_the_garbage_collector(model):
+    import gc
+
+    ids = _ids(12)
+    assert gc.isenabled()
+    model.generate(ids, max_new_tokens=2, do_sample=False)
+    assert gc.isenabled()
+    gc.disable()
+    try:
+        model.generate(ids, max_new_tokens=2, do_sample=False)
+        assert not gc.isenabled()
+    finally:
+        gc.enable()
