@@ -22,6 +22,7 @@ host->device token input and device->host token output from pinned memory.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -313,8 +314,7 @@ def main():
         max_batch_size=B, comm_impl=args.comm_impl, random_init=True, seed=0,
         num_micro_batches=2)
     # the model's tensors and modules are long-lived: move them out of the cyclic
-    # collector's generations so a collection during a timed region stays short
-    import gc
+    # collector's generations so a collection between timed regions stays short
     gc.collect()
     gc.freeze()
     V = model.config.vocab_size
@@ -357,6 +357,8 @@ def main():
         bar()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
+        # no cyclic-GC pause inside the timed region (as in generate)
+        gc.disable()
         if clocks is not None:
             clocks.mark_start()
         s.record()
@@ -366,6 +368,7 @@ def main():
         torch.cuda.synchronize()
         if clocks is not None:
             clocks.mark_end()
+        gc.enable()
         ctx.barrier()
         ms = s.elapsed_time(e)
         if world > 1:
