@@ -81,9 +81,12 @@ class PipelineEngine:
         every = {s_main, s_ffn} | set(mb_streams or ())
         for s in every - {None}:
             s.wait_stream(caller)
+        # two streams sharing one GPU: no programmatic dependent launch (see ops.no_pdl)
+        two_streams_one_gpu = colocated and not serial and s_main is not None
         try:
-            return self._forward(plan, input_ids, serial, crosslayer, trackers or {}, last_only,
-                                 advance_cache, s_main, s_ffn, mb_streams)
+            with (ops.no_pdl() if two_streams_one_gpu else _Null()):
+                return self._forward(plan, input_ids, serial, crosslayer, trackers or {},
+                                     last_only, advance_cache, s_main, s_ffn, mb_streams)
         finally:
             for s in every - {None}:
                 caller.wait_stream(s)

@@ -46,6 +46,8 @@ int g_num_sms = 0;
 static int g_sm_cap = 0;
 
 void set_gemm_sm_cap(int64_t cap) { g_sm_cap = (int)cap; }
+// -1: launches follow AFD_PDL; 0 / 1: programmatic dependent launch off / on
+void set_pdl_override(int64_t v) { afd::set_pdl_override((int)v); }
 
 int num_sms() {
   if (g_num_sms == 0) {
@@ -758,6 +760,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("moe_gate", &moe_gate);
   m.def("set_gemm_sm_cap", &set_gemm_sm_cap);
+  m.def("set_pdl_override", &set_pdl_override);
   m.def("moe_align_mt", &moe_align_mt);
   m.def("gemm_down_combine", &gemm_down_combine);
   m.def("moe_gather", &moe_gather);

@@ -55,7 +55,12 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Process-wide override of programmatic dependent launch, set by the host
+// around work where it hurts (-1: none, 0: off, 1: on).
+inline int g_pdl_override = -1;
+
 inline bool pdl_enabled() {
+  if (g_pdl_override >= 0) return g_pdl_override == 1;
   static int on = -1;
   if (on < 0) {
     const char* e = getenv("AFD_PDL");

@@ -1482,6 +1482,8 @@ int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t*
                        counters, partials);
 }
 
+void set_pdl_override(int v) { g_pdl_override = v; }
+
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s) {
   return (int)launch_k(signal_flags_kernel, dim3(1), dim3(32), 0, s, a);
 }

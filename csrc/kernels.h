@@ -209,6 +209,9 @@ int launch_moe_combine(const MoeCombineArgs& a, int T, cudaStream_t s);
 int argmax_partial_ints(int rows, int V);
 int launch_argmax(const __nv_bfloat16* logits, int rows, int V, int ld, int64_t* out,
                   int* counters, int* partials, cudaStream_t s);
+// Process-wide override of programmatic dependent launch for later launches:
+// -1 follows AFD_PDL, 0 / 1 off / on.
+void set_pdl_override(int v);
 int launch_signal_flags(const FlagArgs& a, cudaStream_t s);
 int launch_wait_flags(const FlagArgs& a, cudaStream_t s);
 int launch_add_i32(int* p, int by, cudaStream_t s);
