@@ -11,7 +11,8 @@ this script loads the model once per job and runs every cell through
 
 Per cell and mode: decode TPOT (`decode_tpot_ms`, the reference's
 decode_loop_ms / (tokens - 1)) and prefill TTFT (`prefill_ms`), device-timed,
-max over ranks, the second of two runs (the first captures the CUDA graphs).
+max over ranks, measured after warm-up runs (the first captures the CUDA graphs;
+more follow while the caching allocator is still growing).
 Modes: serial (serial prefill and decode), dbo (prefill DBO, decode DBO),
 dbo-crosslayer (prefill DBO, cross-layer decode DBO). A cell whose batch the
 attention ranks cannot split into two micro-batches runs serial only. Rank 0
@@ -53,6 +54,11 @@ def main(argv=None) -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1:
+        # one GPU: both roles' streams hand tensors to each other; expandable
+        # segments keep the caching allocator from fragmenting (set before the
+        # first CUDA allocation)
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     devmod.init_backend("cuda")
     torch.cuda.set_device(local)
     ctx = get_distributed_context()
@@ -95,7 +101,19 @@ def main(argv=None) -> int:
                           num_decode_micro_batches=2, decode_use_crosslayer=xl,
                           prefill_mode="dbo" if dbo else "serial",
                           num_prefill_micro_batches=2 if dbo else 1, use_cuda_graph=True)
-                model.generate(ids, **kw)  # captures this batch's graphs
+                # warm-up: captures this batch's graphs, and repeats (at most 4
+                # times, every rank agreeing) while the caching allocator still
+                # adds device segments, whose cudaMalloc stalls would land in
+                # the measured call
+                last = -1
+                for i in range(4):
+                    model.generate(ids, **kw)
+                    torch.cuda.synchronize()
+                    n = int(torch.cuda.memory_stats().get("num_device_alloc", 0))
+                    grew = mx([1.0 if (i < 1 or n != last) else 0.0])[0]
+                    last = n
+                    if grew == 0.0:
+                        break
                 model.generate(ids, **kw)
                 m = model._last_generation_metrics
                 pf, tp = mx([m["prefill_ms"], m["decode_tpot_ms"]])
