@@ -401,6 +401,33 @@ class DisaggregatedQwenModel:
     def release_graphs(self) -> None:
         self._graphs.clear()
 
+    def warm_up(self, input_ids: torch.Tensor, max_rounds: int = 8, **generate_kwargs) -> int:
+        """Runs `generate(input_ids, **generate_kwargs)` until the CUDA caching
+        allocator stops adding device segments (at most `max_rounds` calls;
+        every rank runs the same number). Until then, a forward can stall on
+        cudaMalloc for up to hundreds of ms; with both roles on one GPU the two
+        streams hand tensors to each other, and the pool keeps growing for
+        several forwards. Call it at the largest batch and prompt that will be
+        served, after starting the process with
+        ``PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True`` on one GPU.
+        Returns the number of calls made (1 without CUDA)."""
+        import torch.distributed as dist
+
+        last = -1
+        for i in range(max(1, max_rounds)):
+            self.generate(input_ids, **generate_kwargs)
+            if self.device.type != "cuda":
+                return i + 1
+            torch.cuda.synchronize(self.device)
+            n = int(torch.cuda.memory_stats(self.device).get("num_device_alloc", 0))
+            grew = torch.tensor([1.0 if (i < 1 or n != last) else 0.0], device=self.device)
+            if self.ctx.world_size > 1 and dist.is_initialized():
+                dist.all_reduce(grew, op=dist.ReduceOp.MAX)
+            last = n
+            if float(grew.item()) == 0.0:
+                return i + 1
+        return max(1, max_rounds)
+
     # --------------------------------------------------------- generation
     def generate(self, *args, **kwargs) -> torch.Tensor:
         """See ``_generate``. A failure on this rank is published to the

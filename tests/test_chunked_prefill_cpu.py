@@ -89,3 +89,8 @@ def test_generate_restores_the_garbage_collector(model):
         assert not gc.isenabled()
     finally:
         gc.enable()
+
+
+def test_warm_up_runs_generate(model):
+    """On CPU there is no caching allocator to watch: one call."""
+    assert model.warm_up(_ids(10), max_new_tokens=2, do_sample=False) == 1

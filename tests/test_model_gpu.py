@@ -40,3 +40,14 @@ def test_chunked_prefill_matches_one_shot(model, chunk):
     assert got.shape == full.shape
     assert _rel(got, full) < 3e-2
     assert _rel(got[:, -1], full[:, -1]) < 3e-2
+
+
+def test_warm_up_settles_the_allocator(model):
+    """warm_up repeats generate until a call adds no CUDA segment (bounded)."""
+    ids = _ids(4, 64, 43)
+    kw = dict(max_new_tokens=3, do_sample=False, use_decode_dbo=True,
+              decode_use_crosslayer=True, prefill_mode="dbo", num_prefill_micro_batches=2)
+    n = model.warm_up(ids, max_rounds=6, **kw)
+    assert 1 <= n <= 6
+    out = model.generate(ids, **kw)
+    assert out.shape == (4, 67)
