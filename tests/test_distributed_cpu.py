@@ -1,7 +1,8 @@
-"""Multi-process runs on CPU with gloo: 1 attention + 1 FFN rank and
-2 attention (data parallel) + 2 FFN (expert parallel) ranks must generate the
-same greedy tokens as the single-process model, in serial, DBO and
-cross-layer DBO schedules (the tiny Qwen3-MoE oracle configuration)."""
+"""Multi-process runs on CPU with gloo: 1 attention + 1 FFN rank,
+2 attention (data parallel) + 2 FFN (expert parallel) ranks, and the uneven
+splits 1 attention + 2 FFN and 2 attention + 1 FFN must generate the same greedy
+tokens as the single-process model, in serial, DBO and cross-layer DBO schedules
+(the tiny Qwen3-MoE oracle configuration)."""
 
 import os
 import socket
@@ -46,7 +47,7 @@ def _mask():
     return m
 
 
-def _worker(rank, world, port, ckpt, modes, out_dir):
+def _worker(rank, world, port, ckpt, modes, out_dir, n_attn=None):
     import torch
 
     from afd_demo_b200.models import DisaggregatedQwenModel
@@ -57,7 +58,7 @@ def _worker(rank, world, port, ckpt, modes, out_dir):
     ctx = get_distributed_context()
     ctx.initialize(DistributedConfig(world_size=world, rank=rank, backend="gloo",
                                      master_addr="127.0.0.1", master_port=str(port),
-                                     timeout_s=120))
+                                     n_attn=n_attn, timeout_s=120))
     m = DisaggregatedQwenModel.from_pretrained(ckpt, device="cpu", dtype=torch.float32,
                                                max_seq_len=64, max_batch_size=4,
                                                comm_impl="nccl")
@@ -90,13 +91,13 @@ def _reference(ckpt):
     return toks, m.run_forward(_ids(), "serial", 1, reset_cache=True, attention_mask=_mask())
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_multi_rank_matches_single_process(ckpt, world):
+@pytest.mark.parametrize("world,n_attn", [(2, 1), (4, 2), (3, 1), (3, 2)],
+                         ids=["1A1F", "2A2F", "1A2F", "2A1F"])
+def test_multi_rank_matches_single_process(ckpt, world, n_attn):
     want, want_logits = _reference(ckpt)
     out = tempfile.mkdtemp(prefix="afd_out_")
-    mp.start_processes(_worker, args=(world, _free_port(), ckpt, MODES, out), nprocs=world,
-                       join=True, start_method="spawn")
-    n_attn = world // 2
+    mp.start_processes(_worker, args=(world, _free_port(), ckpt, MODES, out, n_attn),
+                       nprocs=world, join=True, start_method="spawn")
     for name in MODES:
         got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))[name]
                          for a in range(n_attn)])
