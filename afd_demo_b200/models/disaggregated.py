@@ -428,6 +428,47 @@ class DisaggregatedQwenModel:
                 return i + 1
         return max(1, max_rounds)
 
+    @torch.no_grad()
+    def transport_agreement(self, input_ids: torch.Tensor, mode: str = "dbo",
+                            num_micro_batches: int = 2, crosslayer: bool = True
+                            ) -> Dict[str, float]:
+        """Self-check of the A2F/F2A transport in use against NCCL
+        point-to-point (the reference's mechanism; gloo on CPU): one prefill
+        forward of `input_ids` from an empty cache over each, with the same
+        kernels otherwise. Returns ``max_abs_diff``, the largest |difference|
+        of the last-position logits, and ``argmax_agree``, the fraction of
+        sequences whose greedy next token is the same, agreed over every
+        rank (max and min). Every rank calls it with the same arguments; the
+        cache holds the second forward's keys and values afterwards."""
+        import torch.distributed as dist
+
+        if self.ctx.is_colocated:
+            raise ValueError("one process holds both roles: there is no transport to compare")
+        cuda = self.device.type == "cuda"
+        first = self.run_forward(input_ids, mode, num_micro_batches, crosslayer, reset_cache=True)
+        if cuda:
+            torch.cuda.synchronize(self.device)
+        saved = (self.transport, self.comm_impl)
+        self.transport = NcclTransport(self.ctx, self.hidden_size, self.dtype, self.device,
+                                       crosslayer=crosslayer)
+        self.comm_impl = "nccl"
+        try:
+            second = self.run_forward(input_ids, mode, num_micro_batches, crosslayer,
+                                      reset_cache=True)
+            if cuda:
+                torch.cuda.synchronize(self.device)
+        finally:
+            self.transport, self.comm_impl = saved
+        diff, agree = 0.0, 1.0
+        if first is not None and first.shape[0] > 0:
+            a, b = first.float(), second.float()
+            diff = float((a - b).abs().max())
+            agree = float((a.argmax(-1) == b.argmax(-1)).float().mean())
+        t = torch.tensor([diff, -agree], dtype=torch.float64, device=self.device)
+        if self.ctx.world_size > 1 and dist.is_initialized():
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return {"max_abs_diff": float(t[0]), "argmax_agree": -float(t[1])}
+
     # --------------------------------------------------------- generation
     def generate(self, *args, **kwargs) -> torch.Tensor:
         """See ``_generate``. A failure on this rank is published to the

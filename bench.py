@@ -170,6 +170,8 @@ def measure_cells(model, args, B, S, T, local, world, timed, ctx):
     * 8 GPUs: prefill TTFT at batch 32, prompt 512, DBO (2 micro-batches)
       and serial; cross-layer DBO and serial decode TPOT at batch 16, 64 and
       256, prompt 256, 20 tokens, through ``generate``;
+    * N > 1: one prefill over the fused transport and over NCCL, compared
+      (largest logit difference, share of equal greedy tokens);
     * N > 1: the headline decode step with the A2F/F2A hand-offs over NCCL
       isend/irecv (the reference's mechanism) instead of the fused
       peer-memory path, both run eagerly (the NCCL path keeps host-side work
@@ -234,6 +236,11 @@ def measure_cells(model, args, B, S, T, local, world, timed, ctx):
             model.release_graphs()
         out["decode_s256_8gpu"] = sweep
     if world > 1:
+        # correctness record: the same prefill over the fused transport and
+        # over NCCL isend/irecv, greedy tokens and logits compared
+        agree = model.transport_agreement(ids_of(B, S, 1234), "dbo", 2, crosslayer=True)
+        out["transport_agreement"] = dict(agree, batch=B, seq_len=S,
+                                          mode="prefill DBO, cross-layer, fused vs NCCL")
         # eager decode steps: fused peer-memory transport vs NCCL isend/irecv
         logits = model.run_forward(ids_of(B, S, 1234), "dbo", 2, crosslayer=True,
                                    reset_cache=True)

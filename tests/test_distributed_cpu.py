@@ -67,6 +67,8 @@ def _worker(rank, world, port, ckpt, modes, out_dir, n_attn=None):
         res[name] = m.generate(_ids(), max_new_tokens=5, do_sample=False, **kw)
     res["padded_prefill"] = m.run_forward(_ids(), "dbo", 2, reset_cache=True,
                                           attention_mask=_mask())
+    # every rank gets the same agreed figures
+    res["agreement"] = m.transport_agreement(_ids())
     if ctx.is_attention_node:
         torch.save(res, os.path.join(out_dir, f"attn{ctx.attn_index}.pt"))
     ctx.barrier()
@@ -106,6 +108,10 @@ def test_multi_rank_matches_single_process(ckpt, world, n_attn):
     got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))["padded_prefill"]
                      for a in range(n_attn)])
     torch.testing.assert_close(got, want_logits, rtol=1e-4, atol=1e-4)
+    # the transport self-check: the same transport twice is the same computation
+    for a in range(n_attn):
+        agreement = torch.load(os.path.join(out, f"attn{a}.pt"))["agreement"]
+        assert agreement == {"max_abs_diff": 0.0, "argmax_agree": 1.0}, agreement
 
 
 def test_single_process_schedules_agree(ckpt):
@@ -119,3 +125,5 @@ def test_single_process_schedules_agree(ckpt):
             for k, kw in MODES.items()}
     assert torch.equal(outs["serial"], outs["dbo"])
     assert torch.equal(outs["serial"], outs["xl"])
+    with pytest.raises(ValueError, match="no transport"):
+        m.transport_agreement(_ids())

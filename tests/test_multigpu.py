@@ -1,6 +1,7 @@
 """Multi-GPU runs (one process per GPU) of the fused peer-memory transport
-and the NCCL baseline against the single-GPU model. Skipped with fewer than
-two GPUs. NVLS stays off (plain peer loads/stores only)."""
+and the NCCL baseline against the single-GPU model, and the fused transport
+against NCCL on the same ranks (``transport_agreement``). Skipped with fewer
+than two GPUs. NVLS stays off (plain peer loads/stores only)."""
 
 import os
 import socket
@@ -56,9 +57,12 @@ def _run(rank, world, port, impl, out_dir):
         res[name] = m.generate(ids, max_new_tokens=6, do_sample=False, **kw)
     torch.cuda.synchronize()
     m.transport.check()
+    # the fused transport against NCCL point-to-point on one prefill
+    agreement = m.transport_agreement(ids) if impl == "fused" else None
     if ctx.is_attention_node:
-        torch.save({k: v.cpu() for k, v in res.items() if v is not None},
-                   os.path.join(out_dir, f"{impl}_w{world}_a{ctx.attn_index}.pt"))
+        out = {k: v.cpu() for k, v in res.items() if v is not None}
+        out["agreement"] = agreement
+        torch.save(out, os.path.join(out_dir, f"{impl}_w{world}_a{ctx.attn_index}.pt"))
     m.release_graphs()
     ctx.barrier()
     ctx.cleanup()
@@ -115,6 +119,11 @@ def test_multi_gpu_matches_single(single, impl, world):
     assert float((long - ref_long).norm() / ref_long.norm()) < 2e-2
     if world == 2:  # no expert split: bitwise the single-GPU computation
         assert torch.equal(torch.cat([g["serial"] for g in got]), want["serial"])
+    if impl == "fused":
+        a = got[0]["agreement"]
+        print(f"fused vs NCCL transport, world {world}: {a}")
+        assert all(g["agreement"] == a for g in got)  # agreed over every rank
+        assert a["argmax_agree"] == 1.0 and a["max_abs_diff"] < 0.25, a
     for g in got:
         # same schedule eager vs captured graph: identical kernels, identical tokens
         assert torch.equal(g["xl"], g["graph"])
