@@ -56,6 +56,14 @@ class DisaggregatedQwenModel:
         if not self.ctx.initialized:
             from ..parallel.dist import DistributedConfig
             self.ctx.initialize(DistributedConfig(world_size=1, backend=devmod.DIST_BACKEND))
+        if self.device.type == "cuda":
+            # streams, CUDA graphs and the peer-memory mappings are made on the
+            # current device: make it this model's (one process drives one GPU)
+            if self.device.index is None:
+                self.device = torch.device("cuda", torch.cuda.current_device())
+            elif torch.cuda.current_device() != self.device.index:
+                logger.info(f"current CUDA device set to {self.device}")
+                torch.cuda.set_device(self.device)
         self.hidden_size = config.hidden_size
         self.num_layers = config.num_hidden_layers
         self.model_type = config.model_type

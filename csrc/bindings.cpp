@@ -22,6 +22,12 @@ inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().strea
 #define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
 #define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
 #define CHECK_ROWMAJOR(x) TORCH_CHECK((x).stride(-1) == 1, #x " must have unit inner stride")
+// Every launch goes to the current stream of the device that holds the op's
+// tensors, whichever device the calling thread has current (a process may
+// drive several GPUs); the previous device is restored on return.
+#define DEVICE_GUARD(x)                                  \
+  TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor"); \
+  const c10::cuda::CUDAGuard device_guard_((x).device())
 
 inline void check_rc(int rc, const char* what) {
   TORCH_CHECK(rc == 0, what, " failed with code ", rc,
@@ -69,6 +75,7 @@ void gemm(const at::Tensor& w, const at::Tensor& x, at::Tensor& out, int64_t f_t
           const c10::optional<at::Tensor>& epoch, int64_t k_splits,
           const c10::optional<at::Tensor>& ws, const c10::optional<at::Tensor>& tile_counters,
           const c10::optional<at::Tensor>& row_ids, bool token_major, bool stream_k) {
+  DEVICE_GUARD(x);
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(out);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(out);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
@@ -158,6 +165,7 @@ void gemm_down_combine(const at::Tensor& w, const at::Tensor& x, at::Tensor& y, 
                        const c10::optional<at::Tensor>& done_counter,
                        const c10::optional<at::Tensor>& status,
                        const c10::optional<at::Tensor>& epoch, at::Tensor& cmb_counters) {
+  DEVICE_GUARD(x);
   CHECK_CUDA(w); CHECK_CUDA(x); CHECK_CUDA(y);
   CHECK_BF16(w); CHECK_BF16(x); CHECK_BF16(y);
   CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(y);
@@ -240,6 +248,7 @@ void sum_rmsnorm(std::vector<at::Tensor> parts, const at::Tensor& weight,
                  const c10::optional<at::Tensor>& status, int64_t timeout_ns,
                  const c10::optional<at::Tensor>& epoch) {
   TORCH_CHECK(!parts.empty() && parts.size() <= (size_t)afd::kMaxParts, "1..8 parts");
+  DEVICE_GUARD(parts[0]);
   afd::SumNormArgs a{};
   const int64_t H = parts[0].size(-1);
   const int64_t rows = parts[0].numel() / H;
@@ -264,6 +273,7 @@ void qk_norm_rope_cache(const at::Tensor& qkv, const at::Tensor& q_norm, const a
                         const at::Tensor& rope, at::Tensor& q_out, at::Tensor& k_cache,
                         at::Tensor& v_cache, const at::Tensor& start_pos, int64_t q_len,
                         int64_t batch_offset, int64_t nq, int64_t nkv, double eps) {
+  DEVICE_GUARD(qkv);
   CHECK_BF16(qkv); CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(q_out);
   TORCH_CHECK(rope.scalar_type() == at::kFloat, "rope table must be fp32");
   TORCH_CHECK(start_pos.scalar_type() == at::kInt, "start_pos must be int32");
@@ -292,6 +302,7 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
                       at::Tensor& out, const at::Tensor& start_pos, int64_t batch_offset,
                       int64_t nsplit, const c10::optional<at::Tensor>& o_part,
                       const c10::optional<at::Tensor>& ml_part) {
+  DEVICE_GUARD(q);
   afd::DecodeAttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);
@@ -322,6 +333,7 @@ void decode_attention_tc(const c10::optional<at::Tensor>& q, at::Tensor& k_cache
                          const c10::optional<at::Tensor>& q_norm,
                          const c10::optional<at::Tensor>& k_norm,
                          const c10::optional<at::Tensor>& rope, double eps) {
+  DEVICE_GUARD(k_cache);
   CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(out);
   TORCH_CHECK(out.is_contiguous() && out.dim() == 3, "out must be contiguous [B, nq, D]");
   TORCH_CHECK(start_pos.scalar_type() == at::kInt, "start_pos must be int32");
@@ -370,6 +382,7 @@ void decode_attention_fused(const at::Tensor& qkv, const at::Tensor& q_norm,
                             const at::Tensor& k_norm, const at::Tensor& rope, at::Tensor& k_cache,
                             at::Tensor& v_cache, at::Tensor& out, const at::Tensor& start_pos,
                             int64_t batch_offset, int64_t nq, double eps) {
+  DEVICE_GUARD(qkv);
   CHECK_BF16(qkv); CHECK_BF16(k_cache); CHECK_BF16(v_cache); CHECK_BF16(out);
   TORCH_CHECK(rope.scalar_type() == at::kFloat, "rope table must be fp32");
   afd::FusedDecodeArgs a{};
@@ -396,6 +409,7 @@ void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at:
                        at::Tensor& out, const at::Tensor& start_pos, int64_t q_len,
                        int64_t batch_offset, const c10::optional<at::Tensor>& key_lo,
                        const c10::optional<at::Tensor>& key_hi, int64_t variant) {
+  DEVICE_GUARD(q);
   afd::PrefillAttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);
@@ -432,6 +446,7 @@ void prefill_attention(const at::Tensor& q, const at::Tensor& k_cache, const at:
 
 void router_topk(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, int64_t top_k,
                  bool renorm) {
+  DEVICE_GUARD(logits);
   afd::RouterArgs a{};
   a.logits = cbf(logits);
   a.ld_logits = (int)logits.stride(0);
@@ -448,6 +463,7 @@ void moe_align(const at::Tensor& ids, const at::Tensor& weights, int64_t expert_
                int64_t n_local, int64_t block_n, at::Tensor& inv, at::Tensor& row_token,
                at::Tensor& row_weight, at::Tensor& expert_offsets, at::Tensor& blocks,
                at::Tensor& num_blocks, at::Tensor& num_rows) {
+  DEVICE_GUARD(ids);
   afd::MoeAlignArgs a{};
   a.ids = ids.data_ptr<int32_t>();
   a.weights = weights.data_ptr<float>();
@@ -472,6 +488,7 @@ void moe_align_mt(const at::Tensor& ids, const at::Tensor& weights, int64_t expe
                at::Tensor& row_weight, at::Tensor& expert_offsets, at::Tensor& blocks,
                at::Tensor& num_blocks, at::Tensor& num_rows, at::Tensor& part,
                at::Tensor& counter) {
+  DEVICE_GUARD(ids);
   afd::MoeAlignArgs a{};
   a.ids = ids.data_ptr<int32_t>();
   a.weights = weights.data_ptr<float>();
@@ -501,6 +518,7 @@ void moe_route(const at::Tensor& logits, at::Tensor& ids, at::Tensor& weights, i
                at::Tensor& inv, at::Tensor& row_token, at::Tensor& row_weight,
                at::Tensor& expert_offsets, at::Tensor& blocks, at::Tensor& num_blocks,
                at::Tensor& num_rows) {
+  DEVICE_GUARD(logits);
   afd::RouterArgs r{};
   r.logits = cbf(logits);
   r.ld_logits = (int)logits.stride(0);
@@ -538,6 +556,7 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
               const c10::optional<at::Tensor>& status, int64_t timeout_ns,
               const c10::optional<at::Tensor>& epoch,
               const c10::optional<at::Tensor>& stamps) {
+  DEVICE_GUARD(h);
   TORCH_CHECK(h.stride(1) == 1 && xn.is_contiguous() && logits.is_contiguous() &&
                   w_router.is_contiguous(),
               "moe_gate: contiguous rows expected");
@@ -582,6 +601,7 @@ void moe_gate(const at::Tensor& h, const at::Tensor& norm_w, const at::Tensor& w
 
 void moe_gather(const at::Tensor& x, const at::Tensor& row_token, const at::Tensor& num_rows,
                 at::Tensor& out, int64_t max_rows) {
+  DEVICE_GUARD(x);
   afd::MoeGatherArgs a{};
   a.x = cbf(x);
   a.ld_x = (int)x.stride(0);
@@ -598,6 +618,7 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv, int64_t T, int64_t 
                  int64_t peer_row_offset, std::vector<int64_t> flags, int64_t signal_value,
                  const c10::optional<at::Tensor>& done_counter,
                  const c10::optional<at::Tensor>& epoch) {
+  DEVICE_GUARD(y);
   TORCH_CHECK(peers.size() <= 8 && flags.size() <= (size_t)afd::kMaxFlagPeers, "too many peers");
   TORCH_CHECK(peers.empty() || seg_offsets.size() == peers.size() + 1,
               "seg_offsets needs one entry per peer plus the end");
@@ -630,6 +651,7 @@ void moe_combine(const at::Tensor& y, const at::Tensor& inv, int64_t T, int64_t 
 
 void argmax(const at::Tensor& logits, at::Tensor& out, const c10::optional<at::Tensor>& counters,
             const c10::optional<at::Tensor>& partials) {
+  DEVICE_GUARD(logits);
   CHECK_BF16(logits);
   TORCH_CHECK(logits.stride(1) == 1, "argmax: rows must be contiguous");
   const int rows = (int)logits.size(0);
@@ -671,6 +693,8 @@ afd::FlagArgs flag_args(const std::vector<int64_t>& flags, int64_t value,
 
 void signal_flags(std::vector<int64_t> flags, int64_t value,
                   const c10::optional<at::Tensor>& epoch) {
+  c10::cuda::OptionalCUDAGuard device_guard_;
+  if (epoch.has_value() && epoch->is_cuda()) device_guard_.set_device(epoch->device());
   check_rc(afd::launch_signal_flags(flag_args(flags, value, c10::nullopt, 0, epoch), cur_stream()),
            "signal_flags");
 }
@@ -680,6 +704,9 @@ void signal_flags(std::vector<int64_t> flags, int64_t value,
 // word records kTimeoutPeerFlag and the stream continues.
 void wait_flags(std::vector<int64_t> flags, int64_t value, const c10::optional<at::Tensor>& status,
                 int64_t timeout_ns, const c10::optional<at::Tensor>& epoch) {
+  c10::cuda::OptionalCUDAGuard device_guard_;
+  if (status.has_value() && status->is_cuda()) device_guard_.set_device(status->device());
+  else if (epoch.has_value() && epoch->is_cuda()) device_guard_.set_device(epoch->device());
   check_rc(afd::launch_wait_flags(flag_args(flags, value, status, timeout_ns, epoch), cur_stream()),
            "wait_flags");
 }
@@ -687,6 +714,7 @@ void wait_flags(std::vector<int64_t> flags, int64_t value, const c10::optional<a
 void peer_copy(const at::Tensor& src, std::vector<int64_t> dst, std::vector<int64_t> flags,
                int64_t signal_value, const c10::optional<at::Tensor>& done_counter,
                const c10::optional<at::Tensor>& epoch, int64_t grid) {
+  DEVICE_GUARD(src);
   TORCH_CHECK(dst.size() <= 8 && flags.size() == dst.size(), "1..8 peers with one flag each");
   afd::PeerCopyArgs a{};
   a.src = src.data_ptr();
@@ -703,6 +731,7 @@ void peer_copy(const at::Tensor& src, std::vector<int64_t> dst, std::vector<int6
 }
 
 void add_i32(at::Tensor& t, int64_t by) {
+  DEVICE_GUARD(t);
   check_rc(afd::launch_add_i32(t.data_ptr<int>(), (int)by, cur_stream()), "add_i32");
 }
 
@@ -723,6 +752,7 @@ at::Tensor ipc_alloc(int64_t nbytes, int64_t device) {
 }
 
 pybind11::bytes ipc_handle(const at::Tensor& t) {
+  DEVICE_GUARD(t);
   cudaIpcMemHandle_t h;
   cudaError_t e = cudaIpcGetMemHandle(&h, t.data_ptr());
   TORCH_CHECK(e == cudaSuccess, "cudaIpcGetMemHandle: ", cudaGetErrorString(e));

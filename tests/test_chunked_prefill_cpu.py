@@ -94,3 +94,29 @@ def test_generate_restores_the_garbage_collector(model):
 def test_warm_up_runs_generate(model):
     """On CPU there is no caching allocator to watch: one call."""
     assert model.warm_up(_ids(10), max_new_tokens=2, do_sample=False) == 1
+
+
+def test_model_makes_its_cuda_device_current(monkeypatch):
+    """A model on cuda:k makes device k current (its streams, graphs and
+    peer mappings are made on the current device); a bare "cuda" takes the
+    current device's index. CUDA calls are faked: no GPU is needed."""
+    from afd_demo_b200.models import DisaggregatedQwenModel
+    from afd_demo_b200.utils import device as devmod
+
+    devmod.init_backend("cpu")
+    current = {"dev": 0}
+    calls = []
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: current["dev"])
+
+    def set_device(d):
+        calls.append(torch.device(d).index)
+        current["dev"] = torch.device(d).index
+
+    monkeypatch.setattr(torch.cuda, "set_device", set_device)
+    m = DisaggregatedQwenModel(tiny_qwen3_moe(), "cuda:1")
+    assert m.device == torch.device("cuda:1") and calls == [1]
+    m = DisaggregatedQwenModel(tiny_qwen3_moe(), "cuda:1")  # already current: no call
+    assert calls == [1]
+    current["dev"] = 3
+    m = DisaggregatedQwenModel(tiny_qwen3_moe(), "cuda")
+    assert m.device == torch.device("cuda:3") and calls == [1]
