@@ -212,3 +212,49 @@ def test_decode_cells_cli():
     assert p.returncode == 0, p.stderr
     for opt in ("--batches", "--seqs", "--modes", "--attn-gpus", "--output"):
         assert opt in p.stdout
+
+
+def test_run_node_reference_form_dry_run():
+    """run_node.sh <role> [master_addr] [master_port] [options]: the role picks
+    the rank and is passed on; options pass through; other first words fail."""
+    def cmd(*a):
+        p = subprocess.run(["bash", "afd_demo_b200/scripts/run_node.sh", *a], cwd=ROOT,
+                           env=dict(os.environ, RUN_NODE_DRY_RUN="1"), capture_output=True,
+                           text=True, timeout=60)
+        return p.returncode, p.stdout.split(), p.stderr
+
+    rc, argv, _ = cmd("ffn", "10.1.2.3", "29600", "--no-dbo")
+    assert rc == 0
+    flag = lambda f: argv[argv.index(f) + 1]  # noqa: E731
+    assert (flag("--role"), flag("--rank"), flag("--master-addr"), flag("--master-port")) == \
+        ("ffn", "1", "10.1.2.3", "29600")
+    assert argv[-1] == "--no-dbo"
+    rc, argv, _ = cmd("attention", "--greedy")
+    assert rc == 0 and flag("--rank") == "0" and flag("--master-port") == "29500"
+    rc, argv, _ = cmd("--no-dbo")  # environment form: no role
+    assert rc == 0 and "--role" not in argv
+    rc, _, err = cmd("worker")
+    assert rc == 1 and "role must be" in err
+
+
+def test_run_node_reference_form_two_ranks(tmp_path):
+    """Both roles started the reference's way (role, address, port) on CPU
+    over gloo with the tiny model; each rank exits 0."""
+    port = str(_free_port())
+    env = dict(os.environ, MODEL_PATH="tiny", BATCH_SIZE="2", MAX_SEQ_LEN="32", TOKENS="3",
+               CUDA_DEVICES="")
+    common = ["127.0.0.1", port, "--synthetic", "--prefill-seq-len", "8", "--greedy",
+              "--no-dbo", "--results-dir", str(tmp_path)]
+    procs = [subprocess.Popen(["bash", "afd_demo_b200/scripts/run_node.sh", role, *common],
+                              cwd=ROOT, env=env, stdout=subprocess.PIPE,
+                              stderr=subprocess.STDOUT, text=True)
+             for role in ("attention", "ffn")]
+    outs = []
+    try:
+        for p in procs:
+            outs.append(p.communicate(timeout=600)[0])
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    assert [p.returncode for p in procs] == [0, 0], "\n".join(o[-2000:] for o in outs)
