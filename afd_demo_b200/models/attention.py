@@ -48,6 +48,28 @@ class AttentionWorker:
         # (padding masks), set by the model around one forward; None = causal only
         self.key_range = None
 
+    @classmethod
+    def from_pretrained(cls, model_name: str, device, dtype=torch.bfloat16,
+                        max_batch: int = 4, max_seq: int = 2048,
+                        random_init: Optional[bool] = None, seed: int = 0) -> "AttentionWorker":
+        """Reference: ``AttentionWorker.from_pretrained``
+        (src/model/attention_worker.py:316-344), which loads the whole HF
+        model on the CPU and keeps its attention parts. Here only the
+        checkpoint's attention-side tensors (embedding, attention, norms, LM
+        head) are read, straight to `device`; a preset name without a
+        checkpoint directory gets random weights (`seed`)."""
+        import os
+
+        from ..config import resolve_model_config
+        from .weights import load_attention_weights, random_attention_weights
+
+        cfg = resolve_model_config(model_name)
+        if random_init is None:
+            random_init = not os.path.isdir(model_name)
+        w = (random_attention_weights(cfg, seed, device, dtype) if random_init
+             else load_attention_weights(model_name, cfg, device, dtype))
+        return cls(cfg, w, device, dtype, max_batch, max_seq)
+
     # ------------------------------------------------------------------
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         """[B, S] ids -> [B*S, H] hidden states."""

@@ -44,6 +44,28 @@ class FFNWorker:
         self.tracker = None  # optional TimingTracker for router / experts spans
         self.layers = [FFNLayer(self, l) for l in range(self.num_layers)]
 
+    @classmethod
+    def from_pretrained(cls, model_name: str, device, dtype=torch.bfloat16,
+                        expert_range: Optional[range] = None,
+                        random_init: Optional[bool] = None, seed: int = 0) -> "FFNWorker":
+        """Reference: ``FFNWorker.from_pretrained`` (src/model/ffn_worker.py:228-256),
+        which loads the whole HF model on the CPU and keeps its MLP parts.
+        Here only the checkpoint's FFN-side tensors (post-attention norms,
+        routers, the experts in `expert_range` (default all) and dense MLPs) are read,
+        straight to `device`; a preset name without a checkpoint directory
+        gets random weights (`seed`)."""
+        import os
+
+        from ..config import resolve_model_config
+        from .weights import load_ffn_weights, random_ffn_weights
+
+        cfg = resolve_model_config(model_name)
+        if random_init is None:
+            random_init = not os.path.isdir(model_name)
+        w = (random_ffn_weights(cfg, expert_range, seed, device, dtype) if random_init
+             else load_ffn_weights(model_name, cfg, expert_range, device, dtype))
+        return cls(cfg, w, device, dtype)
+
     def _mark(self, start: bool, et: EventType, l: int, mb: int):
         if self.tracker is not None:
             (self.tracker.mark_start if start else self.tracker.mark_end)(et, l, mb)

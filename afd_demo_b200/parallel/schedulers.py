@@ -99,18 +99,38 @@ def _finish(trackers: Dict[str, TimingTracker], ctx) -> Optional[PipelineTiming]
 
 
 class SimplePipelineScheduler:
-    def __init__(self, model, num_micro_batches: int = 2):
+    """Serial schedule (reference: src/pipeline/scheduler.py:20-57, 132-...):
+    the micro-batches of each layer run one after another, with the same
+    constructor, ``run`` and ``get_timing_data`` as the reference's. With
+    `enable_timing` the per-layer events go to a ``TimingTracker`` in
+    `timing_mode` ("cuda_events", "sync" or "device")."""
+
+    def __init__(self, model, num_micro_batches: int = 2, enable_timing: bool = False,
+                 timing_mode: str = "cuda_events"):
         self.model = model
         self.num_micro_batches = num_micro_batches
+        self.enable_timing = enable_timing
+        self.timing_mode = timing_mode
         self.mb_manager = MicroBatchManager(num_micro_batches, model.device)
+        self._timing_data: Optional[PipelineTiming] = None
 
     @torch.no_grad()
     def run(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None):
-        out = self.model.run_forward(input_ids, "serial", self.num_micro_batches,
-                                     reset_cache=True, attention_mask=attention_mask)
-        if self.model.transport is not None and devmod.is_cuda():
-            self.model.transport.check()
+        m = self.model
+        nmb = min(self.num_micro_batches, input_ids.shape[0])
+        tr = _trackers(m, self.enable_timing, nmb, self.timing_mode, "enqueue")
+        out = m.run_forward(input_ids, "serial", self.num_micro_batches, trackers=tr,
+                            reset_cache=True, attention_mask=attention_mask)
+        if self.enable_timing:
+            devmod.synchronize()
+        self._timing_data = _finish(tr, m.ctx)
+        if m.transport is not None and devmod.is_cuda():
+            m.transport.check()
         return out
+
+    def get_timing_data(self) -> Optional[PipelineTiming]:
+        """The last run's timing (None unless `enable_timing`)."""
+        return self._timing_data
 
 
 class AsyncPipelineScheduler:

@@ -100,3 +100,26 @@ def test_schedules_agree_numerically(model):
                                   ("dbo", 2, True), ("dbo", 3, True))]
     for o in outs[1:]:
         torch.testing.assert_close(o, outs[0], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("timing_mode", ["cuda_events", "sync"])
+def test_serial_scheduler_timing(model, timing_mode):
+    """The reference's serial-scheduler interface: ``enable_timing`` fills
+    ``get_timing_data`` with per-layer, per-micro-batch events; without it the
+    timing stays None; the logits equal the engine's serial forward."""
+    from afd_demo_b200.parallel.schedulers import SimplePipelineScheduler
+
+    ids = torch.randint(0, 1024, (4, 9), generator=torch.Generator().manual_seed(2))
+    plain = SimplePipelineScheduler(model, 2)
+    out = plain.run(ids)
+    assert plain.get_timing_data() is None
+    timed = SimplePipelineScheduler(model, num_micro_batches=2, enable_timing=True,
+                                    timing_mode=timing_mode)
+    torch.testing.assert_close(timed.run(ids), out)
+    t = timed.get_timing_data()
+    assert t is not None and t.num_layers == model.num_layers and t.num_micro_batches == 2
+    assert t.total_time_ms > 0
+    d = t.to_dict()
+    layers = {e["layer"] for e in d["events"]}
+    assert layers == set(range(model.num_layers)), layers
+    assert {e["mb"] for e in d["events"]} == {0, 1}

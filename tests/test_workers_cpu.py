@@ -1,0 +1,53 @@
+"""The reference's worker constructors (``AttentionWorker.from_pretrained``,
+``FFNWorker.from_pretrained``) on CPU: each reads only its role's tensors of a
+checkpoint (an expert slice for the FFN), and a preset name gives random
+weights of the preset's shape."""
+
+import torch
+
+from afd_demo_b200.config import tiny_qwen3_moe
+from afd_demo_b200.models.attention import AttentionWorker
+from afd_demo_b200.models.ffn import FFNWorker
+from afd_demo_b200.models.weights import (random_attention_weights, random_ffn_weights,
+                                          save_checkpoint)
+
+
+def test_workers_from_a_checkpoint(tmp_path):
+    cfg = tiny_qwen3_moe()
+    aw0 = random_attention_weights(cfg, 0, "cpu", torch.float32)
+    fw0 = random_ffn_weights(cfg, None, 0, "cpu", torch.float32)
+    save_checkpoint(str(tmp_path), cfg, aw0, fw0)
+
+    aw = AttentionWorker.from_pretrained(str(tmp_path), "cpu", torch.float32, max_batch=2,
+                                         max_seq=32)
+    assert aw.num_layers == cfg.num_hidden_layers and len(aw.layers) == cfg.num_hidden_layers
+    torch.testing.assert_close(aw.w.embed, aw0.embed)
+    torch.testing.assert_close(aw.w.lm_head, aw0.lm_head)
+    assert (aw.cache.max_batch, aw.cache.max_seq) == (2, 32)
+
+    lo, hi = 2, 6
+    fw = FFNWorker.from_pretrained(str(tmp_path), "cpu", torch.float32,
+                                   expert_range=range(lo, hi))
+    assert fw.expert_range == range(lo, hi)
+    for l in range(cfg.num_hidden_layers):
+        got, want = fw.w.layers[l], fw0.layers[l]
+        torch.testing.assert_close(got.post_norm, want.post_norm)
+        torch.testing.assert_close(got.w_router, want.w_router)
+        torch.testing.assert_close(got.w_gate_up, want.w_gate_up[lo:hi])
+        torch.testing.assert_close(got.w_down, want.w_down[lo:hi])
+
+    # a worker built this way runs a layer
+    full = FFNWorker.from_pretrained(str(tmp_path), "cpu", torch.float32)
+    h = torch.randn(5, cfg.hidden_size, generator=torch.Generator().manual_seed(0))
+    out = full.forward_ffn_layer(0, h.clone())
+    assert out.shape == h.shape and torch.isfinite(out).all()
+
+
+def test_workers_from_a_preset():
+    cfg = tiny_qwen3_moe()
+    aw = AttentionWorker.from_pretrained("tiny", "cpu", torch.float32, max_seq=16)
+    fw = FFNWorker.from_pretrained("tiny", "cpu", torch.float32, seed=3)
+    assert aw.cfg.hidden_size == cfg.hidden_size and aw.num_layers == cfg.num_hidden_layers
+    assert fw.expert_range == range(cfg.num_experts)
+    again = FFNWorker.from_pretrained("tiny", "cpu", torch.float32, seed=3)
+    assert torch.equal(fw.w.layers[0].w_gate_up, again.w.layers[0].w_gate_up)
