@@ -14,9 +14,10 @@ shard layers over the role's visible GPUs. Here one B200 holds every layer
    transport the epilogue stores h straight into the FFN GPUs' receive
    buffers and raises their flags.
 
-``forward_attention_layer`` returns h = attn_out + residual, the
+``attention_block`` returns h = attn_out + residual, the
 "pre-combined" tensor the reference ships to the FFN
-(src/model/disaggregated.py:184).
+(src/model/disaggregated.py:184). ``forward_attention_layer`` and
+``forward_lm_head`` keep the reference's per-layer calls.
 """
 
 from __future__ import annotations
@@ -75,18 +76,38 @@ class AttentionWorker:
         """[B, S] ids -> [B*S, H] hidden states."""
         return torch.nn.functional.embedding(input_ids.reshape(-1), self.w.embed)
 
-    def get_position_embeddings(self, position_ids: torch.Tensor):
-        """(cos, sin) [B, S, D] for code written against the HF signature."""
+    def get_position_embeddings(self, hidden_states: torch.Tensor,
+                                position_ids: Optional[torch.Tensor] = None):
+        """(cos, sin) [B, S, D] for `position_ids`, with the reference's
+        signature (hidden_states, position_ids); `hidden_states` only gives
+        the call its HF shape. Called with one tensor, that tensor is taken as
+        the position ids."""
+        if position_ids is None:
+            position_ids = hidden_states
         D = self.cfg.head_dim
         cs = self.rope[position_ids.long()]
         cos = torch.cat([cs[..., : D // 2]] * 2, -1).to(self.dtype)
         sin = torch.cat([cs[..., D // 2:]] * 2, -1).to(self.dtype)
         return cos, sin
 
-    def forward_attention_layer(self, layer_idx: int, x_parts: Sequence[torch.Tensor],
-                                batch_offset: int, q_len: int, start_pos: Optional[int] = None,
-                                sink=None, out: Optional[torch.Tensor] = None,
-                                wait=None, add_residual: bool = True) -> torch.Tensor:
+    def forward_attention_layer(self, layer_idx: int, hidden_states: torch.Tensor,
+                                attention_mask: Optional[torch.Tensor] = None,
+                                position_ids: Optional[torch.Tensor] = None,
+                                position_embeddings=None, use_cache: bool = False,
+                                past_key_value=None):
+        """The reference's per-layer call
+        (src/model/attention_worker.py:271-307): `hidden_states` [B, S, H] ->
+        (attn_output, residual), plus the KV cache with `use_cache`. Same
+        behaviour as ``self.layers[layer_idx]`` (``AttentionLayer``)."""
+        return self.layers[layer_idx](hidden_states, attention_mask=attention_mask,
+                                      position_ids=position_ids,
+                                      past_key_value=past_key_value, use_cache=use_cache,
+                                      position_embeddings=position_embeddings)
+
+    def attention_block(self, layer_idx: int, x_parts: Sequence[torch.Tensor],
+                        batch_offset: int, q_len: int, start_pos: Optional[int] = None,
+                        sink=None, out: Optional[torch.Tensor] = None,
+                        wait=None, add_residual: bool = True) -> torch.Tensor:
         """One attention block for the micro-batch whose sequences occupy cache
         rows [batch_offset, batch_offset + T // q_len). `x_parts` are the
         layer inputs (the F2A partials); returns h = x + o_proj(attn). `wait`
@@ -116,8 +137,16 @@ class AttentionWorker:
             return ops.linear(o, lw.w_o, residual=x, out=out, **sink.gemm_kwargs())
         return ops.linear(o, lw.w_o, residual=x, out=out)
 
-    def forward_lm_head(self, x_parts: Sequence[torch.Tensor], q_len: int = 1,
-                        last_only: bool = True, wait=None) -> torch.Tensor:
+    def forward_lm_head(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        """The reference's call (src/model/attention_worker.py:309-313): final
+        RMSNorm + LM head over every position, [..., H] -> [..., V]."""
+        H = self.cfg.hidden_size
+        x = hidden_states.reshape(-1, H).to(self.device, self.dtype)
+        logits = self.lm_head_block([x], 1, last_only=False)
+        return logits.view(*hidden_states.shape[:-1], logits.shape[-1])
+
+    def lm_head_block(self, x_parts: Sequence[torch.Tensor], q_len: int = 1,
+                      last_only: bool = True, wait=None) -> torch.Tensor:
         """Final RMSNorm + LM head. With `last_only`, only the last position of
         each sequence is projected (that is all sampling needs); returns
         [B, V] (or [T, V])."""
@@ -161,8 +190,8 @@ class AttentionLayer:
                        if attention_mask is not None and attention_mask.dim() == 2 and S > 1
                        else None)
         try:
-            o = w.forward_attention_layer(self.layer_idx, [x], 0, S, start_pos=start,
-                                          add_residual=False)
+            o = w.attention_block(self.layer_idx, [x], 0, S, start_pos=start,
+                                  add_residual=False)
         finally:
             w.key_range = None
         out = (o.view(B, S, H), x.view(B, S, H))

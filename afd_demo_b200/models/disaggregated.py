@@ -338,7 +338,7 @@ class DisaggregatedQwenModel:
                         if attention_mask is not None and attention_mask.dim() == 2 and S > 1
                         else None)
         try:
-            h = aw.forward_attention_layer(layer_idx, [x], 0, S, start_pos=start)
+            h = aw.attention_block(layer_idx, [x], 0, S, start_pos=start)
         finally:
             aw.key_range = None
         return fw.forward_ffn_layer(layer_idx, h, add_residual=True).view(B, S, H)

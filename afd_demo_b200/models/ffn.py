@@ -72,10 +72,14 @@ class FFNWorker:
 
     def forward_ffn_layer(self, layer_idx: int, hidden_states: torch.Tensor,
                           add_residual: bool = True, sink=None, out: Optional[torch.Tensor] = None,
-                          mb_idx: int = 0, wait=None) -> torch.Tensor:
+                          mb_idx: int = 0, wait=None, return_timing: bool = False):
         """h [T, H] (= attn_out + residual) -> h + moe(norm(h)) [T, H], or only
         the local experts' partial sum when `add_residual` is False. `wait`
-        (an ``ops.FlagWait``): h arrives from peers; the first kernel waits."""
+        (an ``ops.FlagWait``): h arrives from peers; the first kernel waits.
+        `return_timing` (the reference's flag, src/model/ffn_worker.py:201-225)
+        returns (output, ``FFNStageTiming``) through the layer view."""
+        if return_timing:
+            return self.layers[layer_idx](hidden_states, return_timing=True)
         cfg = self.cfg
         lw = self.w.layers[layer_idx]
         H = cfg.hidden_size

@@ -206,7 +206,7 @@ class PipelineEngine:
                     recv(l - 1, m)
                     if ta:
                         ta.mark_start(EventType.ATTN_COMPUTE, l, m)
-                    h = attn.forward_attention_layer(l, xs[m], s.batch_offset, s.q_len,
+                    h = attn.attention_block(l, xs[m], s.batch_offset, s.q_len,
                                                      start_pos=start, sink=tr.a2f_sink(l, m),
                                                      wait=waits.pop(m, None))
                     if ta:
@@ -224,7 +224,7 @@ class PipelineEngine:
         for s in slots:
             with _on(st_attn(s.idx)):
                 recv(L - 1, s.idx)
-                logits.append(attn.forward_lm_head(xs[s.idx], s.q_len, last_only=last_only,
+                logits.append(attn.lm_head_block(xs[s.idx], s.q_len, last_only=last_only,
                                                    wait=waits.pop(s.idx, None)))
         with _on(s_attn):
             if mb_streams is not None:

@@ -121,21 +121,21 @@ class PipelineTiming:
     total_moe_experts_ms: float = 0.0
     total_moe_shared_or_dense_ms: float = 0.0
 
-    def add_event(self, ev: TimingEvent) -> None:
-        self.events.append(ev)
-        t = ev.event_type
+    def add_event(self, event: TimingEvent) -> None:
+        self.events.append(event)
+        t = event.event_type
         if t in (EventType.ATTN_COMPUTE.value, EventType.FFN_COMPUTE.value):
-            self.total_compute_ms += ev.duration_ms
+            self.total_compute_ms += event.duration_ms
         elif t == EventType.MOE_ROUTER.value:
-            self.total_moe_router_ms += ev.duration_ms
+            self.total_moe_router_ms += event.duration_ms
         elif t == EventType.MOE_EXPERTS.value:
-            self.total_moe_experts_ms += ev.duration_ms
+            self.total_moe_experts_ms += event.duration_ms
         elif t == EventType.MOE_SHARED_OR_DENSE.value:
-            self.total_moe_shared_or_dense_ms += ev.duration_ms
+            self.total_moe_shared_or_dense_ms += event.duration_ms
         elif t == EventType.RECV_WAIT.value:
-            self.total_recv_wait_ms += ev.duration_ms
+            self.total_recv_wait_ms += event.duration_ms
         elif t == EventType.SEND_TRANSFER.value:
-            self.total_send_wait_ms += ev.duration_ms
+            self.total_send_wait_ms += event.duration_ms
 
     @property
     def compute_ratio(self) -> float:
@@ -276,8 +276,8 @@ class TimingTracker:
                               tensor_bytes, completion_source)
 
     @staticmethod
-    def tensor_nbytes(t: Optional[torch.Tensor]) -> Optional[int]:
-        return None if t is None else int(t.numel() * t.element_size())
+    def tensor_nbytes(tensor: Optional[torch.Tensor]) -> Optional[int]:
+        return None if tensor is None else int(tensor.numel() * tensor.element_size())
 
     def record_event(self, event_type: EventType, layer_idx: int, mb_idx: int,
                      start_time: float, end_time: float, tensor_bytes: Optional[int] = None,

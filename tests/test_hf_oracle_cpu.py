@@ -135,7 +135,7 @@ def test_forward_prefill_and_decode_shapes_match_hf(models):
 def _head(model, h):
     aw = model.attention_worker
     B, S, H = h.shape
-    return aw.forward_lm_head([h.reshape(B * S, H)], S, last_only=False).view(B, S, -1)
+    return aw.lm_head_block([h.reshape(B * S, H)], S, last_only=False).view(B, S, -1)
 
 
 def test_per_layer_entry_points_match_hf(models):
@@ -185,7 +185,7 @@ def test_layer_views_match_hf_and_fused_path(models):
     ours.reset_kv_cache()
     attn, res = aw.layers[0](x)
     ours.reset_kv_cache()
-    h = aw.forward_attention_layer(0, [x.reshape(B * S, -1)], 0, S, start_pos=0)
+    h = aw.attention_block(0, [x.reshape(B * S, -1)], 0, S, start_pos=0)
     torch.testing.assert_close((attn + res).reshape(B * S, -1), h, rtol=1e-5, atol=1e-5)
     ours.reset_kv_cache()
     attn2, res2, cache = aw.layers[0](x, use_cache=True)

@@ -51,3 +51,42 @@ def test_workers_from_a_preset():
     assert fw.expert_range == range(cfg.num_experts)
     again = FFNWorker.from_pretrained("tiny", "cpu", torch.float32, seed=3)
     assert torch.equal(fw.w.layers[0].w_gate_up, again.w.layers[0].w_gate_up)
+
+
+def test_reference_per_layer_calls():
+    """The reference's worker calls: forward_attention_layer(l, h [B, S, H])
+    -> (attn_output, residual), forward_lm_head(h) -> logits [B, S, V],
+    get_position_embeddings(h, position_ids), forward_ffn_layer(...,
+    return_timing=True) -> (output, FFNStageTiming)."""
+    from afd_demo_b200.models.ffn import FFNStageTiming
+
+    cfg = tiny_qwen3_moe()
+    aw = AttentionWorker.from_pretrained("tiny", "cpu", torch.float32, max_batch=2, max_seq=16)
+    fw = FFNWorker.from_pretrained("tiny", "cpu", torch.float32)
+    B, S, H = 2, 5, cfg.hidden_size
+    h = torch.randn(B, S, H, generator=torch.Generator().manual_seed(1))
+
+    o, res = aw.forward_attention_layer(0, h)
+    o2, res2 = aw.layers[0](h)
+    assert o.shape == (B, S, H) and torch.equal(res, h)
+    torch.testing.assert_close(o, o2)
+    o3, _, cache = aw.forward_attention_layer(0, h, use_cache=True)
+    torch.testing.assert_close(o3, o)
+    assert cache is aw.cache
+
+    logits = aw.forward_lm_head(h)
+    assert logits.shape == (B, S, cfg.vocab_size)
+    torch.testing.assert_close(
+        logits, aw.lm_head_block([h.reshape(B * S, H)], S, last_only=False).view(B, S, -1))
+
+    pos = torch.arange(S).unsqueeze(0).expand(B, S)
+    cos, sin = aw.get_position_embeddings(h, pos)
+    assert cos.shape == (B, S, cfg.head_dim)
+    cos1, sin1 = aw.get_position_embeddings(pos)
+    assert torch.equal(cos, cos1) and torch.equal(sin, sin1)
+
+    x = (h + o).reshape(B * S, H)
+    plain = fw.forward_ffn_layer(0, x.clone())
+    out, st = fw.forward_ffn_layer(0, x.clone(), return_timing=True)
+    assert isinstance(st, FFNStageTiming) and st.router_s >= 0 and st.experts_s >= 0
+    torch.testing.assert_close(out, plain)
