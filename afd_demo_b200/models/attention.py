@@ -49,6 +49,24 @@ class AttentionWorker:
         # (padding masks), set by the model around one forward; None = causal only
         self.key_range = None
 
+    # the reference's attribute names (src/model/attention_worker.py:158-245);
+    # one GPU holds every layer, so the role's device list is this device
+    @property
+    def config(self) -> ModelConfig:
+        return self.cfg
+
+    @property
+    def hidden_size(self) -> int:
+        return self.cfg.hidden_size
+
+    @property
+    def attention_layers(self) -> list:
+        return self.layers
+
+    @property
+    def role_devices(self) -> list:
+        return [self.device]
+
     @classmethod
     def from_pretrained(cls, model_name: str, device, dtype=torch.bfloat16,
                         max_batch: int = 4, max_seq: int = 2048,

@@ -44,6 +44,24 @@ class FFNWorker:
         self.tracker = None  # optional TimingTracker for router / experts spans
         self.layers = [FFNLayer(self, l) for l in range(self.num_layers)]
 
+    # the reference's attribute names (src/model/ffn_worker.py:125-189); one
+    # GPU holds every layer, so the role's device list is this device
+    @property
+    def config(self) -> ModelConfig:
+        return self.cfg
+
+    @property
+    def hidden_size(self) -> int:
+        return self.cfg.hidden_size
+
+    @property
+    def ffn_layers(self) -> list:
+        return self.layers
+
+    @property
+    def role_devices(self) -> list:
+        return [self.device]
+
     @classmethod
     def from_pretrained(cls, model_name: str, device, dtype=torch.bfloat16,
                         expert_range: Optional[range] = None,

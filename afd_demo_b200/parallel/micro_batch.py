@@ -49,7 +49,12 @@ class MicroBatch:
     hidden_states: Optional[torch.Tensor] = None
     state: MicroBatchState = MicroBatchState.WAITING
     current_layer: int = 0
-    batch_offset: int = 0
+    # the reference's remaining fields, in its order: position embeddings
+    # computed once per micro-batch, and host timestamps for profiling
+    position_embeddings: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+    start_time: Optional[float] = None
+    end_time: Optional[float] = None
+    batch_offset: int = 0  # first sequence of this micro-batch in the batch
 
     def advance_layer(self) -> None:
         self.current_layer += 1

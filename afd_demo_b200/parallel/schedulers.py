@@ -108,6 +108,7 @@ class SimplePipelineScheduler:
     def __init__(self, model, num_micro_batches: int = 2, enable_timing: bool = False,
                  timing_mode: str = "cuda_events"):
         self.model = model
+        self.ctx = model.ctx
         self.num_micro_batches = num_micro_batches
         self.enable_timing = enable_timing
         self.timing_mode = timing_mode
@@ -138,6 +139,7 @@ class AsyncPipelineScheduler:
                  enable_timing: bool = False, timing_mode: str = "device",
                  comm_timing_mode: str = "enqueue", crosslayer: bool = True):
         self.model = model
+        self.ctx = model.ctx
         self.num_micro_batches = num_micro_batches
         self.use_cuda_streams = use_cuda_streams
         self.enable_timing = enable_timing
@@ -183,6 +185,7 @@ class DecodeDBOScheduler:
                  timing_mode: str = "device", comm_timing_mode: str = "enqueue",
                  use_crosslayer: bool = False):
         self.model = model
+        self.ctx = model.ctx
         self.num_micro_batches = num_micro_batches
         self.enable_timing = enable_timing
         self.timing_mode = timing_mode

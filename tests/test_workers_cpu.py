@@ -90,3 +90,21 @@ def test_reference_per_layer_calls():
     out, st = fw.forward_ffn_layer(0, x.clone(), return_timing=True)
     assert isinstance(st, FFNStageTiming) and st.router_s >= 0 and st.experts_s >= 0
     torch.testing.assert_close(out, plain)
+
+
+def test_reference_attribute_names():
+    from afd_demo_b200.parallel.micro_batch import MicroBatch, MicroBatchManager
+
+    cfg = tiny_qwen3_moe()
+    aw = AttentionWorker.from_pretrained("tiny", "cpu", torch.float32, max_seq=16)
+    fw = FFNWorker.from_pretrained("tiny", "cpu", torch.float32)
+    for w, layers in ((aw, aw.attention_layers), (fw, fw.ffn_layers)):
+        assert w.config is w.cfg and w.hidden_size == cfg.hidden_size
+        assert layers is w.layers and w.role_devices == [torch.device("cpu")]
+    # the reference's MicroBatch field order (positional construction lines up)
+    ids = torch.zeros(2, 3, dtype=torch.long)
+    mb = MicroBatch(0, ids, None, None, None)
+    assert (mb.position_embeddings, mb.start_time, mb.end_time, mb.batch_offset) == \
+        (None, None, None, 0)
+    split = MicroBatchManager(2).split_batch(torch.zeros(5, 3, dtype=torch.long))
+    assert [m.batch_offset for m in split] == [0, 3]
