@@ -89,6 +89,20 @@ class AttentionWorker:
              else load_attention_weights(model_name, cfg, device, dtype))
         return cls(cfg, w, device, dtype, max_batch, max_seq)
 
+    @classmethod
+    def from_hf_model(cls, model, device, dtype=torch.bfloat16, max_batch: int = 4,
+                      max_seq: int = 2048) -> "AttentionWorker":
+        """The counterpart of the reference's ``AttentionWorker(model, device,
+        dtype)`` (src/model/attention_worker.py:170-237), which takes a loaded
+        HF ``Qwen3MoeForCausalLM``: its config and attention-side tensors are
+        copied to `device` (per-expert or fused expert layouts alike)."""
+        from ..config import ModelConfig
+        from .weights import load_attention_weights
+
+        cfg = ModelConfig.from_dict(model.config.to_dict())
+        w = load_attention_weights(model.state_dict(), cfg, device, dtype)
+        return cls(cfg, w, device, dtype, max_batch, max_seq)
+
     # ------------------------------------------------------------------
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         """[B, S] ids -> [B*S, H] hidden states."""

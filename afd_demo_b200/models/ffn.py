@@ -84,6 +84,21 @@ class FFNWorker:
              else load_ffn_weights(model_name, cfg, expert_range, device, dtype))
         return cls(cfg, w, device, dtype)
 
+    @classmethod
+    def from_hf_model(cls, model, device, dtype=torch.bfloat16,
+                      expert_range: Optional[range] = None) -> "FFNWorker":
+        """The counterpart of the reference's ``FFNWorker(model, device, dtype)``
+        (src/model/ffn_worker.py:135-189), which takes a loaded HF
+        ``Qwen3MoeForCausalLM``: its config and FFN-side tensors (experts in
+        `expert_range`, default all) are copied to `device`; experts may be
+        stored per expert or fused (transformers 5)."""
+        from ..config import ModelConfig
+        from .weights import load_ffn_weights
+
+        cfg = ModelConfig.from_dict(model.config.to_dict())
+        w = load_ffn_weights(model.state_dict(), cfg, expert_range, device, dtype)
+        return cls(cfg, w, device, dtype)
+
     def _mark(self, start: bool, et: EventType, l: int, mb: int):
         if self.tracker is not None:
             (self.tracker.mark_start if start else self.tracker.mark_end)(et, l, mb)

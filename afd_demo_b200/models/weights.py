@@ -39,6 +39,7 @@ from __future__ import annotations
 import hashlib
 import json
 import os
+import re
 from dataclasses import dataclass, field
 from typing import Dict, Iterable, List, Optional
 
@@ -300,9 +301,57 @@ class _ShardReader:
         return key in self.weight_map
 
 
-def load_attention_weights(path: str, cfg: ModelConfig, device="cpu",
+class _StateDictReader:
+    """Reads tensors from an in-memory state dict under the checkpoint's key
+    names. Experts may be stored per expert (``mlp.experts.{e}.gate_proj.weight``
+    and so on: transformers 4, and every saved checkpoint) or fused
+    (``mlp.experts.gate_up_proj`` [E, 2I, H], gate rows first, and
+    ``mlp.experts.down_proj`` [E, H, I]: a transformers 5 model in memory);
+    fused ones are sliced per expert."""
+
+    _PER_EXPERT = re.compile(r"^(.*\.mlp\.experts\.)(\d+)\.(gate_proj|up_proj|down_proj)\.weight$")
+
+    def __init__(self, state_dict):
+        self.sd = state_dict
+
+    def get(self, key: str) -> torch.Tensor:
+        t = self.sd.get(key)
+        if t is not None:
+            return t
+        m = self._PER_EXPERT.match(key)
+        if m is not None:
+            base, e, proj = m.group(1), int(m.group(2)), m.group(3)
+            if proj == "down_proj":
+                fused = self.sd.get(base + "down_proj")
+                if fused is not None:
+                    return fused[e]
+            else:
+                fused = self.sd.get(base + "gate_up_proj")
+                if fused is not None:
+                    half = fused.shape[1] // 2
+                    return fused[e, :half] if proj == "gate_proj" else fused[e, half:]
+        raise KeyError(key)
+
+    def __contains__(self, key: str) -> bool:
+        try:
+            self.get(key)
+        except KeyError:
+            return False
+        return True
+
+
+def _reader(source):
+    """A checkpoint directory, or a state dict (see ``_StateDictReader``)."""
+    if isinstance(source, (str, os.PathLike)):
+        return _ShardReader(os.fspath(source))
+    return _StateDictReader(source)
+
+
+def load_attention_weights(path, cfg: ModelConfig, device="cpu",
                            dtype=torch.bfloat16) -> AttentionWeights:
-    r = _ShardReader(path)
+    """The attention-side tensors of `path`: a checkpoint directory or a
+    state dict with the checkpoint's key names."""
+    r = _reader(path)
     cv = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
     lm_key = "lm_head.weight" if "lm_head.weight" in r else "model.embed_tokens.weight"
     aw = AttentionWeights(embed=cv(r.get("model.embed_tokens.weight")),
@@ -322,9 +371,11 @@ def load_attention_weights(path: str, cfg: ModelConfig, device="cpu",
     return aw
 
 
-def load_ffn_weights(path: str, cfg: ModelConfig, expert_range: Optional[range] = None,
+def load_ffn_weights(path, cfg: ModelConfig, expert_range: Optional[range] = None,
                      device="cpu", dtype=torch.bfloat16) -> FFNWeights:
-    r = _ShardReader(path)
+    """The FFN-side tensors of `path` (experts in `expert_range`): a
+    checkpoint directory or a state dict with the checkpoint's key names."""
+    r = _reader(path)
     cv = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
     if expert_range is None:
         expert_range = range(cfg.num_experts)

@@ -108,3 +108,49 @@ def test_reference_attribute_names():
         (None, None, None, 0)
     split = MicroBatchManager(2).split_batch(torch.zeros(5, 3, dtype=torch.long))
     assert [m.batch_offset for m in split] == [0, 3]
+
+
+def test_workers_from_an_hf_model(tmp_path):
+    """The reference builds its workers from a loaded HF model. Loaded by
+    transformers (experts fused in memory under transformers 5), the workers
+    built with ``from_hf_model`` hold the same tensors as those read from the
+    checkpoint directory."""
+    import transformers
+
+    cfg = tiny_qwen3_moe()
+    save_checkpoint(str(tmp_path), cfg, random_attention_weights(cfg, 0, "cpu", torch.float32),
+                    random_ffn_weights(cfg, None, 0, "cpu", torch.float32))
+    hf = transformers.AutoModelForCausalLM.from_pretrained(str(tmp_path), dtype=torch.float32)
+
+    aw = AttentionWorker.from_hf_model(hf, "cpu", torch.float32, max_seq=16)
+    aw_ref = AttentionWorker.from_pretrained(str(tmp_path), "cpu", torch.float32, max_seq=16)
+    assert aw.cfg.num_hidden_layers == cfg.num_hidden_layers
+    torch.testing.assert_close(aw.w.embed, aw_ref.w.embed, rtol=0, atol=0)
+    torch.testing.assert_close(aw.w.layers[1].w_qkv, aw_ref.w.layers[1].w_qkv, rtol=0, atol=0)
+
+    fw = FFNWorker.from_hf_model(hf, "cpu", torch.float32, expert_range=range(1, 3))
+    fw_ref = FFNWorker.from_pretrained(str(tmp_path), "cpu", torch.float32,
+                                       expert_range=range(1, 3))
+    for l in range(cfg.num_hidden_layers):
+        for name in ("post_norm", "w_router", "w_gate_up", "w_down"):
+            torch.testing.assert_close(getattr(fw.w.layers[l], name),
+                                       getattr(fw_ref.w.layers[l], name), rtol=0, atol=0)
+
+
+def test_state_dict_reader_expert_layouts():
+    """Per-expert keys are read as they are; fused transformers-5 expert
+    tensors are sliced per expert (gate rows first); other keys are absent."""
+    from afd_demo_b200.models.weights import _StateDictReader
+
+    E, I, H = 3, 4, 5
+    gu = torch.randn(E, 2 * I, H)
+    dn = torch.randn(E, H, I)
+    p = "model.layers.0.mlp.experts."
+    fused = _StateDictReader({p + "gate_up_proj": gu, p + "down_proj": dn})
+    assert torch.equal(fused.get(p + "2.gate_proj.weight"), gu[2, :I])
+    assert torch.equal(fused.get(p + "2.up_proj.weight"), gu[2, I:])
+    assert torch.equal(fused.get(p + "1.down_proj.weight"), dn[1])
+    assert p + "0.gate_proj.weight" in fused and "lm_head.weight" not in fused
+    per = _StateDictReader({p + "0.up_proj.weight": gu[0, I:]})
+    assert torch.equal(per.get(p + "0.up_proj.weight"), gu[0, I:])
+    assert p + "0.gate_proj.weight" not in per
