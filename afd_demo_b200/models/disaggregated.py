@@ -73,6 +73,7 @@ class DisaggregatedQwenModel:
         self.attention_worker: Optional[AttentionWorker] = None
         self.ffn_worker: Optional[FFNWorker] = None
         self.transport: Optional[Transport] = None
+        self.communicator = None  # the reference's AFDCommunicator (setup_communicator)
         self.engine = PipelineEngine(self)
         self.attn_stream = None
         self.ffn_stream = None
@@ -173,8 +174,18 @@ class DisaggregatedQwenModel:
 
     def setup_communicator(self, max_seq_len: int = 2048, max_batch_size: int = 4,
                            num_buffers: int = 2) -> None:
-        """Reference-compatible name for transport set-up."""
+        """Transport set-up under the reference's name
+        (src/model/disaggregated.py:117-143). With the roles on separate ranks
+        it also builds ``self.communicator``: the reference's buffered
+        point-to-point ``AFDCommunicator`` to the other role's first rank, for
+        code that sends through it directly (this framework's forwards use the
+        transport). Every rank calls it."""
         self.setup_transport("auto", max_batch_size, max_seq_len, num_buffers)
+        if not self.ctx.is_colocated and self.ctx.world_size > 1:
+            from ..parallel.communicator import AFDCommunicator
+
+            self.communicator = AFDCommunicator(self.hidden_size, max_seq_len, max_batch_size,
+                                                num_buffers, self.dtype)
 
     @classmethod
     def from_pretrained(cls, model_name: str, device=None, dtype=torch.bfloat16,

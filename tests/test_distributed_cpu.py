@@ -69,6 +69,16 @@ def _worker(rank, world, port, ckpt, modes, out_dir, n_attn=None):
                                           attention_mask=_mask())
     # every rank gets the same agreed figures
     res["agreement"] = m.transport_agreement(_ids())
+    if world == 2:
+        # the reference's model.communicator, between the two roles
+        m.setup_communicator(max_seq_len=8, max_batch_size=2)
+        if ctx.is_attention_node:
+            m.communicator.send_sync(torch.full((2, 8, m.hidden_size), 3.0), tag=5)
+        else:
+            got = m.communicator.recv_sync((2, 8), tag=5)
+            assert got.shape == (2, 8, m.hidden_size) and bool((got == 3.0).all())
+        res["generate_after_setup"] = m.generate(_ids(), max_new_tokens=5, do_sample=False,
+                                                 use_decode_dbo=False)
     if ctx.is_attention_node:
         torch.save(res, os.path.join(out_dir, f"attn{ctx.attn_index}.pt"))
     ctx.barrier()
@@ -108,6 +118,9 @@ def test_multi_rank_matches_single_process(ckpt, world, n_attn):
     got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))["padded_prefill"]
                      for a in range(n_attn)])
     torch.testing.assert_close(got, want_logits, rtol=1e-4, atol=1e-4)
+    if world == 2:  # the transport rebuilt by setup_communicator still generates the same
+        got = torch.load(os.path.join(out, "attn0.pt"))["generate_after_setup"]
+        assert torch.equal(got, want)
     # the transport self-check: the same transport twice is the same computation
     for a in range(n_attn):
         agreement = torch.load(os.path.join(out, f"attn{a}.pt"))["agreement"]
