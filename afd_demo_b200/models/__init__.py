@@ -1,3 +1,8 @@
+"""Model layer: the attention and FFN workers (one role each), the preallocated
+KV cache, checkpoint reading and random initialisation, and
+``DisaggregatedQwenModel``, which holds this process's roles and runs forwards
+and generation (reference: src/model/)."""
+
 from .attention import AttentionWorker
 from .disaggregated import DisaggregatedQwenModel
 from .ffn import FFNWorker

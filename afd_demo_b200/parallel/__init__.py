@@ -1,3 +1,9 @@
+"""Distribution and scheduling: the distributed context (roles per rank), the
+pipeline engine and the reference's scheduler classes over it, micro-batch
+planning, the A2F/F2A transports (fused peer memory, NCCL, local), the
+reference's buffered communicator, P2P warm-up, and host-side failure
+detection and fault injection (reference: src/distributed/, src/pipeline/)."""
+
 from .dist import (DistributedConfig, DistributedContext, config_from_env,
                    get_distributed_context, init_distributed)
 from .engine import PipelineEngine

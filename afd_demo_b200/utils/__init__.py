@@ -1,3 +1,7 @@
+"""Helpers with the reference's names: device selection, timers and the
+profiler, sampling, the timing tracker and its JSON schema, and output
+validation (reference: src/utils/)."""
+
 from . import device
 from .profiler import CUDATimer, Timer, profile_function
 from .sampling import StoppingCriteria, repetition_penalty, sample_next_token, top_k_filtering, top_p_filtering
