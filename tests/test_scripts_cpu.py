@@ -258,3 +258,16 @@ def test_run_node_reference_form_two_ranks(tmp_path):
             if p.poll() is None:
                 p.kill()
     assert [p.returncode for p in procs] == [0, 0], "\n".join(o[-2000:] for o in outs)
+
+
+@pytest.mark.parametrize("module", ["kernel_probe", "bench_kernels", "trace_decode", "decode_cells",
+                                    "bench_comm_transfer", "capture_serial_split", "gen_experiment_report",
+                                    "audit_experiment_baselines", "visualize_dbo_pipeline",
+                                    "plot_all_pipelines"])
+def test_script_imports_and_parses_arguments(module):
+    """Every script module imports without a GPU and answers --help (the GPU
+    tools run only on a GPU box; an import error there would show up here)."""
+    p = subprocess.run([sys.executable, "-m", f"afd_demo_b200.scripts.{module}", "--help"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stderr[-2000:]
+    assert "usage" in p.stdout.lower()
