@@ -78,7 +78,8 @@ class ModelConfig:
         d = dataclasses.asdict(self)
         d.update(
             {
-                "architectures": ["Qwen3MoeForCausalLM"],
+                "architectures": ["Qwen3ForCausalLM" if self.model_type == "qwen3"
+                                  else "Qwen3MoeForCausalLM"],
                 "hidden_act": "silu",
                 "attention_bias": False,
                 "attention_dropout": 0.0,
@@ -99,9 +100,10 @@ class ModelConfig:
     def from_dict(cls, d: Dict) -> "ModelConfig":
         names = {f.name for f in dataclasses.fields(cls)}
         kw = {k: v for k, v in d.items() if k in names}
-        # transformers 5 writes the expert count as num_local_experts
-        if "num_experts" not in d and "num_local_experts" in d:
-            kw["num_experts"] = d["num_local_experts"]
+        # transformers 5 writes the expert count as num_local_experts; a dense
+        # model's config (model_type "qwen3") has no expert count at all
+        if "num_experts" not in d:
+            kw["num_experts"] = d.get("num_local_experts", 0)
         if "rope_theta" not in d and isinstance(d.get("rope_parameters"), dict):
             kw["rope_theta"] = d["rope_parameters"].get("rope_theta", cls.rope_theta)
         if "head_dim" not in d and "hidden_size" in d and "num_attention_heads" in d:

@@ -126,8 +126,10 @@ class DisaggregatedQwenModel:
         if ctx.is_ffn_node:
             er = range(cfg.num_experts) if ctx.is_colocated else \
                 self.topology.experts_of(ctx.ffn_index, cfg.num_experts)
-            fw = (random_ffn_weights(cfg, er, seed, dev, dt) if random_init
-                  else load_ffn_weights(model_name, cfg, er, dev, dt))
+            # dense layers: this FFN rank's slice of the intermediate dimension
+            dp = (0, 1) if ctx.is_colocated else (ctx.ffn_index, self.topology.n_ffn)
+            fw = (random_ffn_weights(cfg, er, seed, dev, dt, dense_part=dp) if random_init
+                  else load_ffn_weights(model_name, cfg, er, dev, dt, dense_part=dp))
             self.ffn_worker = FFNWorker(cfg, fw, dev, dt)
         logger.info(f"weights ready for role {ctx.role} (experts "
                     f"{self.ffn_worker.expert_range if self.ffn_worker else '-'})")
@@ -136,7 +138,8 @@ class DisaggregatedQwenModel:
                         max_seq_len: int = 2048, num_micro_batches: int = 2,
                         crosslayer: bool = True, timeout_ms: float = 10000.0) -> None:
         """Streams and the A2F/F2A transport. ``auto`` = local when
-        co-located, fused peer memory on CUDA, NCCL otherwise (gloo on CPU)."""
+        co-located, fused peer memory on CUDA for MoE models, NCCL otherwise
+        (gloo on CPU; also on CUDA when some layer is a dense MLP)."""
         ctx = self.ctx
         self.max_batch_size = max_batch_size
         self.max_seq_len = max_seq_len
@@ -144,10 +147,16 @@ class DisaggregatedQwenModel:
         if self.device.type == "cuda":
             self.attn_stream = torch.cuda.Stream(self.device)
             self.ffn_stream = torch.cuda.Stream(self.device) if ctx.is_colocated else self.attn_stream
+        # the fused F2A store is the MoE combine's epilogue: models with dense
+        # MLP layers hand off over NCCL
+        dense = any(not self.config.is_sparse_layer(l) for l in range(self.num_layers))
         if ctx.is_colocated:
             comm_impl = "local"
         elif comm_impl == "auto":
-            comm_impl = "fused" if self.device.type == "cuda" else "nccl"
+            comm_impl = "fused" if self.device.type == "cuda" and not dense else "nccl"
+        elif comm_impl == "fused" and dense:
+            raise ValueError("the fused transport covers MoE layers only; this model has dense "
+                             "MLP layers: use comm_impl 'nccl' (or 'auto')")
         self.comm_impl = comm_impl
         if comm_impl == "local":
             self.transport = LocalTransport(self.attn_stream, self.ffn_stream)

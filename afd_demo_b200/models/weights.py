@@ -8,7 +8,9 @@ only the tensors it owns, straight from the safetensors shards:
 * attention ranks: embedding, per-layer input norm, q/k/v/o projections,
   q/k norms, final norm, LM head;
 * FFN ranks: per-layer post-attention norm, router, and the experts in their
-  expert-parallel slice.
+  expert-parallel slice; a dense MLP layer (``mlp_only_layers``, or every
+  layer of a dense Qwen3 model) is split over the FFN ranks along its
+  intermediate dimension (``dense_slice``).
 
 On-disk layout (HF Qwen3-MoE, per-expert keys)::
 
@@ -41,7 +43,7 @@ import json
 import os
 import re
 from dataclasses import dataclass, field
-from typing import Dict, Iterable, List, Optional
+from typing import Dict, Iterable, List, Optional, Tuple
 
 import torch
 
@@ -123,12 +125,13 @@ def random_attention_weights(cfg: ModelConfig, seed: int = 0, device="cpu",
 
 
 def random_ffn_weights(cfg: ModelConfig, expert_range: Optional[range] = None, seed: int = 0,
-                       device="cpu", dtype=torch.bfloat16) -> FFNWeights:
+                       device="cpu", dtype=torch.bfloat16,
+                       dense_part: Tuple[int, int] = (0, 1)) -> FFNWeights:
     if expert_range is None:
         expert_range = range(cfg.num_experts)
     fw = FFNWeights(expert_range=expert_range)
     for l in range(cfg.num_hidden_layers):
-        fw.layers.append(_layer_only_ffn(cfg, l, seed, dtype, device, expert_range))
+        fw.layers.append(_layer_only_ffn(cfg, l, seed, dtype, device, expert_range, dense_part))
     return fw
 
 
@@ -244,12 +247,34 @@ def _layer_only_attention(cfg: ModelConfig, l: int, seed: int, dtype,
     )
 
 
+def dense_slice(gate_up: torch.Tensor, down: torch.Tensor,
+                part: Tuple[int, int] = (0, 1)) -> Tuple[torch.Tensor, torch.Tensor]:
+    """FFN rank i of n (`part` = (i, n)) keeps rows [i*DI/n, (i+1)*DI/n) of a
+    dense MLP's gate and of its up projection (`gate_up` is [2*DI, H], gate
+    rows first) and the same columns of `down` [H, DI]. Its output is then
+    that slice's share of the down projection, and the attention side's sum
+    of the FFN ranks' outputs (the same sum that adds up the experts'
+    partials) is the whole MLP."""
+    i, n = part
+    if n == 1:
+        return gate_up, down
+    DI = down.shape[1]
+    if DI % n:
+        raise ValueError(f"dense intermediate size {DI} does not split over {n} FFN ranks")
+    w = DI // n
+    lo, hi = i * w, (i + 1) * w
+    return (torch.cat([gate_up[lo:hi], gate_up[DI + lo:DI + hi]]).contiguous(),
+            down[:, lo:hi].contiguous())
+
+
 def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype, device="cpu",
-                    expert_range: Optional[range] = None) -> FFNLayerWeights:
+                    expert_range: Optional[range] = None,
+                    dense_part: Tuple[int, int] = (0, 1)) -> FFNLayerWeights:
     """One layer's FFN weights. The experts' gate/up and down projections are
     one seeded draw each over all experts of the layer, of which this rank
     keeps `expert_range`: every expert-parallel split therefore holds the
-    same values as one GPU holding all experts."""
+    same values as one GPU holding all experts. A dense layer is drawn whole
+    and this rank keeps its `dense_part` slice (``dense_slice``)."""
     std = cfg.initializer_range
     H, I, E = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts
     er = range(E) if expert_range is None else expert_range
@@ -265,8 +290,9 @@ def _layer_only_ffn(cfg: ModelConfig, l: int, seed: int, dtype, device="cpu",
         lw.w_gate_up, lw.w_down, lw.expert_start = gu, dn, er.start
     else:
         DI = cfg.intermediate_size
-        lw.w_dense_gate_up = _randn((2 * DI, H), p + "dense.gate_up", seed, std, device, dtype)
-        lw.w_dense_down = _randn((H, DI), p + "dense.down", seed, std, device, dtype)
+        lw.w_dense_gate_up, lw.w_dense_down = dense_slice(
+            _randn((2 * DI, H), p + "dense.gate_up", seed, std, device, dtype),
+            _randn((H, DI), p + "dense.down", seed, std, device, dtype), dense_part)
     return lw
 
 
@@ -372,9 +398,11 @@ def load_attention_weights(path, cfg: ModelConfig, device="cpu",
 
 
 def load_ffn_weights(path, cfg: ModelConfig, expert_range: Optional[range] = None,
-                     device="cpu", dtype=torch.bfloat16) -> FFNWeights:
-    """The FFN-side tensors of `path` (experts in `expert_range`): a
-    checkpoint directory or a state dict with the checkpoint's key names."""
+                     device="cpu", dtype=torch.bfloat16,
+                     dense_part: Tuple[int, int] = (0, 1)) -> FFNWeights:
+    """The FFN-side tensors of `path` (experts in `expert_range`, the
+    `dense_part` slice of dense layers): a checkpoint directory or a state
+    dict with the checkpoint's key names."""
     r = _reader(path)
     cv = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
     if expert_range is None:
@@ -396,9 +424,9 @@ def load_ffn_weights(path, cfg: ModelConfig, expert_range: Optional[range] = Non
                 dn[i] = cv(r.get(q + "down_proj.weight"))
             lw.w_gate_up, lw.w_down, lw.expert_start = gu, dn, expert_range.start
         else:
-            lw.w_dense_gate_up = cv(torch.cat([r.get(p + "mlp.gate_proj.weight"),
-                                               r.get(p + "mlp.up_proj.weight")]))
-            lw.w_dense_down = cv(r.get(p + "mlp.down_proj.weight"))
+            lw.w_dense_gate_up, lw.w_dense_down = dense_slice(
+                cv(torch.cat([r.get(p + "mlp.gate_proj.weight"), r.get(p + "mlp.up_proj.weight")])),
+                cv(r.get(p + "mlp.down_proj.weight")), dense_part)
         fw.layers.append(lw)
     return fw
 

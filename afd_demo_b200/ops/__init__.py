@@ -864,6 +864,9 @@ def dense_mlp(xn: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     T, H = xn.shape
     I2 = w_gate_up.shape[0]
     I = I2 // 2
+    if I % 128:
+        raise ValueError(f"dense MLP width {I} (this rank's slice) is not a multiple of 128, "
+                         "the SwiGLU GEMM's feature tile")
     act = torch.empty(T, I, device=xn.device, dtype=xn.dtype)
     bn = _block_n(T)
     units = ((T + bn - 1) // bn) * (I // 128)

@@ -140,3 +140,35 @@ def test_single_process_schedules_agree(ckpt):
     assert torch.equal(outs["serial"], outs["xl"])
     with pytest.raises(ValueError, match="no transport"):
         m.transport_agreement(_ids())
+
+
+def _dense_ckpt(kind: str) -> str:
+    d = tempfile.mkdtemp(prefix=f"afd_{kind}_")
+    cfg = tiny_qwen3_moe()
+    if kind == "mixed":
+        cfg.mlp_only_layers = [1]  # layer 1 is a dense MLP, layer 0 MoE
+    else:  # a dense Qwen3 model: no experts at all
+        cfg.num_experts, cfg.model_type = 0, "qwen3"
+    save_checkpoint(d, cfg, random_attention_weights(cfg, 0, "cpu", torch.float32),
+                    random_ffn_weights(cfg, None, 0, "cpu", torch.float32))
+    return d
+
+
+@pytest.mark.parametrize("kind", ["mixed", "dense"])
+@pytest.mark.parametrize("world,n_attn", [(3, 1), (4, 2)], ids=["1A2F", "2A2F"])
+def test_dense_layers_split_over_ffn_ranks(kind, world, n_attn):
+    """Dense MLP layers on several FFN ranks: each rank holds a slice of the
+    intermediate dimension and the attention side's sum of the partials is the
+    whole MLP, so tokens equal the single-process model's."""
+    d = _dense_ckpt(kind)
+    want, want_logits = _reference(d)
+    out = tempfile.mkdtemp(prefix="afd_out_")
+    mp.start_processes(_worker, args=(world, _free_port(), d, MODES, out, n_attn),
+                       nprocs=world, join=True, start_method="spawn")
+    for name in MODES:
+        got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))[name]
+                         for a in range(n_attn)])
+        assert torch.equal(got, want), (kind, world, name)
+    got = torch.cat([torch.load(os.path.join(out, f"attn{a}.pt"))["padded_prefill"]
+                     for a in range(n_attn)])
+    torch.testing.assert_close(got, want_logits, rtol=1e-4, atol=1e-4)

@@ -88,6 +88,33 @@ def test_dense_mlp_layers_match_hf(tmp_path):
     assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
 
 
+def test_dense_qwen3_checkpoint_matches_hf(tmp_path):
+    """A dense Qwen3 model (``Qwen3ForCausalLM``: no router, no expert count
+    in its config), saved by transformers, loads as a model whose every FFN
+    layer is a dense MLP; logits and greedy tokens match HF's own."""
+    hcfg = transformers.Qwen3Config(vocab_size=512, hidden_size=128, intermediate_size=256,
+                                    num_hidden_layers=2, num_attention_heads=4,
+                                    num_key_value_heads=2, head_dim=32,
+                                    max_position_embeddings=256, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    hf = transformers.Qwen3ForCausalLM(hcfg).float().eval()
+    hf.save_pretrained(str(tmp_path))
+    ours = DisaggregatedQwenModel.from_pretrained(str(tmp_path), device="cpu",
+                                                  dtype=torch.float32, max_seq_len=64,
+                                                  max_batch_size=2)
+    assert ours.config.num_experts == 0 and ours.config.model_type == "qwen3"
+    assert ours.ffn_worker.w.layers[0].w_router is None
+    ids = torch.randint(0, 512, (2, 12), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        ref = hf(ids).logits[:, -1].float()
+        want = hf.generate(ids, max_new_tokens=6, do_sample=False)
+    for mode, nmb in (("serial", 1), ("dbo", 2)):
+        out = ours.run_forward(ids, mode, nmb, reset_cache=True).float()
+        assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+    got = ours.generate(ids, max_new_tokens=6, do_sample=False, use_decode_dbo=False)
+    assert torch.equal(got, want)
+
+
 @pytest.mark.parametrize("side", ["right", "left"])
 def test_padding_mask_matches_hf(models, side):
     """Prefill with a padding mask (the reference's `--prefill-seq-len`
