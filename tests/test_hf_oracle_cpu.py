@@ -88,14 +88,17 @@ def test_dense_mlp_layers_match_hf(tmp_path):
     assert (out - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
 
 
-def test_dense_qwen3_checkpoint_matches_hf(tmp_path):
+@pytest.mark.parametrize("tied", [False, True])
+def test_dense_qwen3_checkpoint_matches_hf(tmp_path, tied):
     """A dense Qwen3 model (``Qwen3ForCausalLM``: no router, no expert count
     in its config), saved by transformers, loads as a model whose every FFN
-    layer is a dense MLP; logits and greedy tokens match HF's own."""
+    layer is a dense MLP; logits and greedy tokens match HF's own. With tied
+    embeddings the checkpoint has no ``lm_head.weight`` and the embedding is
+    the LM head."""
     hcfg = transformers.Qwen3Config(vocab_size=512, hidden_size=128, intermediate_size=256,
                                     num_hidden_layers=2, num_attention_heads=4,
                                     num_key_value_heads=2, head_dim=32,
-                                    max_position_embeddings=256, tie_word_embeddings=False)
+                                    max_position_embeddings=256, tie_word_embeddings=tied)
     torch.manual_seed(0)
     hf = transformers.Qwen3ForCausalLM(hcfg).float().eval()
     hf.save_pretrained(str(tmp_path))
