@@ -22,7 +22,7 @@ residual, so the attention side's sum over FFN ranks is the layer output.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -65,13 +65,15 @@ class FFNWorker:
     @classmethod
     def from_pretrained(cls, model_name: str, device, dtype=torch.bfloat16,
                         expert_range: Optional[range] = None,
-                        random_init: Optional[bool] = None, seed: int = 0) -> "FFNWorker":
+                        random_init: Optional[bool] = None, seed: int = 0,
+                        dense_part: Tuple[int, int] = (0, 1)) -> "FFNWorker":
         """Reference: ``FFNWorker.from_pretrained`` (src/model/ffn_worker.py:228-256),
         which loads the whole HF model on the CPU and keeps its MLP parts.
         Here only the checkpoint's FFN-side tensors (post-attention norms,
         routers, the experts in `expert_range` (default all) and dense MLPs) are read,
         straight to `device`; a preset name without a checkpoint directory
-        gets random weights (`seed`)."""
+        gets random weights (`seed`). `dense_part` = (i, n): this worker is FFN
+        rank i of n and keeps that slice of each dense MLP layer."""
         import os
 
         from ..config import resolve_model_config
@@ -80,13 +82,14 @@ class FFNWorker:
         cfg = resolve_model_config(model_name)
         if random_init is None:
             random_init = not os.path.isdir(model_name)
-        w = (random_ffn_weights(cfg, expert_range, seed, device, dtype) if random_init
-             else load_ffn_weights(model_name, cfg, expert_range, device, dtype))
+        w = (random_ffn_weights(cfg, expert_range, seed, device, dtype, dense_part) if random_init
+             else load_ffn_weights(model_name, cfg, expert_range, device, dtype, dense_part))
         return cls(cfg, w, device, dtype)
 
     @classmethod
     def from_hf_model(cls, model, device, dtype=torch.bfloat16,
-                      expert_range: Optional[range] = None) -> "FFNWorker":
+                      expert_range: Optional[range] = None,
+                      dense_part: Tuple[int, int] = (0, 1)) -> "FFNWorker":
         """The counterpart of the reference's ``FFNWorker(model, device, dtype)``
         (src/model/ffn_worker.py:135-189), which takes a loaded HF
         ``Qwen3MoeForCausalLM``: its config and FFN-side tensors (experts in
@@ -96,7 +99,7 @@ class FFNWorker:
         from .weights import load_ffn_weights
 
         cfg = ModelConfig.from_dict(model.config.to_dict())
-        w = load_ffn_weights(model.state_dict(), cfg, expert_range, device, dtype)
+        w = load_ffn_weights(model.state_dict(), cfg, expert_range, device, dtype, dense_part)
         return cls(cfg, w, device, dtype)
 
     def _mark(self, start: bool, et: EventType, l: int, mb: int):

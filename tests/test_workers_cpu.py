@@ -154,3 +154,24 @@ def test_state_dict_reader_expert_layouts():
     per = _StateDictReader({p + "0.up_proj.weight": gu[0, I:]})
     assert torch.equal(per.get(p + "0.up_proj.weight"), gu[0, I:])
     assert p + "0.gate_proj.weight" not in per
+
+
+def test_ffn_worker_dense_slices_add_up():
+    """Two FFN workers holding the two halves of a dense MLP layer: their
+    outputs (residual on the first only) add up to the whole layer's."""
+    cfg = tiny_qwen3_moe()
+    cfg.mlp_only_layers = [1]
+    import tempfile
+
+    d = tempfile.mkdtemp(prefix="afd_dense_")
+    save_checkpoint(d, cfg, random_attention_weights(cfg, 0, "cpu", torch.float32),
+                    random_ffn_weights(cfg, None, 0, "cpu", torch.float32))
+    whole = FFNWorker.from_pretrained(d, "cpu", torch.float32)
+    halves = [FFNWorker.from_pretrained(d, "cpu", torch.float32, dense_part=(i, 2))
+              for i in range(2)]
+    assert halves[0].w.layers[1].w_dense_down.shape[1] == cfg.intermediate_size // 2
+    h = torch.randn(4, cfg.hidden_size, generator=torch.Generator().manual_seed(4))
+    want = whole.forward_ffn_layer(1, h.clone())
+    got = (halves[0].forward_ffn_layer(1, h.clone(), add_residual=True)
+           + halves[1].forward_ffn_layer(1, h.clone(), add_residual=False))
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5)
